@@ -1,0 +1,447 @@
+#!/usr/bin/env python
+"""Benchmark: the packed linears of one decode step of a Llama-3-8B-shaped Q4_K-M model.
+
+A step is every quantized linear of one token (M = 1): 32 layers x (q, k, v, o,
+gate, up in Q4_K; down in Q6_K) plus the Q6_K output head, 4.84 GB of packed
+weights -- far larger than the 126 MB L2, so no flush is needed between steps.
+At N GPUs the linears are tensor-parallel (column-parallel q/k/v/gate/up/head,
+row-parallel o/down, two all-reduces per layer and an all-gather of the logits).
+
+Prints one JSON line (rank 0): whole-job HBM GB/s over the step, tok/s, the
+roofline of the dominant kernel (the Q4_K GEMV), the CPU baseline, the
+end-to-end number through the host-buffer C ABI, and clocks.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl clq|reference]
+"""
+import argparse
+import datetime
+import importlib
+import json
+import os
+import pathlib
+import statistics
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "oracle"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "quant GEMV HBM GB/s (%peak) + 8B-shape Q4_K decode tok/s @1/2/4/8 GPU"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=300)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["clq", "reference"], default="clq")
+    ap.add_argument("--model", choices=["8b", "70b"], default="8b")
+    ap.add_argument("--m", type=int, default=1, help="activation rows (tokens) per step")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler(threading.Thread):
+    """SM clock and throttle reasons through NVML every 10 ms (reads only)."""
+
+    REASONS = {0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x4: "sw_power_cap"}
+
+    def __init__(self, index):
+        super().__init__(daemon=True)
+        self.samples, self.reasons, self.stop_flag = [], set(), threading.Event()
+        self.max_mhz = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self.nv = None
+
+    def run(self):
+        while self.nv and not self.stop_flag.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                mask = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:
+                break
+            time.sleep(0.01)
+
+    def result(self):
+        self.stop_flag.set()
+        self.join(timeout=1)
+        med = statistics.median(self.samples) if self.samples else None
+        return {"sm_mhz": med, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+def dist_setup(torch):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=120))
+    return rank, world, local
+
+
+def device_weight(torch, dtype, n, k, seed):
+    """Packed bytes with the configuration's distributions, generated on the device."""
+    clq = importlib.import_module("cl-inference_b200")
+    dt = clq.find_dtype(dtype)
+    nblocks = n * (k // dt.block_size)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    raw = torch.randint(0, 256, (nblocks, dt.block_bytes), dtype=torch.uint8, device="cuda", generator=g)
+
+    def halves(scale):
+        v = (torch.randn(nblocks, device="cuda", generator=g).abs() * scale).half()
+        return v.view(torch.uint8).view(nblocks, 2)
+
+    if dt.name == "q4_k":
+        raw[:, 0:2] = halves(0.01)
+        raw[:, 2:4] = halves(0.01)
+    elif dt.name == "q6_k":
+        raw[:, 192:208] = torch.randint(-64, 64, (nblocks, 16), device="cuda", generator=g).to(torch.int8).view(torch.uint8)
+        raw[:, 208:210] = halves(0.005)
+    elif dt.name == "q4_0":
+        raw[:, 0:2] = halves(0.02 / 8)
+    elif dt.name == "q8_0":
+        raw[:, 0:2] = halves(0.02 / 127)
+        raw[:, 2:34] = torch.randint(-127, 128, (nblocks, 32), device="cuda", generator=g).to(torch.int8).view(torch.uint8)
+    return raw.reshape(-1)
+
+
+def run_clq(args):
+    import torch
+    clq = importlib.import_module("cl-inference_b200")
+    tp = importlib.import_module("cl-inference_b200.tp")
+    rank, world, local = dist_setup(torch)
+    dist = torch.distributed if world > 1 else None
+    cfg = tp.LLAMA3_8B if args.model == "8b" else tp.LLAMA3_70B
+    m = args.m
+    linears = tp.model_linears(cfg)
+    q_dim = cfg["heads"] * cfg["head_dim"]
+
+    # ---- this rank's shards --------------------------------------------------
+    stores, host_copies = [], []
+    keep_host = world == 1 and not args.no_e2e
+    for i, (name, dtype, n, k, kind, src) in enumerate(linears):
+        s = tp.plan(dtype, n, k, kind, rank, world)
+        data = device_weight(torch, dtype, s.n, s.k, seed=4000 + 97 * i + rank)
+        stores.append((clq.Store(dtype, s.n, s.k, data), s, dtype, kind, src, name))
+        if keep_host:
+            host_copies.append(data.cpu().numpy())
+        del data
+    torch.cuda.synchronize()
+
+    gen = torch.Generator(device="cuda")
+    gen.manual_seed(7)
+    attn_cols = tp.split(q_dim, world, rank, 256)
+    ffn_cols = tp.split(cfg["ffn"], world, rank, 256)
+    inputs = {
+        "hidden": torch.randn(m, cfg["hidden"], device="cuda", generator=gen),
+        "attn": torch.randn(m, attn_cols[1] - attn_cols[0], device="cuda", generator=gen),
+        "ffn": torch.randn(m, ffn_cols[1] - ffn_cols[0], device="cuda", generator=gen),
+    }
+    outs = [torch.empty(m, st.n, device="cuda") for (_, st, *_r) in stores]
+    logits = torch.empty(world, m, stores[-1][1].n, device="cuda")
+    launches_per_step = len(stores)
+
+    def step():
+        for (store, s, dtype, kind, src, name), out in zip(stores, outs):
+            store.linear(inputs[src], out=out)
+            if dist is not None and kind == "cols":
+                dist.all_reduce(out)
+        if dist is not None:
+            dist.all_gather_into_tensor(logits, outs[-1])
+
+    # algorithmic bytes (W + x + out) of this rank's step, summed over ranks
+    def lin_bytes(st, dtype):
+        return tp.weight_bytes(dtype, st.n, st.k) + 4 * m * st.k + 4 * m * st.n
+    step_bytes = float(sum(lin_bytes(st, dt) for (_, st, dt, *_r) in stores))
+    if dist is not None:
+        t = torch.tensor([step_bytes], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        job_bytes = float(t.item())
+    else:
+        job_bytes = step_bytes
+
+    # ---- warm up eagerly (NCCL communicators), then capture a graph ----------
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(max(args.warmup, 3)):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    # ---- timed region ---------------------------------------------------------
+    clocks = ClockSampler(local)
+    clocks.start()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        graph.replay()
+    end.record()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    clock = clocks.result()
+    ms = start.elapsed_time(end) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    gbs = job_bytes / (ms * 1e-3) / 1e9
+    peak, peak_kind = peaks()
+
+    # ---- dominant kernel: the Q4_K GEMV launches alone, back to back ----------
+    q4k = [(store, s, src, out) for (store, s, dtype, kind, src, name), out in zip(stores, outs)
+           if dtype == "q4_k"]
+    kgraph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(kgraph):
+        for store, s, src, out in q4k:
+            store.linear(inputs[src], out=out)
+    reps = max(5, min(50, args.steps // 5))
+    for _ in range(3):
+        kgraph.replay()
+    torch.cuda.synchronize()
+    ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ks.record()
+    for _ in range(reps):
+        kgraph.replay()
+    ke.record()
+    torch.cuda.synchronize()
+    k_ms = ks.elapsed_time(ke) / (reps * len(q4k))
+    k_bytes = sum(lin_bytes(s, "q4_k") for _, s, _, _ in q4k) / len(q4k)
+    k_gbs = k_bytes / (k_ms * 1e-3) / 1e9
+    traffic = None
+    tfile = ROOT / "profiles" / "q4k_gemv_traffic.json"
+    if tfile.exists():
+        traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch_8b_step_avg")
+
+    # ---- end to end -------------------------------------------------------------
+    e2e = None
+    if not args.no_e2e:
+        e2e = e2e_dropin(args, clq, stores, host_copies, m, job_bytes) if world == 1 else \
+            e2e_tp(args, torch, dist, graph, inputs, logits, job_bytes)
+
+    del graph, kgraph
+    result = None
+    if rank == 0:
+        result = {
+            "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {
+                "workload": f"llama3-{args.model}-shape Q4_K-M decode linears, M={m}: "
+                            f"{cfg['layers']} layers x (q,k,v,o,gate,up Q4_K; down Q6_K) + Q6_K output",
+                "m": m, "parallelism": f"tp{world}", "weights_gb": round(job_bytes / 1e9, 3),
+                "l2": "weights per step far above the 126 MB L2; no flush",
+            },
+            "tok_per_s": round(1000.0 / ms, 2),
+            "hbm_frac": round(gbs / world / peak, 4),
+            "roofline": {"bound": "hbm", "kernel": "Q4_K GEMV (clq linear, M=%d)" % m,
+                         "achieved": round(k_gbs, 1), "peak": peak, "peak_kind": peak_kind,
+                         "unit": "GB/s", "frac": round(k_gbs / peak, 4), "traffic": traffic,
+                         "algorithmic_bytes_per_launch": round(k_bytes),
+                         "us_per_launch": round(k_ms * 1e3, 3)},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clock,
+        }
+        if e2e:
+            result["e2e"] = e2e
+        if world == 1 and not args.no_cpu:
+            result["cpu_baseline"] = cpu_baseline(args, tp, cfg, m)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+def e2e_dropin(args, clq, stores, host_copies, m, job_bytes):
+    """The host-buffer C ABI (clq_q4_k_matmul & co.), one synchronous call per linear."""
+    import numpy as np
+    lib = clq._lib.lib
+    fns = {"q4_k": lib.clq_q4_k_matmul, "q6_k": lib.clq_q6_k_matmul,
+           "q8_0": lib.clq_q8_0_matmul, "q4_0": lib.clq_q4_0_matmul}
+    rng = np.random.default_rng(3)
+    xs = {}
+    outs = []
+    calls = []
+    h2d = d2h = 0
+    for (store, s, dtype, kind, src, name), data in zip(stores, host_copies):
+        key = (src, s.k)
+        if key not in xs:
+            xs[key] = rng.standard_normal((m, s.k), dtype=np.float32)
+        out = np.empty((m, s.n), np.float32)
+        outs.append(out)
+        calls.append((fns[dtype], out, xs[key], data, s.n, s.k))
+        h2d += 4 * m * s.k
+        d2h += 4 * m * s.n
+
+    def one():
+        for fn, out, x, data, n, k in calls:
+            rc = fn(out.ctypes.data, x.ctypes.data, data.ctypes.data, m, n, k)
+            if rc:
+                raise clq.ClqError(rc, clq._lib.last_error())
+
+    for _ in range(3):
+        one()  # first call uploads each weight once (cached by host range)
+    steps = max(5, min(args.steps, 50))
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one()
+    sec = (time.perf_counter() - t0) / steps
+    lib.clq_clear_cache()
+    return {"value": round(job_bytes / sec / 1e9, 1), "unit": "GB/s", "ms_per_step": round(sec * 1e3, 4),
+            "tok_per_s": round(1.0 / sec, 2), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "clq_q4_k_matmul/clq_q6_k_matmul, host buffers, one synchronous call per linear",
+            "steps": steps}
+
+
+def e2e_tp(args, torch, dist, graph, inputs, logits, job_bytes):
+    """Per step: pinned host input -> device, the captured tensor-parallel step, logits -> host."""
+    host_in = torch.randn(inputs["hidden"].shape, pin_memory=True)
+    host_out = torch.empty(logits.shape, pin_memory=True)
+    steps = max(5, min(args.steps, 100))
+    for _ in range(3):
+        inputs["hidden"].copy_(host_in, non_blocking=True)
+        graph.replay()
+        host_out.copy_(logits, non_blocking=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        inputs["hidden"].copy_(host_in, non_blocking=True)
+        graph.replay()
+        host_out.copy_(logits, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+    sec = (time.perf_counter() - t0) / steps
+    t = torch.tensor([sec], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    sec = float(t.item())
+    return {"value": round(job_bytes / sec / 1e9, 1), "unit": "GB/s", "ms_per_step": round(sec * 1e3, 4),
+            "tok_per_s": round(1.0 / sec, 2), "h2d_bytes_per_step": host_in.numel() * 4,
+            "d2h_bytes_per_step": host_out.numel() * 4,
+            "api": "tensor-parallel step (clq_linear_device + NCCL) with pinned host input/logits",
+            "steps": steps}
+
+
+def cpu_sample(tp, cfg, m):
+    """One decoder layer's seven linears at full size, host bytes (numpy seeded)."""
+    import numpy as np
+    synth = importlib.import_module("cl-inference_b200.synth")
+    sample = []
+    for i, (name, dtype, n, k, kind, src) in enumerate(tp.layer_linears(cfg)):
+        data = synth.packed_blocks(dtype, n, k, seed=8000 + i)
+        x = synth.activations(m, k, seed=8100 + i)
+        sample.append((dtype, n, k, data, x))
+    nbytes = sum(tp.weight_bytes(d, n, k) + 4 * m * k + 4 * m * n for d, n, k, _, _ in sample)
+    return sample, nbytes
+
+
+def time_cpu(sample, nbytes, seconds, threads):
+    import oracle
+    runs, t0 = 0, time.perf_counter()
+    while True:
+        for dtype, n, k, data, x in sample:
+            oracle.matmul_f32(dtype, x, data, n, threads)
+        runs += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            return runs * nbytes / el / 1e9, runs, el
+
+
+def cpu_baseline(args, tp, cfg, m):
+    import oracle
+    sample, nbytes = cpu_sample(tp, cfg, m)
+    threads = oracle.max_threads()
+    gbs, runs, el = time_cpu(sample, nbytes, args.cpu_seconds, threads)
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"one layer's 7 linears ({nbytes/1e6:.1f} MB) x {runs} in {el:.1f} s, "
+                      f"fp32 CPU port of the packed kernel contract, OpenMP"}
+
+
+def run_reference(args):
+    """The reference arm: the CPU port of cl-inference's packed kernels on the host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    tp = importlib.import_module("cl-inference_b200.tp")
+    import oracle
+    cfg = tp.LLAMA3_8B if args.model == "8b" else tp.LLAMA3_70B
+    sample, nbytes = cpu_sample(tp, cfg, args.m)
+    threads = oracle.max_threads()
+    for _ in range(args.warmup):
+        for dtype, n, k, data, x in sample[:1]:
+            oracle.matmul_f32(dtype, x, data, n, threads)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        for dtype, n, k, data, x in sample:
+            oracle.matmul_f32(dtype, x, data, n, threads)
+        times.append(time.perf_counter() - t0)
+        if sum(times) > 120:
+            break
+    sec = sum(times) / len(times)
+    gbs = nbytes / sec / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"llama3-{args.model}-shape Q4_K-M decode linears, M={args.m}; "
+                               "each step one layer's 7 linears (bounded sample)", "m": args.m},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": f"one layer's 7 linears ({nbytes/1e6:.1f} MB) per step"},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "cl-inference's CPU kernels (trivial-simd, Common Lisp host) cannot be built here; "
+                "this is the C port of their contract (oracle/clq_oracle.c)",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_clq(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,516 @@
+// api.cu -- the C ABI of libclq (include/clq.h): status codes, the device
+// store, the host-range weight cache behind the drop-in kernels, and the
+// per-thread stream and staging buffers for host-pointer calls.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/clq.h"
+#include "clq_internal.h"
+
+struct clq_store {
+    int dtype = 0;
+    int64_t n = 0, k = 0;
+    size_t nbytes = 0;
+    int device = -1;
+    uint8_t* dev = nullptr;
+    int elems = 0, block_bytes = 0;
+    int64_t row_bytes = 0;
+};
+
+namespace {
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+    if (e == cudaErrorMemoryAllocation)
+        return fail(CLQ_ERR_OUT_OF_MEMORY, "%s: %s", what, cudaGetErrorString(e));
+    return fail(CLQ_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+const char* dtype_name(int dtype) {
+    switch (dtype) {
+    case CLQ_Q4_0: return "Q4_0";
+    case CLQ_Q8_0: return "Q8_0";
+    case CLQ_Q4_K: return "Q4_K";
+    case CLQ_Q6_K: return "Q6_K";
+    default: return "?";
+    }
+}
+
+// The current device, checked once per device to be an sm_100 part.
+int current_device(int* dev) {
+    static std::mutex mu;
+    static std::vector<int> checked;  // 0 unknown, 1 ok, 2 bad
+    cudaError_t e = cudaGetDevice(dev);
+    if (e != cudaSuccess) return fail(CLQ_ERR_NO_DEVICE, "no CUDA device: %s", cudaGetErrorString(e));
+    std::lock_guard<std::mutex> lock(mu);
+    if ((int)checked.size() <= *dev) checked.resize(*dev + 1, 0);
+    if (checked[*dev] == 0) {
+        cudaDeviceProp prop;
+        e = cudaGetDeviceProperties(&prop, *dev);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetDeviceProperties");
+        checked[*dev] = prop.major == 10 ? 1 : 2;
+    }
+    if (checked[*dev] != 1)
+        return fail(CLQ_ERR_NO_DEVICE, "device %d is not an sm_100 (B200-class) GPU", *dev);
+    return CLQ_OK;
+}
+
+int check_shape(int dtype, int64_t n, int64_t k, int* elems, int* bb) {
+    if (!clq::geometry(dtype, elems, bb)) return fail(CLQ_ERR_ARGUMENT, "unknown packed dtype %d", dtype);
+    if (n < 0 || k < 0) return fail(CLQ_ERR_SHAPE, "negative shape (%lld %lld)", (long long)n, (long long)k);
+    if (k % *elems)
+        return fail(CLQ_ERR_SHAPE, "%s row length %lld is not a multiple of %d", dtype_name(dtype),
+                    (long long)k, *elems);
+    return CLQ_OK;
+}
+
+clq::WeightView view_of(const clq_store* s, int64_t row_begin) {
+    clq::WeightView v;
+    v.bytes = s->dev + row_begin * s->row_bytes;
+    v.dtype = s->dtype;
+    v.rows = s->n - row_begin;
+    v.k = s->k;
+    v.row_bytes = s->row_bytes;
+    v.elems = s->elems;
+    v.block_bytes = s->block_bytes;
+    return v;
+}
+
+void destroy_store(clq_store* s) {
+    if (!s) return;
+    if (s->dev) {
+        int prev = -1;
+        cudaGetDevice(&prev);
+        if (prev != s->device) cudaSetDevice(s->device);
+        cudaFree(s->dev);
+        if (prev >= 0 && prev != s->device) cudaSetDevice(prev);
+    }
+    delete s;
+}
+
+// Allocate, copy (from host or device), validate scales.  Synchronous.
+int make_store(int dtype, int64_t n, int64_t k, const void* src, bool src_on_device, size_t nbytes,
+               cudaStream_t stream, clq_store** out) {
+    int elems, bb, rc;
+    if ((rc = check_shape(dtype, n, k, &elems, &bb))) return rc;
+    if (nbytes % (size_t)bb)
+        return fail(CLQ_ERR_BLOCKS, "%s data of %zu bytes is not a whole number of %d-byte blocks",
+                    dtype_name(dtype), nbytes, bb);
+    const int64_t row_bytes = k / elems * bb;
+    if ((size_t)(n * row_bytes) != nbytes)
+        return fail(CLQ_ERR_SHAPE, "%s weight (%lld %lld) needs %lld bytes, got %zu", dtype_name(dtype),
+                    (long long)n, (long long)k, (long long)(n * row_bytes), nbytes);
+    if (nbytes && !src) return fail(CLQ_ERR_ARGUMENT, "null weight bytes");
+    int device;
+    if ((rc = current_device(&device))) return rc;
+    std::unique_ptr<clq_store, void (*)(clq_store*)> s(new clq_store, destroy_store);
+    s->dtype = dtype; s->n = n; s->k = k; s->nbytes = nbytes; s->device = device;
+    s->elems = elems; s->block_bytes = bb; s->row_bytes = row_bytes;
+    // Round up and keep 256 zero bytes of tail so vector loads past the last
+    // block stay inside the allocation.
+    size_t alloc = ((nbytes + 255) & ~(size_t)255) + 256;
+    cudaError_t e = cudaMalloc((void**)&s->dev, alloc);
+    if (e != cudaSuccess) { s->dev = nullptr; return cuda_fail(e, "cudaMalloc(weight store)"); }
+    unsigned long long* flag = nullptr;
+    e = cudaMalloc((void**)&flag, sizeof *flag);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(flag)");
+    unsigned long long first_bad = ~0ull;
+    do {
+        if ((e = cudaMemsetAsync(s->dev + nbytes, 0, alloc - nbytes, stream)) != cudaSuccess) break;
+        if (nbytes &&
+            (e = cudaMemcpyAsync(s->dev, src, nbytes,
+                                 src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                 stream)) != cudaSuccess)
+            break;
+        if ((e = cudaMemcpyAsync(flag, &first_bad, sizeof first_bad, cudaMemcpyHostToDevice, stream)) !=
+            cudaSuccess)
+            break;
+        if ((e = clq::launch_validate_scales(s->dev, dtype, (int64_t)(nbytes / bb), flag, stream)) !=
+            cudaSuccess)
+            break;
+        if ((e = cudaMemcpyAsync(&first_bad, flag, sizeof first_bad, cudaMemcpyDeviceToHost, stream)) !=
+            cudaSuccess)
+            break;
+        e = cudaStreamSynchronize(stream);
+    } while (0);
+    cudaFree(flag);
+    if (e != cudaSuccess) return cuda_fail(e, "weight upload");
+    if (first_bad != ~0ull)
+        return fail(CLQ_ERR_NONFINITE_SCALE, "Non-finite %s scale at byte %llu", dtype_name(dtype),
+                    first_bad * (unsigned long long)bb);
+    *out = s.release();
+    return CLQ_OK;
+}
+
+// ---- per-thread stream and staging for host-pointer calls -----------------
+
+struct DeviceBuffer {
+    void* ptr = nullptr;
+    size_t cap = 0;
+    cudaError_t ensure(size_t bytes) {
+        if (bytes <= cap) return cudaSuccess;
+        if (ptr) cudaFree(ptr);
+        ptr = nullptr; cap = 0;
+        size_t want = bytes < 4096 ? 4096 : bytes + bytes / 4;
+        cudaError_t e = cudaMalloc(&ptr, want);
+        if (e == cudaSuccess) cap = want;
+        return e;
+    }
+};
+
+struct ThreadContext {
+    int device = -1;
+    cudaStream_t stream = nullptr;
+    DeviceBuffer x, out, ids;
+};
+
+struct ThreadContexts {
+    std::vector<ThreadContext*> per_device;
+    ~ThreadContexts() {
+        for (ThreadContext* c : per_device) {
+            if (!c) continue;
+            cudaSetDevice(c->device);
+            if (c->stream) cudaStreamDestroy(c->stream);
+            if (c->x.ptr) cudaFree(c->x.ptr);
+            if (c->out.ptr) cudaFree(c->out.ptr);
+            if (c->ids.ptr) cudaFree(c->ids.ptr);
+            delete c;
+        }
+    }
+};
+thread_local ThreadContexts t_contexts;
+
+int thread_context(int device, ThreadContext** out) {
+    auto& v = t_contexts.per_device;
+    if ((int)v.size() <= device) v.resize(device + 1, nullptr);
+    if (!v[device]) {
+        auto* c = new ThreadContext;
+        c->device = device;
+        cudaError_t e = cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) { delete c; return cuda_fail(e, "cudaStreamCreate"); }
+        v[device] = c;
+    }
+    *out = v[device];
+    return CLQ_OK;
+}
+
+// ---- host-range weight cache ----------------------------------------------
+
+struct CacheEntry {
+    const uint8_t* host;
+    size_t nbytes;
+    std::shared_ptr<clq_store> store;
+};
+std::mutex g_cache_mu;
+std::vector<CacheEntry> g_cache;
+
+// Find or create the store holding N rows of the weight at host address BYTES.
+int cached_store(int dtype, int64_t n, int64_t k, const uint8_t* bytes, int device, bool use_cache,
+                 cudaStream_t stream, std::shared_ptr<clq_store>* out, int64_t* row_begin) {
+    int elems, bb, rc;
+    if ((rc = check_shape(dtype, n, k, &elems, &bb))) return rc;
+    const int64_t row_bytes = k / elems * bb;
+    const size_t need = (size_t)(n * row_bytes);
+    if (use_cache) {
+        std::lock_guard<std::mutex> lock(g_cache_mu);
+        for (const CacheEntry& e : g_cache) {
+            const clq_store* s = e.store.get();
+            if (s->device != device || s->dtype != dtype || s->k != k) continue;
+            if (bytes < e.host || bytes + need > e.host + e.nbytes) continue;
+            size_t off = (size_t)(bytes - e.host);
+            if (row_bytes == 0 || off % (size_t)row_bytes) continue;
+            *out = e.store;
+            *row_begin = (int64_t)(off / (size_t)row_bytes);
+            return CLQ_OK;
+        }
+    }
+    clq_store* raw = nullptr;
+    if ((rc = make_store(dtype, n, k, bytes, false, need, stream, &raw))) return rc;
+    std::shared_ptr<clq_store> s(raw, destroy_store);
+    if (use_cache) {
+        std::lock_guard<std::mutex> lock(g_cache_mu);
+        g_cache.push_back({bytes, need, s});
+    }
+    *out = s;
+    *row_begin = 0;
+    return CLQ_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+
+extern "C" {
+
+int clq_abi_version(void) { return CLQ_ABI_VERSION; }
+
+int clq_last_error(char* buf, size_t len) {
+    if (!buf || !len) return CLQ_ERR_ARGUMENT;
+    std::snprintf(buf, len, "%s", t_last_error.c_str());
+    return CLQ_OK;
+}
+
+int clq_block_geometry(int dtype, int64_t* elements, int64_t* block_bytes) {
+    int e, b;
+    if (!clq::geometry(dtype, &e, &b)) return fail(CLQ_ERR_ARGUMENT, "unknown packed dtype %d", dtype);
+    if (elements) *elements = e;
+    if (block_bytes) *block_bytes = b;
+    return CLQ_OK;
+}
+
+int clq_store_create(int dtype, int64_t n, int64_t k, const uint8_t* host_bytes, size_t nbytes,
+                     unsigned flags, clq_store** out) {
+    if (!out) return fail(CLQ_ERR_ARGUMENT, "null store result pointer");
+    if (flags != CLQ_STORE_DEFAULT) return fail(CLQ_ERR_ARGUMENT, "unknown store flags 0x%x", flags);
+    *out = nullptr;
+    int device, rc;
+    if ((rc = current_device(&device))) return rc;
+    ThreadContext* ctx;
+    if ((rc = thread_context(device, &ctx))) return rc;
+    return make_store(dtype, n, k, host_bytes, false, nbytes, ctx->stream, out);
+}
+
+int clq_store_create_device(int dtype, int64_t n, int64_t k, const void* device_bytes, size_t nbytes,
+                            unsigned flags, void* stream, clq_store** out) {
+    if (!out) return fail(CLQ_ERR_ARGUMENT, "null store result pointer");
+    if (flags != CLQ_STORE_DEFAULT) return fail(CLQ_ERR_ARGUMENT, "unknown store flags 0x%x", flags);
+    *out = nullptr;
+    return make_store(dtype, n, k, device_bytes, true, nbytes, (cudaStream_t)stream, out);
+}
+
+int clq_store_free(clq_store* store) {
+    destroy_store(store);
+    return CLQ_OK;
+}
+
+int clq_store_info(const clq_store* s, int* dtype, int64_t* n, int64_t* k, size_t* nbytes,
+                   const void** device_bytes, int* device) {
+    if (!s) return fail(CLQ_ERR_ARGUMENT, "null store");
+    if (dtype) *dtype = s->dtype;
+    if (n) *n = s->n;
+    if (k) *k = s->k;
+    if (nbytes) *nbytes = s->nbytes;
+    if (device_bytes) *device_bytes = s->dev;
+    if (device) *device = s->device;
+    return CLQ_OK;
+}
+
+int clq_linear_device(const clq_store* w, int64_t row_begin, int64_t rows, const void* x, int xtype,
+                      int64_t m, float* out, int64_t ldo, unsigned flags, void* stream) {
+    if (!w) return fail(CLQ_ERR_ARGUMENT, "null store");
+    if (xtype != CLQ_X_F32 && xtype != CLQ_X_BF16 && xtype != CLQ_X_F16)
+        return fail(CLQ_ERR_ARGUMENT, "unknown activation type %d", xtype);
+    if (flags & ~(CLQ_MATH_FAST)) return fail(CLQ_ERR_ARGUMENT, "unknown product flags 0x%x", flags);
+    if (row_begin < 0 || rows < 0 || row_begin + rows > w->n || m < 0)
+        return fail(CLQ_ERR_SHAPE, "rows [%lld, %lld) / m %lld outside a (%lld %lld) weight",
+                    (long long)row_begin, (long long)(row_begin + rows), (long long)m,
+                    (long long)w->n, (long long)w->k);
+    if (ldo < rows) return fail(CLQ_ERR_SHAPE, "output stride %lld < rows %lld", (long long)ldo, (long long)rows);
+    if (m == 0 || rows == 0) return CLQ_OK;
+    if (!x || !out) return fail(CLQ_ERR_ARGUMENT, "null activation or output pointer");
+    int device, rc;
+    if ((rc = current_device(&device))) return rc;
+    if (device != w->device)
+        return fail(CLQ_ERR_ARGUMENT, "store lives on device %d, current device is %d", w->device, device);
+    if (w->k == 0) {
+        for (int64_t i = 0; i < m; i++) {
+            cudaError_t e = cudaMemsetAsync(out + i * ldo, 0, rows * sizeof(float), (cudaStream_t)stream);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync");
+        }
+        return CLQ_OK;
+    }
+    cudaError_t e = clq::launch_linear(view_of(w, row_begin), rows, x, xtype, m, out, ldo, flags,
+                                       (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "linear kernel launch");
+    return CLQ_OK;
+}
+
+int clq_dequantize_device(const clq_store* w, int64_t row_begin, int64_t rows, float* out,
+                          int transposed, void* stream) {
+    if (!w) return fail(CLQ_ERR_ARGUMENT, "null store");
+    if (row_begin < 0 || rows < 0 || row_begin + rows > w->n)
+        return fail(CLQ_ERR_SHAPE, "rows [%lld, %lld) outside %lld rows", (long long)row_begin,
+                    (long long)(row_begin + rows), (long long)w->n);
+    if (rows == 0 || w->k == 0) return CLQ_OK;
+    if (!out) return fail(CLQ_ERR_ARGUMENT, "null output");
+    clq::WeightView v = view_of(w, row_begin);
+    cudaError_t e = clq::launch_dequantize(v, rows, out, transposed != 0, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "dequantize kernel launch");
+    return CLQ_OK;
+}
+
+int clq_gather_device(const clq_store* w, const int32_t* ids, int64_t count, float* out, void* stream) {
+    if (!w) return fail(CLQ_ERR_ARGUMENT, "null store");
+    if (count < 0) return fail(CLQ_ERR_SHAPE, "negative id count");
+    if (count == 0 || w->k == 0) return CLQ_OK;
+    if (!ids || !out) return fail(CLQ_ERR_ARGUMENT, "null ids or output");
+    cudaError_t e = clq::launch_gather(view_of(w, 0), ids, count, out, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "gather kernel launch");
+    return CLQ_OK;
+}
+
+int clq_matmul(int dtype, float* out, const float* x, const uint8_t* bytes, int64_t m, int64_t n,
+               int64_t k, unsigned flags) {
+    int elems, bb, rc;
+    if ((rc = check_shape(dtype, n, k, &elems, &bb))) return rc;
+    if (m < 0) return fail(CLQ_ERR_SHAPE, "negative activation rows %lld", (long long)m);
+    if (flags & ~(CLQ_MATH_FAST | CLQ_NO_CACHE)) return fail(CLQ_ERR_ARGUMENT, "unknown flags 0x%x", flags);
+    if (m == 0 || n == 0) return CLQ_OK;
+    if (!out || (k && (!x || !bytes))) return fail(CLQ_ERR_ARGUMENT, "null out, x or weight bytes");
+    if (k == 0) {
+        std::memset(out, 0, (size_t)(m * n) * sizeof(float));
+        return CLQ_OK;
+    }
+    int device;
+    if ((rc = current_device(&device))) return rc;
+    ThreadContext* ctx;
+    if ((rc = thread_context(device, &ctx))) return rc;
+    std::shared_ptr<clq_store> store;
+    int64_t row_begin = 0;
+    if ((rc = cached_store(dtype, n, k, bytes, device, !(flags & CLQ_NO_CACHE), ctx->stream, &store,
+                           &row_begin)))
+        return rc;
+    const size_t xbytes = (size_t)(m * k) * sizeof(float), obytes = (size_t)(m * n) * sizeof(float);
+    cudaError_t e;
+    if ((e = ctx->x.ensure(xbytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(x)");
+    if ((e = ctx->out.ensure(obytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(out)");
+    if ((e = cudaMemcpyAsync(ctx->x.ptr, x, xbytes, cudaMemcpyHostToDevice, ctx->stream)) != cudaSuccess)
+        return cuda_fail(e, "copy x to device");
+    if ((e = clq::launch_linear(view_of(store.get(), row_begin), n, ctx->x.ptr, CLQ_X_F32, m,
+                                (float*)ctx->out.ptr, n, flags & CLQ_MATH_FAST, ctx->stream)) != cudaSuccess)
+        return cuda_fail(e, "linear kernel launch");
+    if ((e = cudaMemcpyAsync(out, ctx->out.ptr, obytes, cudaMemcpyDeviceToHost, ctx->stream)) != cudaSuccess)
+        return cuda_fail(e, "copy out to host");
+    if ((e = cudaStreamSynchronize(ctx->stream)) != cudaSuccess) return cuda_fail(e, "linear");
+    return CLQ_OK;
+}
+
+int clq_q8_0_matmul(float* out, const float* x, const uint8_t* bytes, int64_t m, int64_t n, int64_t k) {
+    return clq_matmul(CLQ_Q8_0, out, x, bytes, m, n, k, 0);
+}
+int clq_q4_0_matmul(float* out, const float* x, const uint8_t* bytes, int64_t m, int64_t n, int64_t k) {
+    return clq_matmul(CLQ_Q4_0, out, x, bytes, m, n, k, 0);
+}
+int clq_q4_k_matmul(float* out, const float* x, const uint8_t* bytes, int64_t m, int64_t n, int64_t k) {
+    return clq_matmul(CLQ_Q4_K, out, x, bytes, m, n, k, 0);
+}
+int clq_q6_k_matmul(float* out, const float* x, const uint8_t* bytes, int64_t m, int64_t n, int64_t k) {
+    return clq_matmul(CLQ_Q6_K, out, x, bytes, m, n, k, 0);
+}
+
+int clq_forget(const uint8_t* bytes, size_t nbytes) {
+    std::vector<std::shared_ptr<clq_store>> dropped;  // freed outside the lock
+    {
+        std::lock_guard<std::mutex> lock(g_cache_mu);
+        for (size_t i = 0; i < g_cache.size();) {
+            const CacheEntry& e = g_cache[i];
+            bool overlap = e.host < bytes + nbytes && bytes < e.host + e.nbytes;
+            if (overlap) {
+                dropped.push_back(e.store);
+                g_cache.erase(g_cache.begin() + i);
+            } else {
+                i++;
+            }
+        }
+    }
+    return CLQ_OK;
+}
+
+int clq_clear_cache(void) {
+    std::vector<CacheEntry> dropped;
+    {
+        std::lock_guard<std::mutex> lock(g_cache_mu);
+        dropped.swap(g_cache);
+    }
+    return CLQ_OK;
+}
+
+int clq_cache_stats(int64_t* count, int64_t* device_bytes) {
+    std::lock_guard<std::mutex> lock(g_cache_mu);
+    int64_t bytes = 0;
+    for (const CacheEntry& e : g_cache) bytes += (int64_t)e.store->nbytes;
+    if (count) *count = (int64_t)g_cache.size();
+    if (device_bytes) *device_bytes = bytes;
+    return CLQ_OK;
+}
+
+int clq_dequantize(int dtype, const uint8_t* bytes, size_t nbytes, float* out) {
+    int elems, bb, rc;
+    if (!clq::geometry(dtype, &elems, &bb)) return fail(CLQ_ERR_ARGUMENT, "unknown packed dtype %d", dtype);
+    if (nbytes % (size_t)bb)
+        return fail(CLQ_ERR_BLOCKS, "%s data of %zu bytes is not a whole number of %d-byte blocks",
+                    dtype_name(dtype), nbytes, bb);
+    const int64_t nblocks = (int64_t)(nbytes / bb);
+    if (nblocks == 0) return CLQ_OK;
+    if (!bytes || !out) return fail(CLQ_ERR_ARGUMENT, "null bytes or output");
+    int device;
+    if ((rc = current_device(&device))) return rc;
+    ThreadContext* ctx;
+    if ((rc = thread_context(device, &ctx))) return rc;
+    clq_store* raw = nullptr;
+    // One row of nblocks blocks.
+    if ((rc = make_store(dtype, 1, nblocks * elems, bytes, false, nbytes, ctx->stream, &raw))) return rc;
+    std::unique_ptr<clq_store, void (*)(clq_store*)> s(raw, destroy_store);
+    const size_t obytes = (size_t)(nblocks * elems) * sizeof(float);
+    cudaError_t e;
+    if ((e = ctx->out.ensure(obytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(out)");
+    if ((e = clq::launch_dequantize(view_of(s.get(), 0), 1, (float*)ctx->out.ptr, false, ctx->stream)) !=
+        cudaSuccess)
+        return cuda_fail(e, "dequantize kernel launch");
+    if ((e = cudaMemcpyAsync(out, ctx->out.ptr, obytes, cudaMemcpyDeviceToHost, ctx->stream)) != cudaSuccess)
+        return cuda_fail(e, "copy out to host");
+    if ((e = cudaStreamSynchronize(ctx->stream)) != cudaSuccess) return cuda_fail(e, "dequantize");
+    return CLQ_OK;
+}
+
+int clq_take(int dtype, const uint8_t* bytes, int64_t n, int64_t k, const int32_t* ids, int64_t count,
+             float* out) {
+    int elems, bb, rc;
+    if ((rc = check_shape(dtype, n, k, &elems, &bb))) return rc;
+    if (count < 0) return fail(CLQ_ERR_SHAPE, "negative id count");
+    for (int64_t i = 0; i < count; i++)
+        if (ids[i] < 0 || ids[i] >= n)
+            return fail(CLQ_ERR_ARGUMENT, "row id %d outside [0, %lld)", ids[i], (long long)n);
+    if (count == 0 || k == 0) return CLQ_OK;
+    if (!bytes || !out) return fail(CLQ_ERR_ARGUMENT, "null bytes or output");
+    int device;
+    if ((rc = current_device(&device))) return rc;
+    ThreadContext* ctx;
+    if ((rc = thread_context(device, &ctx))) return rc;
+    std::shared_ptr<clq_store> store;
+    int64_t row_begin = 0;
+    if ((rc = cached_store(dtype, n, k, bytes, device, true, ctx->stream, &store, &row_begin))) return rc;
+    const size_t ibytes = (size_t)count * sizeof(int32_t), obytes = (size_t)(count * k) * sizeof(float);
+    cudaError_t e;
+    if ((e = ctx->ids.ensure(ibytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(ids)");
+    if ((e = ctx->out.ensure(obytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(out)");
+    if ((e = cudaMemcpyAsync(ctx->ids.ptr, ids, ibytes, cudaMemcpyHostToDevice, ctx->stream)) != cudaSuccess)
+        return cuda_fail(e, "copy ids to device");
+    clq::WeightView v = view_of(store.get(), row_begin);
+    v.rows = n;
+    if ((e = clq::launch_gather(v, (const int32_t*)ctx->ids.ptr, count, (float*)ctx->out.ptr, ctx->stream)) !=
+        cudaSuccess)
+        return cuda_fail(e, "gather kernel launch");
+    if ((e = cudaMemcpyAsync(out, ctx->out.ptr, obytes, cudaMemcpyDeviceToHost, ctx->stream)) != cudaSuccess)
+        return cuda_fail(e, "copy out to host");
+    if ((e = cudaStreamSynchronize(ctx->stream)) != cudaSuccess) return cuda_fail(e, "take");
+    return CLQ_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,45 @@
+// clq_internal.h -- launchers shared between the C ABI layer and the kernels.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace clq {
+
+// A packed weight as the kernels see it: N rows of K/elems blocks, row-major,
+// in native GGUF bytes on the device.
+struct WeightView {
+    const uint8_t* bytes;  // first byte of row 0 (already offset by any row_begin)
+    int dtype;
+    int64_t rows;          // rows available from `bytes`
+    int64_t k;             // elements per row
+    int64_t row_bytes;     // k / elems * block_bytes
+    int elems;
+    int block_bytes;
+};
+
+bool geometry(int dtype, int* elems, int* block_bytes);
+
+// Writes into *first_bad the smallest block index whose fp16 scale has
+// exponent 31, or leaves it untouched (caller initialises it to ~0ull).
+cudaError_t launch_validate_scales(const uint8_t* dev, int dtype, int64_t nblocks,
+                                   unsigned long long* first_bad, cudaStream_t stream);
+
+cudaError_t launch_dequantize(const WeightView& w, int64_t rows, float* out, bool transposed,
+                              cudaStream_t stream);
+
+// Rows ids[i] of w; an id outside [0, w.rows) yields a row of quiet NaNs.
+cudaError_t launch_gather(const WeightView& w, const int32_t* ids, int64_t count, float* out,
+                          cudaStream_t stream);
+
+// out[i*ldo + j] = sum_c x[i, c] * W[j, c], i < m, j < rows.
+// Returns cudaErrorNotSupported when no kernel covers the request.
+cudaError_t launch_linear(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
+                          float* out, int64_t ldo, unsigned flags, cudaStream_t stream);
+
+// The generic (any alignment, any M) kernel, also used as a fallback by launch_linear.
+cudaError_t launch_linear_generic(const WeightView& w, int64_t rows, const void* x, int xtype,
+                                  int64_t m, float* out, int64_t ldo, cudaStream_t stream);
+
+}  // namespace clq

@@ -1,0 +1,194 @@
+// kernels_basic.cu -- scale validation, bit-exact dequantize/gather, and the
+// generic linear kernel (any row alignment, any number of activation rows).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "../../include/clq.h"
+#include "clq_internal.h"
+#include "formats.cuh"
+
+namespace clq {
+
+bool geometry(int dtype, int* elems, int* block_bytes) {
+    switch (dtype) {
+    case kQ4_0: *elems = 32; *block_bytes = 18; return true;
+    case kQ8_0: *elems = 32; *block_bytes = 34; return true;
+    case kQ4_K: *elems = 256; *block_bytes = 144; return true;
+    case kQ6_K: *elems = 256; *block_bytes = 210; return true;
+    default: return false;
+    }
+}
+
+namespace {
+
+constexpr int kThreads = 256;
+
+int grid_for(int64_t work, int threads) {
+    int64_t blocks = (work + threads - 1) / threads;
+    // 148 SMs x 8 resident blocks of 256 threads covers the machine; grid-stride beyond.
+    return (int)(blocks < 148 * 16 ? (blocks > 0 ? blocks : 1) : 148 * 16);
+}
+
+// mlx/gguf/weights.lisp:19-23 checks (byte & 0x7C) == 0x7C on each scale's high byte.
+__global__ void validate_scales_kernel(const uint8_t* __restrict__ w, int64_t nblocks,
+                                       int block_bytes, int off0, int off1, int noff,
+                                       unsigned long long* first_bad) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nblocks;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const uint8_t* b = w + i * block_bytes;
+        bool bad = (b[off0 + 1] & 0x7C) == 0x7C;
+        if (noff > 1) bad = bad || (b[off1 + 1] & 0x7C) == 0x7C;
+        if (bad) atomicMin(first_bad, (unsigned long long)i);
+    }
+}
+
+template <int D>
+__global__ void dequantize_kernel(const uint8_t* __restrict__ w, int64_t row_bytes, int64_t k,
+                                  int64_t rows, float* __restrict__ out, int transposed) {
+    constexpr int E = Geometry<D>::kElems, B = Geometry<D>::kBytes;
+    int64_t total = rows * k;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t r = i / k, c = i - r * k;
+        float v = element_exact<D>(w + r * row_bytes + (c / E) * B, (int)(c % E));
+        if (transposed) out[c * rows + r] = v;
+        else out[i] = v;
+    }
+}
+
+template <int D>
+__global__ void gather_kernel(const uint8_t* __restrict__ w, int64_t row_bytes, int64_t k,
+                              int64_t nrows, const int32_t* __restrict__ ids, int64_t count,
+                              float* __restrict__ out) {
+    constexpr int E = Geometry<D>::kElems, B = Geometry<D>::kBytes;
+    int64_t total = count * k;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        int64_t t = i / k, c = i - t * k;
+        int64_t r = ids[t];
+        out[i] = (r >= 0 && r < nrows)
+                     ? element_exact<D>(w + r * row_bytes + (c / E) * B, (int)(c % E))
+                     : __int_as_float(0x7fc00000);
+    }
+}
+
+template <typename T> __device__ __forceinline__ float to_f32(T v);
+template <> __device__ __forceinline__ float to_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
+    return __bfloat162float(v);
+}
+template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return __half2float(v); }
+
+// One warp per weight row; lanes stride over 32-element units of the row and
+// decode each element with the reference formula.  Up to MT activation rows
+// per grid.y slice.  Slow but valid for every alignment and shape.
+template <int D, typename XT, int MT>
+__global__ void linear_generic_kernel(const uint8_t* __restrict__ w, int64_t row_bytes, int64_t k,
+                                      int64_t rows, const XT* __restrict__ x, int64_t m,
+                                      float* __restrict__ out, int64_t ldo) {
+    constexpr int E = Geometry<D>::kElems, B = Geometry<D>::kBytes;
+    const int lane = threadIdx.x & 31;
+    const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (row >= rows) return;
+    const int64_t m0 = (int64_t)blockIdx.y * MT;
+    const uint8_t* wr = w + row * row_bytes;
+    float acc[MT];
+#pragma unroll
+    for (int t = 0; t < MT; t++) acc[t] = 0.f;
+    const int64_t units = k / 32;
+    for (int64_t u = lane; u < units; u += 32) {
+        const int64_t e0 = u * 32;
+        const uint8_t* b = wr + (e0 / E) * B;
+        const int eb = (int)(e0 % E);
+        for (int i = 0; i < 32; i++) {
+            float wv = element_exact<D>(b, eb + i);
+#pragma unroll
+            for (int t = 0; t < MT; t++)
+                if (m0 + t < m) acc[t] = fmaf(to_f32(x[(m0 + t) * k + e0 + i]), wv, acc[t]);
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < MT; t++) {
+        float v = acc[t];
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        if (lane == 0 && m0 + t < m) out[(m0 + t) * ldo + row] = v;
+    }
+}
+
+template <int D, typename XT>
+cudaError_t generic_launch(const WeightView& w, int64_t rows, const XT* x, int64_t m, float* out,
+                           int64_t ldo, cudaStream_t s) {
+    constexpr int MT = 4, WARPS = 4;
+    dim3 grid((unsigned)((rows + WARPS - 1) / WARPS), (unsigned)((m + MT - 1) / MT));
+    if (grid.y > 65535) return cudaErrorInvalidConfiguration;
+    linear_generic_kernel<D, XT, MT><<<grid, WARPS * 32, 0, s>>>(w.bytes, w.row_bytes, w.k, rows, x,
+                                                                 m, out, ldo);
+    return cudaGetLastError();
+}
+
+template <typename XT>
+cudaError_t generic_by_dtype(const WeightView& w, int64_t rows, const XT* x, int64_t m, float* out,
+                             int64_t ldo, cudaStream_t s) {
+    switch (w.dtype) {
+    case kQ4_0: return generic_launch<kQ4_0, XT>(w, rows, x, m, out, ldo, s);
+    case kQ8_0: return generic_launch<kQ8_0, XT>(w, rows, x, m, out, ldo, s);
+    case kQ4_K: return generic_launch<kQ4_K, XT>(w, rows, x, m, out, ldo, s);
+    case kQ6_K: return generic_launch<kQ6_K, XT>(w, rows, x, m, out, ldo, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_validate_scales(const uint8_t* dev, int dtype, int64_t nblocks,
+                                   unsigned long long* first_bad, cudaStream_t stream) {
+    int elems, bb, off[2] = {0, 0};
+    if (!geometry(dtype, &elems, &bb)) return cudaErrorInvalidValue;
+    int noff = scale_offsets(dtype, off);
+    if (nblocks <= 0) return cudaSuccess;
+    validate_scales_kernel<<<grid_for(nblocks, kThreads), kThreads, 0, stream>>>(
+        dev, nblocks, bb, off[0], off[1], noff, first_bad);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_dequantize(const WeightView& w, int64_t rows, float* out, bool transposed,
+                              cudaStream_t s) {
+    if (rows <= 0 || w.k <= 0) return cudaSuccess;
+    int g = grid_for(rows * w.k, kThreads);
+    int t = transposed ? 1 : 0;
+    switch (w.dtype) {
+    case kQ4_0: dequantize_kernel<kQ4_0><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, rows, out, t); break;
+    case kQ8_0: dequantize_kernel<kQ8_0><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, rows, out, t); break;
+    case kQ4_K: dequantize_kernel<kQ4_K><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, rows, out, t); break;
+    case kQ6_K: dequantize_kernel<kQ6_K><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, rows, out, t); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_gather(const WeightView& w, const int32_t* ids, int64_t count, float* out,
+                          cudaStream_t s) {
+    if (count <= 0 || w.k <= 0) return cudaSuccess;
+    int g = grid_for(count * w.k, kThreads);
+    switch (w.dtype) {
+    case kQ4_0: gather_kernel<kQ4_0><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, w.rows, ids, count, out); break;
+    case kQ8_0: gather_kernel<kQ8_0><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, w.rows, ids, count, out); break;
+    case kQ4_K: gather_kernel<kQ4_K><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, w.rows, ids, count, out); break;
+    case kQ6_K: gather_kernel<kQ6_K><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, w.rows, ids, count, out); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_linear_generic(const WeightView& w, int64_t rows, const void* x, int xtype,
+                                  int64_t m, float* out, int64_t ldo, cudaStream_t s) {
+    if (rows <= 0 || m <= 0) return cudaSuccess;
+    switch (xtype) {
+    case CLQ_X_F32: return generic_by_dtype(w, rows, (const float*)x, m, out, ldo, s);
+    case CLQ_X_BF16: return generic_by_dtype(w, rows, (const __nv_bfloat16*)x, m, out, ldo, s);
+    case CLQ_X_F16: return generic_by_dtype(w, rows, (const __half*)x, m, out, ldo, s);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace clq

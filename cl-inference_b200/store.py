@@ -1,0 +1,109 @@
+"""Device-resident packed-weight store and device-pointer products.
+
+torch provides device memory and streams here (plumbing); the products,
+dequantize and gather are libclq kernels.
+"""
+import ctypes
+
+import numpy as np
+
+from . import _lib
+from .quant import find_dtype
+
+_XTYPE = {"float32": _lib.CLQ_X_F32, "bfloat16": _lib.CLQ_X_BF16, "float16": _lib.CLQ_X_F16}
+
+
+def _torch():
+    import torch
+    return torch
+
+
+def current_stream_handle():
+    torch = _torch()
+    return torch.cuda.current_stream().cuda_stream
+
+
+class Store:
+    """N x K packed blocks uploaded once in native GGUF layout (clq_store_create).
+
+    DATA is a host uint8 numpy array, or a uint8 CUDA tensor on the current device.
+    """
+
+    def __init__(self, dtype, n, k, data):
+        self.dtype = find_dtype(dtype)
+        self.n, self.k = int(n), int(k)
+        handle = ctypes.c_void_p()
+        torch = _torch()
+        if isinstance(data, np.ndarray):
+            data = np.ascontiguousarray(data, dtype=np.uint8)
+            _lib.check(_lib.lib.clq_store_create(self.dtype.ggml_type, self.n, self.k, data.ctypes.data,
+                                                 data.size, 0, ctypes.byref(handle)))
+        elif isinstance(data, torch.Tensor) and data.is_cuda and data.dtype == torch.uint8:
+            data = data.contiguous()
+            _lib.check(_lib.lib.clq_store_create_device(self.dtype.ggml_type, self.n, self.k,
+                                                        data.data_ptr(), data.numel(), 0,
+                                                        current_stream_handle(), ctypes.byref(handle)))
+        else:
+            raise TypeError("store data must be a uint8 numpy array or a uint8 CUDA tensor")
+        self._handle = handle
+
+    @property
+    def handle(self):
+        if self._handle is None:
+            raise ValueError("store is closed")
+        return self._handle
+
+    @property
+    def row_bytes(self):
+        return self.k // self.dtype.block_size * self.dtype.block_bytes
+
+    def close(self):
+        if self._handle is not None:
+            _lib.lib.clq_store_free(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def linear(self, x, out=None, row_begin=0, rows=None, flags=0, stream=None):
+        """out[m, :rows] = x[m, K] . W[row_begin:row_begin+rows]^T (clq_linear_device)."""
+        torch = _torch()
+        rows = self.n - row_begin if rows is None else rows
+        if x.dim() != 2 or x.shape[1] != self.k or not x.is_cuda:
+            raise ValueError(f"x must be a CUDA [m, {self.k}] matrix, got {tuple(x.shape)}")
+        x = x.contiguous()
+        m = x.shape[0]
+        if out is None:
+            out = torch.empty((m, rows), dtype=torch.float32, device=x.device)
+        ldo = out.stride(0) if out.dim() == 2 and m > 0 else rows
+        if out.dtype != torch.float32 or (out.dim() == 2 and out.stride(1) != 1):
+            raise ValueError("out must be float32 with unit column stride")
+        xtype = _XTYPE.get(str(x.dtype).replace("torch.", ""))
+        if xtype is None:
+            raise ValueError(f"unsupported activation dtype {x.dtype}")
+        _lib.check(_lib.lib.clq_linear_device(self.handle, row_begin, rows, x.data_ptr(), xtype, m,
+                                              out.data_ptr(), ldo, flags,
+                                              stream if stream is not None else current_stream_handle()))
+        return out
+
+    def dequantize(self, row_begin=0, rows=None, transposed=False, out=None):
+        torch = _torch()
+        rows = self.n - row_begin if rows is None else rows
+        if out is None:
+            shape = (self.k, rows) if transposed else (rows, self.k)
+            out = torch.empty(shape, dtype=torch.float32, device="cuda")
+        _lib.check(_lib.lib.clq_dequantize_device(self.handle, row_begin, rows, out.data_ptr(),
+                                                  1 if transposed else 0, current_stream_handle()))
+        return out
+
+    def gather(self, ids, out=None):
+        torch = _torch()
+        ids = ids.to(dtype=torch.int32).contiguous()
+        if out is None:
+            out = torch.empty((ids.numel(), self.k), dtype=torch.float32, device=ids.device)
+        _lib.check(_lib.lib.clq_gather_device(self.handle, ids.data_ptr(), ids.numel(), out.data_ptr(),
+                                              current_stream_handle()))
+        return out

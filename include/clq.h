@@ -1,0 +1,148 @@
+/*
+ * clq.h -- C ABI of libclq, the B200 (sm_100a) quantized-linear library for
+ * cl-inference's packed GGUF weights (Q8_0, Q4_0, Q4_K, Q6_K).
+ *
+ * Plain pointers and sizes only; no CUDA or torch types.  A `stream` argument
+ * is a cudaStream_t passed as void* (NULL = the library's per-thread stream for
+ * host-pointer calls, the legacy default stream for device-pointer calls).
+ *
+ * Every function returns 0 (CLQ_OK) or a CLQ_ERR_* code; clq_last_error() gives
+ * the calling thread's message for its most recent failure.  Reference paths
+ * cited below are relative to the cl-inference project.
+ */
+#ifndef CLQ_H
+#define CLQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CLQ_ABI_VERSION 1
+
+/* Packed dtypes, numbered by their ggml type id (gguf/reader.lisp:37-52). */
+enum clq_dtype {
+    CLQ_Q4_0 = 2,  /*  32 elements,  18 bytes: quant/packed.lisp:156 */
+    CLQ_Q8_0 = 8,  /*  32 elements,  34 bytes: quant/q8-0.lisp:5-6   */
+    CLQ_Q4_K = 12, /* 256 elements, 144 bytes: quant/packed.lisp:157 */
+    CLQ_Q6_K = 14  /* 256 elements, 210 bytes: quant/packed.lisp:158 */
+};
+
+/* Activation element types for the device-pointer products. */
+enum clq_xtype { CLQ_X_F32 = 0, CLQ_X_BF16 = 1, CLQ_X_F16 = 2 };
+
+enum clq_status {
+    CLQ_OK = 0,
+    CLQ_ERR_ARGUMENT = 1,       /* null pointer, unknown dtype, bad flag            */
+    CLQ_ERR_SHAPE = 2,          /* shape mismatch; K not a multiple of the block    */
+    CLQ_ERR_BLOCKS = 3,         /* byte count is not a whole number of blocks       */
+    CLQ_ERR_NONFINITE_SCALE = 4,/* an fp16 scale has exponent 31 (quant/q8-0.lisp:95) */
+    CLQ_ERR_CUDA = 5,           /* a CUDA runtime call failed                        */
+    CLQ_ERR_NCCL = 6,           /* a collective failed                               */
+    CLQ_ERR_TIMEOUT = 7,        /* a bounded wait ran out                            */
+    CLQ_ERR_NO_DEVICE = 8,      /* no usable sm_100 device                           */
+    CLQ_ERR_UNSUPPORTED = 9,    /* valid request this build does not implement       */
+    CLQ_ERR_OUT_OF_MEMORY = 10
+};
+
+/* Store creation flags. */
+#define CLQ_STORE_DEFAULT 0u
+
+/* Product flags. */
+#define CLQ_MATH_DEFAULT 0u   /* fp32-class results (all M)                          */
+#define CLQ_MATH_FAST 1u      /* prefill GEMM may round dequantized weights to fp16  */
+#define CLQ_NO_CACHE 2u       /* host-pointer calls: upload, use and drop the weight */
+
+/* ---- library ------------------------------------------------------------- */
+
+int clq_abi_version(void);
+/* Copies the calling thread's last error message (NUL-terminated, truncated). */
+int clq_last_error(char *buf, size_t len);
+/* Elements and bytes per block of DTYPE. */
+int clq_block_geometry(int dtype, int64_t *elements, int64_t *block_bytes);
+
+/* ---- drop-in kernels ------------------------------------------------------
+ * Same arguments and meaning as the trivial-simd kernels the packed dtypes
+ * bind: (kernel out x bytes M N K), called from packed-matmul-executor
+ * (quant/packed.lisp:68-75, slots registered at :156-158) and from the Q8_0
+ * matmul-executor (quant/q8-0.lisp:87-94).
+ *   out   host f32 [M, N] row-major, written
+ *   x     host f32 [M, K] row-major, contiguous
+ *   bytes host packed weight, N rows of K/elements blocks (row-major (N K)),
+ *         beginning at the weight view's whole-row offset (packed.lisp:60-66)
+ * The weight is uploaded to the current device once and cached by host
+ * address range (the identity of a mapped GGUF view, gguf/weights.lisp:68-78);
+ * a pointer inside a cached range at a whole-row offset reuses it.  Calls are
+ * synchronous: `out` is valid on return.  M = 0 is a no-op.
+ */
+int clq_q8_0_matmul(float *out, const float *x, const uint8_t *bytes, int64_t m, int64_t n,
+                    int64_t k);
+int clq_q4_0_matmul(float *out, const float *x, const uint8_t *bytes, int64_t m, int64_t n,
+                    int64_t k);
+int clq_q4_k_matmul(float *out, const float *x, const uint8_t *bytes, int64_t m, int64_t n,
+                    int64_t k);
+int clq_q6_k_matmul(float *out, const float *x, const uint8_t *bytes, int64_t m, int64_t n,
+                    int64_t k);
+/* The four above with the dtype as an argument and CLQ_* flags. */
+int clq_matmul(int dtype, float *out, const float *x, const uint8_t *bytes, int64_t m, int64_t n,
+               int64_t k, unsigned flags);
+
+/* Drop cached weights whose host range overlaps [bytes, bytes + nbytes):
+ * call before the mapping is released (close-weights, local/weights.lisp:84-89). */
+int clq_forget(const uint8_t *bytes, size_t nbytes);
+/* Drop every cached weight on every device. */
+int clq_clear_cache(void);
+/* Number of cached weights and their device bytes. */
+int clq_cache_stats(int64_t *count, int64_t *device_bytes);
+
+/* ---- device-resident packed-weight store ----------------------------------
+ * Uploads N x K packed blocks once, in their native GGUF byte layout, to the
+ * current device, after checking that every fp16 scale is finite (the load-time
+ * check of mlx/gguf/weights.lisp:19-23).  The store owns the device copy.
+ */
+typedef struct clq_store clq_store;
+
+int clq_store_create(int dtype, int64_t n, int64_t k, const uint8_t *host_bytes, size_t nbytes,
+                     unsigned flags, clq_store **out);
+/* Same from bytes already on the current device (copied; DEVICE_BYTES may be freed after). */
+int clq_store_create_device(int dtype, int64_t n, int64_t k, const void *device_bytes,
+                            size_t nbytes, unsigned flags, void *stream, clq_store **out);
+int clq_store_free(clq_store *store);
+int clq_store_info(const clq_store *store, int *dtype, int64_t *n, int64_t *k, size_t *nbytes,
+                   const void **device_bytes, int *device);
+
+/* ---- device-pointer products (activations stay resident) ------------------
+ * out[i, j] (j < rows) = sum_c x[i, c] * W[row_begin + j, c] for i < m, with
+ * out row stride LDO floats (>= rows).  X is [m, K] contiguous of XTYPE.
+ * Asynchronous on STREAM.  This is the linear of local/blocks.lisp:106-113 for a
+ * packed weight, over a row range of it (a column-parallel shard when
+ * row_begin/rows select a rank's rows).
+ */
+int clq_linear_device(const clq_store *w, int64_t row_begin, int64_t rows, const void *x,
+                      int xtype, int64_t m, float *out, int64_t ldo, unsigned flags,
+                      void *stream);
+
+/* ---- dequantize and gather ------------------------------------------------
+ * Bit-exact fp32 values of packed-element (quant/packed.lisp:85-108) and the
+ * Q8_0 dequantize-executor (quant/q8-0.lisp:98-123).
+ */
+/* Rows [row_begin, row_begin + rows) into OUT (device, [rows, K] row-major, or
+ * [K, rows] when TRANSPOSED is non-zero: the transposed-view astype). */
+int clq_dequantize_device(const clq_store *w, int64_t row_begin, int64_t rows, float *out,
+                          int transposed, void *stream);
+/* ct:take + dequantize of local/blocks.lisp:136-138: OUT[i, :] = row IDS[i]
+ * (device int32 ids, duplicates allowed; an id outside [0, N) is an error
+ * reported through *bad_id_flag-free status after the call completes). */
+int clq_gather_device(const clq_store *w, const int32_t *ids, int64_t count, float *out,
+                      void *stream);
+/* Host-pointer forms (synchronous; the bytes are uploaded for the call only). */
+int clq_dequantize(int dtype, const uint8_t *bytes, size_t nbytes, float *out);
+int clq_take(int dtype, const uint8_t *bytes, int64_t n, int64_t k, const int32_t *ids,
+             int64_t count, float *out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CLQ_H */
