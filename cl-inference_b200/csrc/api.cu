@@ -11,15 +11,17 @@
 
 #include "../../include/clq.h"
 #include "clq_internal.h"
+#include "layout.cuh"
 
 struct clq_store {
     int dtype = 0;
     int64_t n = 0, k = 0;
-    size_t nbytes = 0;
+    size_t nbytes = 0;            // native GGUF bytes
     int device = -1;
-    uint8_t* dev = nullptr;
+    uint8_t* dev = nullptr;       // re-tiled planes (layout.cuh)
+    size_t s_off = 0, d_off = 0;  // plane offsets inside dev
     int elems = 0, block_bytes = 0;
-    int64_t row_bytes = 0;
+    int64_t row_bytes = 0, nb = 0;
 };
 
 namespace {
@@ -81,14 +83,16 @@ int check_shape(int dtype, int64_t n, int64_t k, int* elems, int* bb) {
 }
 
 clq::WeightView view_of(const clq_store* s, int64_t row_begin) {
+    clq::PlaneGeometry g = clq::plane_geometry(s->dtype);
+    const int64_t blk = row_begin * s->nb;
     clq::WeightView v;
-    v.bytes = s->dev + row_begin * s->row_bytes;
     v.dtype = s->dtype;
     v.rows = s->n - row_begin;
     v.k = s->k;
-    v.row_bytes = s->row_bytes;
-    v.elems = s->elems;
-    v.block_bytes = s->block_bytes;
+    v.nb = s->nb;
+    v.q = s->dev + blk * g.q_block;
+    v.s = s->dev + s->s_off + blk * g.s_block;
+    v.d = s->dev + s->d_off + blk * g.d_block;
     return v;
 }
 
@@ -104,7 +108,8 @@ void destroy_store(clq_store* s) {
     delete s;
 }
 
-// Allocate, copy (from host or device), validate scales.  Synchronous.
+// Copy the native blocks to the device (or use them in place when already
+// there), check every scale is finite, re-tile into the planes.  Synchronous.
 int make_store(int dtype, int64_t n, int64_t k, const void* src, bool src_on_device, size_t nbytes,
                cudaStream_t stream, clq_store** out) {
     int elems, bb, rc;
@@ -121,35 +126,39 @@ int make_store(int dtype, int64_t n, int64_t k, const void* src, bool src_on_dev
     if ((rc = current_device(&device))) return rc;
     std::unique_ptr<clq_store, void (*)(clq_store*)> s(new clq_store, destroy_store);
     s->dtype = dtype; s->n = n; s->k = k; s->nbytes = nbytes; s->device = device;
-    s->elems = elems; s->block_bytes = bb; s->row_bytes = row_bytes;
-    // Round up and keep 256 zero bytes of tail so vector loads past the last
-    // block stay inside the allocation.
-    size_t alloc = ((nbytes + 255) & ~(size_t)255) + 256;
-    cudaError_t e = cudaMalloc((void**)&s->dev, alloc);
+    s->elems = elems; s->block_bytes = bb; s->row_bytes = row_bytes; s->nb = k / elems;
+    const int64_t nblocks = n * s->nb;
+    size_t total;
+    clq::plane_offsets(dtype, nblocks, &s->s_off, &s->d_off, &total);
+    cudaError_t e = cudaMalloc((void**)&s->dev, total);
     if (e != cudaSuccess) { s->dev = nullptr; return cuda_fail(e, "cudaMalloc(weight store)"); }
+    uint8_t* native = nullptr;
+    if (nbytes && !src_on_device) {
+        e = cudaMalloc((void**)&native, nbytes);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(upload staging)");
+    }
     unsigned long long* flag = nullptr;
     e = cudaMalloc((void**)&flag, sizeof *flag);
-    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(flag)");
+    if (e != cudaSuccess) { cudaFree(native); return cuda_fail(e, "cudaMalloc(flag)"); }
+    const uint8_t* nat = src_on_device ? (const uint8_t*)src : native;
     unsigned long long first_bad = ~0ull;
     do {
-        if ((e = cudaMemsetAsync(s->dev + nbytes, 0, alloc - nbytes, stream)) != cudaSuccess) break;
-        if (nbytes &&
-            (e = cudaMemcpyAsync(s->dev, src, nbytes,
-                                 src_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
-                                 stream)) != cudaSuccess)
+        if ((e = cudaMemsetAsync(s->dev, 0, total, stream)) != cudaSuccess) break;
+        if (nbytes && !src_on_device &&
+            (e = cudaMemcpyAsync(native, src, nbytes, cudaMemcpyHostToDevice, stream)) != cudaSuccess)
             break;
         if ((e = cudaMemcpyAsync(flag, &first_bad, sizeof first_bad, cudaMemcpyHostToDevice, stream)) !=
             cudaSuccess)
             break;
-        if ((e = clq::launch_validate_scales(s->dev, dtype, (int64_t)(nbytes / bb), flag, stream)) !=
-            cudaSuccess)
-            break;
+        if ((e = clq::launch_validate_scales(nat, dtype, nblocks, flag, stream)) != cudaSuccess) break;
+        if ((e = clq::launch_retile(nat, dtype, n, s->nb, s->dev, stream)) != cudaSuccess) break;
         if ((e = cudaMemcpyAsync(&first_bad, flag, sizeof first_bad, cudaMemcpyDeviceToHost, stream)) !=
             cudaSuccess)
             break;
         e = cudaStreamSynchronize(stream);
     } while (0);
     cudaFree(flag);
+    if (native) cudaFree(native);
     if (e != cudaSuccess) return cuda_fail(e, "weight upload");
     if (first_bad != ~0ull)
         return fail(CLQ_ERR_NONFINITE_SCALE, "Non-finite %s scale at byte %llu", dtype_name(dtype),

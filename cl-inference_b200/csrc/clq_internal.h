@@ -7,19 +7,24 @@
 
 namespace clq {
 
-// A packed weight as the kernels see it: N rows of K/elems blocks, row-major,
-// in native GGUF bytes on the device.
+// A packed weight as the kernels see it: N rows of K/elems blocks in the
+// re-tiled device planes of layout.cuh, offset to the view's first row.
 struct WeightView {
-    const uint8_t* bytes;  // first byte of row 0 (already offset by any row_begin)
     int dtype;
-    int64_t rows;          // rows available from `bytes`
+    int64_t rows;          // rows available from row 0 of the view
     int64_t k;             // elements per row
-    int64_t row_bytes;     // k / elems * block_bytes
-    int elems;
-    int block_bytes;
+    int64_t nb;            // blocks per row
+    const uint8_t* q;      // planes (see layout.cuh), already offset to row 0
+    const uint8_t* s;
+    const uint8_t* d;
 };
 
 bool geometry(int dtype, int* elems, int* block_bytes);
+
+// Re-tile NBLOCKS native GGUF blocks (N rows of NB blocks) into the planes at
+// DST (layout.cuh); the planes' tail must be zeroed by the caller.
+cudaError_t launch_retile(const uint8_t* native, int dtype, int64_t n, int64_t nb, uint8_t* dst,
+                          cudaStream_t stream);
 
 // Writes into *first_bad the smallest block index whose fp16 scale has
 // exponent 31, or leaves it untouched (caller initialises it to ~0ull).
@@ -37,6 +42,11 @@ cudaError_t launch_gather(const WeightView& w, const int32_t* ids, int64_t count
 // Returns cudaErrorNotSupported when no kernel covers the request.
 cudaError_t launch_linear(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
                           float* out, int64_t ldo, unsigned flags, cudaStream_t stream);
+
+// Tensor-core fused dequant + GEMV (K a multiple of 256).
+bool gemv_mma_supported(const WeightView& w, int64_t m);
+cudaError_t launch_gemv_mma(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
+                            float* out, int64_t ldo, cudaStream_t stream);
 
 // The generic (any alignment, any M) kernel, also used as a fallback by launch_linear.
 cudaError_t launch_linear_generic(const WeightView& w, int64_t rows, const void* x, int xtype,

@@ -6,6 +6,7 @@
 #include "../../include/clq.h"
 #include "clq_internal.h"
 #include "formats.cuh"
+#include "layout.cuh"
 
 namespace clq {
 
@@ -22,6 +23,8 @@ bool geometry(int dtype, int* elems, int* block_bytes) {
 namespace {
 
 constexpr int kThreads = 256;
+
+Planes planes_of(const WeightView& w) { return Planes{w.q, w.s, w.d, w.nb}; }
 
 int grid_for(int64_t work, int threads) {
     int64_t blocks = (work + threads - 1) / threads;
@@ -43,32 +46,62 @@ __global__ void validate_scales_kernel(const uint8_t* __restrict__ w, int64_t nb
 }
 
 template <int D>
-__global__ void dequantize_kernel(const uint8_t* __restrict__ w, int64_t row_bytes, int64_t k,
-                                  int64_t rows, float* __restrict__ out, int transposed) {
-    constexpr int E = Geometry<D>::kElems, B = Geometry<D>::kBytes;
+__global__ void dequantize_kernel(Planes p, int64_t k, int64_t rows, float* __restrict__ out,
+                                  int transposed) {
     int64_t total = rows * k;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         int64_t r = i / k, c = i - r * k;
-        float v = element_exact<D>(w + r * row_bytes + (c / E) * B, (int)(c % E));
+        float v = element_planar<D>(p, r, c);
         if (transposed) out[c * rows + r] = v;
         else out[i] = v;
     }
 }
 
 template <int D>
-__global__ void gather_kernel(const uint8_t* __restrict__ w, int64_t row_bytes, int64_t k,
-                              int64_t nrows, const int32_t* __restrict__ ids, int64_t count,
-                              float* __restrict__ out) {
-    constexpr int E = Geometry<D>::kElems, B = Geometry<D>::kBytes;
+__global__ void gather_kernel(Planes p, int64_t k, int64_t nrows, const int32_t* __restrict__ ids,
+                              int64_t count, float* __restrict__ out) {
     int64_t total = count * k;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         int64_t t = i / k, c = i - t * k;
         int64_t r = ids[t];
-        out[i] = (r >= 0 && r < nrows)
-                     ? element_exact<D>(w + r * row_bytes + (c / E) * B, (int)(c % E))
-                     : __int_as_float(0x7fc00000);
+        out[i] = (r >= 0 && r < nrows) ? element_planar<D>(p, r, c) : __int_as_float(0x7fc00000);
+    }
+}
+
+// One thread per native block: scatter its bytes into the planes.
+template <int D>
+__global__ void retile_kernel(const uint8_t* __restrict__ native, int64_t n, int64_t nb,
+                              uint8_t* __restrict__ q, uint8_t* __restrict__ s, uint8_t* __restrict__ d) {
+    constexpr int B = Geometry<D>::kBytes;
+    const int64_t total = n * nb;
+    for (int64_t blk = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; blk < total;
+         blk += (int64_t)gridDim.x * blockDim.x) {
+        const uint8_t* src = native + blk * B;
+        const int64_t row = blk / nb, j = blk % nb;
+        if (D == kQ4_K) {
+            for (int i = 0; i < 144; i++) q[blk * 144 + i] = src[i];
+        } else if (D == kQ4_0) {
+            d[2 * blk] = src[0]; d[2 * blk + 1] = src[1];
+            for (int i = 0; i < 16; i++) q[row * nb * 16 + chunk_code_offset<16>(nb, j, i)] = src[2 + i];
+        } else if (D == kQ8_0) {
+            d[2 * blk] = src[0]; d[2 * blk + 1] = src[1];
+            for (int i = 0; i < 32; i++) q[row * nb * 32 + chunk_code_offset<32>(nb, j, i)] = src[2 + i];
+        } else {  // Q6_K
+            for (int i = 0; i < 128; i++) {  // ql: element (h, grp, l) low bits
+                const int h = i / 64, p = (i % 64) / 32, l = i % 32;
+                const int half = l / 16, t = (l % 16) / 4, bw = l % 4;
+                q[blk * 192 + t * 48 + (2 * h + half) * 12 + 4 * p + bw] = src[i];
+            }
+            for (int i = 0; i < 64; i++) {  // qh
+                const int h = i / 32, l = i % 32;
+                const int half = l / 16, t = (l % 16) / 4, bw = l % 4;
+                q[blk * 192 + t * 48 + (2 * h + half) * 12 + 8 + bw] = src[128 + i];
+            }
+            for (int i = 0; i < 16; i++) s[blk * 16 + i] = src[192 + i];
+            d[2 * blk] = src[208]; d[2 * blk + 1] = src[209];
+        }
     }
 }
 
@@ -83,25 +116,20 @@ template <> __device__ __forceinline__ float to_f32<__half>(__half v) { return _
 // decode each element with the reference formula.  Up to MT activation rows
 // per grid.y slice.  Slow but valid for every alignment and shape.
 template <int D, typename XT, int MT>
-__global__ void linear_generic_kernel(const uint8_t* __restrict__ w, int64_t row_bytes, int64_t k,
-                                      int64_t rows, const XT* __restrict__ x, int64_t m,
-                                      float* __restrict__ out, int64_t ldo) {
-    constexpr int E = Geometry<D>::kElems, B = Geometry<D>::kBytes;
+__global__ void linear_generic_kernel(Planes p, int64_t k, int64_t rows, const XT* __restrict__ x,
+                                      int64_t m, float* __restrict__ out, int64_t ldo) {
     const int lane = threadIdx.x & 31;
     const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
     if (row >= rows) return;
     const int64_t m0 = (int64_t)blockIdx.y * MT;
-    const uint8_t* wr = w + row * row_bytes;
     float acc[MT];
 #pragma unroll
     for (int t = 0; t < MT; t++) acc[t] = 0.f;
     const int64_t units = k / 32;
     for (int64_t u = lane; u < units; u += 32) {
         const int64_t e0 = u * 32;
-        const uint8_t* b = wr + (e0 / E) * B;
-        const int eb = (int)(e0 % E);
         for (int i = 0; i < 32; i++) {
-            float wv = element_exact<D>(b, eb + i);
+            float wv = element_planar<D>(p, row, e0 + i);
 #pragma unroll
             for (int t = 0; t < MT; t++)
                 if (m0 + t < m) acc[t] = fmaf(to_f32(x[(m0 + t) * k + e0 + i]), wv, acc[t]);
@@ -121,8 +149,7 @@ cudaError_t generic_launch(const WeightView& w, int64_t rows, const XT* x, int64
     constexpr int MT = 4, WARPS = 4;
     dim3 grid((unsigned)((rows + WARPS - 1) / WARPS), (unsigned)((m + MT - 1) / MT));
     if (grid.y > 65535) return cudaErrorInvalidConfiguration;
-    linear_generic_kernel<D, XT, MT><<<grid, WARPS * 32, 0, s>>>(w.bytes, w.row_bytes, w.k, rows, x,
-                                                                 m, out, ldo);
+    linear_generic_kernel<D, XT, MT><<<grid, WARPS * 32, 0, s>>>(planes_of(w), w.k, rows, x, m, out, ldo);
     return cudaGetLastError();
 }
 
@@ -151,16 +178,33 @@ cudaError_t launch_validate_scales(const uint8_t* dev, int dtype, int64_t nblock
     return cudaGetLastError();
 }
 
+cudaError_t launch_retile(const uint8_t* native, int dtype, int64_t n, int64_t nb, uint8_t* dst,
+                          cudaStream_t s) {
+    if (n * nb == 0) return cudaSuccess;
+    size_t s_off, d_off, total;
+    plane_offsets(dtype, n * nb, &s_off, &d_off, &total);
+    uint8_t *q = dst, *sp = dst + s_off, *dp = dst + d_off;
+    int g = grid_for(n * nb, kThreads);
+    switch (dtype) {
+    case kQ4_0: retile_kernel<kQ4_0><<<g, kThreads, 0, s>>>(native, n, nb, q, sp, dp); break;
+    case kQ8_0: retile_kernel<kQ8_0><<<g, kThreads, 0, s>>>(native, n, nb, q, sp, dp); break;
+    case kQ4_K: retile_kernel<kQ4_K><<<g, kThreads, 0, s>>>(native, n, nb, q, sp, dp); break;
+    case kQ6_K: retile_kernel<kQ6_K><<<g, kThreads, 0, s>>>(native, n, nb, q, sp, dp); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
 cudaError_t launch_dequantize(const WeightView& w, int64_t rows, float* out, bool transposed,
                               cudaStream_t s) {
     if (rows <= 0 || w.k <= 0) return cudaSuccess;
     int g = grid_for(rows * w.k, kThreads);
     int t = transposed ? 1 : 0;
     switch (w.dtype) {
-    case kQ4_0: dequantize_kernel<kQ4_0><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, rows, out, t); break;
-    case kQ8_0: dequantize_kernel<kQ8_0><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, rows, out, t); break;
-    case kQ4_K: dequantize_kernel<kQ4_K><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, rows, out, t); break;
-    case kQ6_K: dequantize_kernel<kQ6_K><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, rows, out, t); break;
+    case kQ4_0: dequantize_kernel<kQ4_0><<<g, kThreads, 0, s>>>(planes_of(w), w.k, rows, out, t); break;
+    case kQ8_0: dequantize_kernel<kQ8_0><<<g, kThreads, 0, s>>>(planes_of(w), w.k, rows, out, t); break;
+    case kQ4_K: dequantize_kernel<kQ4_K><<<g, kThreads, 0, s>>>(planes_of(w), w.k, rows, out, t); break;
+    case kQ6_K: dequantize_kernel<kQ6_K><<<g, kThreads, 0, s>>>(planes_of(w), w.k, rows, out, t); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();
@@ -171,10 +215,10 @@ cudaError_t launch_gather(const WeightView& w, const int32_t* ids, int64_t count
     if (count <= 0 || w.k <= 0) return cudaSuccess;
     int g = grid_for(count * w.k, kThreads);
     switch (w.dtype) {
-    case kQ4_0: gather_kernel<kQ4_0><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, w.rows, ids, count, out); break;
-    case kQ8_0: gather_kernel<kQ8_0><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, w.rows, ids, count, out); break;
-    case kQ4_K: gather_kernel<kQ4_K><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, w.rows, ids, count, out); break;
-    case kQ6_K: gather_kernel<kQ6_K><<<g, kThreads, 0, s>>>(w.bytes, w.row_bytes, w.k, w.rows, ids, count, out); break;
+    case kQ4_0: gather_kernel<kQ4_0><<<g, kThreads, 0, s>>>(planes_of(w), w.k, w.rows, ids, count, out); break;
+    case kQ8_0: gather_kernel<kQ8_0><<<g, kThreads, 0, s>>>(planes_of(w), w.k, w.rows, ids, count, out); break;
+    case kQ4_K: gather_kernel<kQ4_K><<<g, kThreads, 0, s>>>(planes_of(w), w.k, w.rows, ids, count, out); break;
+    case kQ6_K: gather_kernel<kQ6_K><<<g, kThreads, 0, s>>>(planes_of(w), w.k, w.rows, ids, count, out); break;
     default: return cudaErrorInvalidValue;
     }
     return cudaGetLastError();

@@ -219,3 +219,24 @@ def test_device_linear_shards_and_activation_types(cuda, clq, synth, oracle, dty
     assert torch.isnan(out[:, n:]).all()
     assert element_bound_ok(got, ref, mag)
     store.close()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_activation_magnitudes_across_fp32_range(cuda, clq, synth, oracle, dtype):
+    """Tiny, huge, zero and mixed activation rows keep the fp32-class bound."""
+    torch = cuda
+    n, k = 48, 1024
+    data = synth.packed_blocks(dtype, n, k, seed=5)
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((4, k)).astype(np.float32)
+    x[0] *= np.float32(1e-30)
+    x[1] *= np.float32(1e30)
+    x[2, :512] = 0.0
+    x[2, 512:] *= np.float32(1e4)
+    x[3, ::7] *= np.float32(1e-6)
+    ref, mag = oracle.matmul_f64(dtype, x, data, n)
+    store = clq.Store(dtype, n, k, data)
+    got = store.linear(torch.from_numpy(x).cuda()).cpu().numpy().astype(np.float64)
+    assert np.all(np.isfinite(got))
+    assert np.all(np.abs(got - ref) <= 1e-5 * mag + 1e-37)
+    store.close()
