@@ -14,6 +14,8 @@
 // results, so the result carries fp32-class error, like an fp32 dot product.
 // The CTA splits K across warps and reduces through shared memory; activations
 // are staged once per CTA into shared memory in MMA-fragment order.
+#include <cstdlib>
+
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -109,27 +111,50 @@ template <> struct Words<kQ8_0> { static constexpr int n = 20; };  // 64 B codes
 
 #define CLQ_PUT4(w, i, v) do { (w)[(i)] = (v).x; (w)[(i) + 1] = (v).y; (w)[(i) + 2] = (v).z; (w)[(i) + 3] = (v).w; } while (0)
 
+// Bytes per 256-column chunk in each plane, and this lane's offset in the q plane.
+template <int D> struct ChunkBytes;
+template <> struct ChunkBytes<kQ4_K> { static constexpr int q = 144, s = 0, d = 0; };
+template <> struct ChunkBytes<kQ6_K> { static constexpr int q = 192, s = 16, d = 2; };
+template <> struct ChunkBytes<kQ4_0> { static constexpr int q = 128, s = 0, d = 16; };
+template <> struct ChunkBytes<kQ8_0> { static constexpr int q = 256, s = 0, d = 16; };
+
+// Start of one weight row in each plane (row-major planes, nb blocks per row).
+struct RowPtr {
+    const uint8_t* q;
+    const uint8_t* s;
+    const uint8_t* d;
+};
+
 template <int D>
-__device__ __forceinline__ void load_chunk(const Planes& p, int64_t row, int64_t c, int t,
-                                           uint32_t (&w)[Words<D>::n], uint32_t& dbits) {
+__device__ __forceinline__ RowPtr row_ptr(const Planes& p, int64_t row) {
+    const int64_t chunks = p.nb / (D == kQ4_K || D == kQ6_K ? 1 : 8);
+    RowPtr r;
+    r.q = p.q + row * chunks * ChunkBytes<D>::q;
+    r.s = p.s + row * chunks * ChunkBytes<D>::s;
+    r.d = p.d + row * chunks * ChunkBytes<D>::d;
+    return r;
+}
+
+template <int D>
+__device__ __forceinline__ void load_chunk(const RowPtr& rp, int c, int t, uint32_t (&w)[Words<D>::n],
+                                           uint32_t& dbits) {
+    const uint8_t* b = rp.q + c * ChunkBytes<D>::q;
     if (D == kQ4_K) {
-        const uint8_t* b = p.q + (row * p.nb + c) * 144;
         uint4 v0 = ldg_stream(b), v1 = ldg_stream(b + 16 + 32 * t), v2 = ldg_stream(b + 32 + 32 * t);
         CLQ_PUT4(w, 0, v0); CLQ_PUT4(w, 4, v1); CLQ_PUT4(w, 8, v2);
     } else if (D == kQ6_K) {
-        const int64_t blk = row * p.nb + c;
-        const uint8_t* b = p.q + blk * 192 + 48 * t;
-        uint4 v0 = ldg_stream(b), v1 = ldg_stream(b + 16), v2 = ldg_stream(b + 32), v3 = ldg_stream(p.s + blk * 16);
+        b += 48 * t;
+        uint4 v0 = ldg_stream(b), v1 = ldg_stream(b + 16), v2 = ldg_stream(b + 32), v3 = ldg_stream(rp.s + c * 16);
         CLQ_PUT4(w, 0, v0); CLQ_PUT4(w, 4, v1); CLQ_PUT4(w, 8, v2); CLQ_PUT4(w, 12, v3);
-        dbits = *reinterpret_cast<const unsigned short*>(p.d + 2 * blk);
+        dbits = *reinterpret_cast<const unsigned short*>(rp.d + 2 * c);
     } else if (D == kQ4_0) {
-        const uint8_t* b = p.q + row * p.nb * 16 + c * 128 + 32 * t;
-        uint4 v0 = ldg_stream(b), v1 = ldg_stream(b + 16), v2 = ldg_stream(p.d + 2 * (row * p.nb + 8 * c));
+        b += 32 * t;
+        uint4 v0 = ldg_stream(b), v1 = ldg_stream(b + 16), v2 = ldg_stream(rp.d + 16 * c);
         CLQ_PUT4(w, 0, v0); CLQ_PUT4(w, 4, v1); CLQ_PUT4(w, 8, v2);
     } else {
-        const uint8_t* b = p.q + row * p.nb * 32 + c * 256 + 64 * t;
+        b += 64 * t;
         uint4 v0 = ldg_stream(b), v1 = ldg_stream(b + 16), v2 = ldg_stream(b + 32), v3 = ldg_stream(b + 48),
-              v4 = ldg_stream(p.d + 2 * (row * p.nb + 8 * c));
+              v4 = ldg_stream(rp.d + 16 * c);
         CLQ_PUT4(w, 0, v0); CLQ_PUT4(w, 4, v1); CLQ_PUT4(w, 8, v2); CLQ_PUT4(w, 12, v3); CLQ_PUT4(w, 16, v4);
     }
 }
@@ -141,6 +166,28 @@ template <typename XT> __device__ __forceinline__ float xload(const XT* p);
 template <> __device__ __forceinline__ float xload<float>(const float* p) { return *p; }
 template <> __device__ __forceinline__ float xload<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
 template <> __device__ __forceinline__ float xload<__half>(const __half* p) { return __half2float(*p); }
+
+// Eight consecutive activations from a 16-byte aligned address.
+__device__ __forceinline__ void xload8(const float* p, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ float2 to_float2(__half2 h) { return __half22float2(h); }
+__device__ __forceinline__ float2 to_float2(__nv_bfloat162 h) { return __bfloat1622float2(h); }
+template <typename H2>
+__device__ __forceinline__ void xload8_h(const void* p, float (&v)[8]) {
+    const uint4 a = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        H2 h = *reinterpret_cast<const H2*>(&w[i]);
+        float2 f = to_float2(h);
+        v[2 * i] = f.x;
+        v[2 * i + 1] = f.y;
+    }
+}
+__device__ __forceinline__ void xload8(const __half* p, float (&v)[8]) { xload8_h<__half2>(p, v); }
+__device__ __forceinline__ void xload8(const __nv_bfloat16* p, float (&v)[8]) { xload8_h<__nv_bfloat162>(p, v); }
 
 // hi + lo split of two scaled fp32 values into f16x2 words.
 __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t& lo) {
@@ -155,24 +202,32 @@ struct Params {
     int64_t rows, k, m, ldo;
     const void* x;
     float* out;
-    int xtype;
-    int part_chunks;  // chunks of x staged per pass
+    int x_aligned;      // x and its rows start on 16-byte boundaries
+    int part_chunks;    // chunks of x staged per pass (all of K when it fits)
+    int tiles_per_cta;  // 16-row tiles each CTA owns
 };
 
 // Stage chunks [c0, c0 + pc) of activation rows [tok0, tok0 + ntok) into
 // shared memory: fragments xf, unscale factors us, and (Q4_K) scaled sub-block
 // sums sxf for the min term.
+// Layout (token-major, PC = part_chunks): xf[(tok*PC + cc)*64 + s*4 + t],
+// sxf[(tok*PC + cc)*4 + t], us[tok*PC + cc].
 template <int D, typename XT, int WARPS>
 __device__ void stage_x(const Params& P, int64_t c0, int pc, int64_t tok0, int ntok, uint4* xf,
                         float* us, uint2* sxf) {
+    const int PC = P.part_chunks;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const XT* x = reinterpret_cast<const XT*>(P.x);
     for (int u = warp; u < pc * ntok; u += WARPS) {
         const int cc = u / ntok, tok = u % ntok;
         const XT* src = x + (tok0 + tok) * P.k + (c0 + cc) * 256 + 8 * lane;
         float v[8];
+        if (P.x_aligned) {
+            xload8(src, v);
+        } else {
 #pragma unroll
-        for (int i = 0; i < 8; i++) v[i] = xload(src + i);
+            for (int i = 0; i < 8; i++) v[i] = xload(src + i);
+        }
         float amax = 0.f;
 #pragma unroll
         for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
@@ -194,7 +249,7 @@ __device__ void stage_x(const Params& P, int64_t c0, int pc, int64_t tok0, int n
             uint4 f;
             split2(v[4 * qq], v[4 * qq + 1], f.x, f.z);
             split2(v[4 * qq + 2], v[4 * qq + 3], f.y, f.w);
-            xf[((cc * 16 + s) * 4 + t) * ntok + tok] = f;
+            xf[(tok * PC + cc) * 64 + s * 4 + t] = f;
         }
         if (D == kQ4_K) {
             float sum = 0.f;
@@ -207,294 +262,379 @@ __device__ void stage_x(const Params& P, int64_t c0, int pc, int64_t tok0, int n
             if ((lane & 7) == 0) {
                 uint2 f;
                 split2(sum, other, f.x, f.y);
-                sxf[(cc * 4 + (lane >> 3)) * ntok + tok] = f;
+                sxf[(tok * PC + cc) * 4 + (lane >> 3)] = f;
             }
         }
-        if (lane == 0) us[cc * ntok + tok] = __uint_as_float((uint32_t)(127 - sexp) << 23);
+        if (lane == 0) us[tok * PC + cc] = __uint_as_float((uint32_t)(127 - sexp) << 23);
     }
 }
 
-template <int D, typename XT, int MT, int R, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32) gemv_mma_kernel(Params P) {
+// One 16-row tile x one 256-column chunk: acc[n][i] += this chunk's products.
+// w[h]: the rows g (h = 0) and g + 8 (h = 1) words of load_chunk; cc: the
+// chunk's index among the staged ones.
+// MMA columns carry (token, part): column 2u + p of n-tile n is token 4n + u,
+// activation part p (0 = hi, 1 = lo), so one MMA yields both partial sums and
+// lane t's accumulators c[2h], c[2h+1] are token 4n + t's hi and lo sums for
+// row g + 8h.
+// xq[n]: the (hi or lo) fragment pair of this lane's column for the chunk,
+// indexed by step * 8 uint2 (token clamped to a staged one; padding columns are
+// computed and discarded); sq[n]: its Q4_K sub-block sums; ut[n]: unscale of
+// token 4n + t.  acc[n][h]: row g + 8h, token 4n + t.
+template <int D, int MT>
+__device__ __forceinline__ void compute_chunk(const uint32_t (&w)[2][Words<D>::n], const uint32_t (&db)[2],
+                                              int t, const uint2* const (&xq)[MT],
+                                              const uint32_t* const (&sq)[MT], const float (&ut)[MT],
+                                              float (&acc)[MT][2]) {
+    if constexpr (D == kQ4_K) {
+        uint32_t SCL[2], NL[2], SCH[2], NH[2], MN[2];
+        float dd[2], dm[2];
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const uint32_t* W = w[h];
+            const int sh = 16 * (t & 1);
+            const uint32_t A = (W[1] >> sh) & 0xFFFF, Bw = (W[2] >> sh) & 0xFFFF, Cw = (W[3] >> sh) & 0xFFFF;
+            const uint32_t sc = t < 2 ? (A & 0x3F3F) : ((Cw & 0x0F0F) | ((A >> 2) & 0x3030));
+            const uint32_t mn = t < 2 ? (Bw & 0x3F3F) : (((Cw >> 4) & 0x0F0F) | ((Bw >> 2) & 0x3030));
+            const uint32_t scp = hsub2(prmt(sc, kMagic, kSelLo), kH1024);  // (sc_lo, sc_hi)
+            SCL[h] = prmt(scp, scp, 0x1010);
+            SCH[h] = prmt(scp, scp, 0x3232);
+            NL[h] = hmul2(SCL[h], kHNeg1024);
+            NH[h] = hmul2(SCH[h], kHNeg64);
+            SCH[h] = hmul2(SCH[h], kHSixteenth);
+            MN[h] = hsub2(prmt(mn, kMagic, kSelLo), kH1024);
+            dd[h] = lo_half(W[0]);
+            dm[h] = hi_half(W[0]);
+        }
+        // two independent accumulator chains (low / high code nibbles)
+        float c2[2][MT][4], cm[MT][4];
+#pragma unroll
+        for (int n = 0; n < MT; n++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) c2[0][n][i] = c2[1][n][i] = cm[n][i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            uint32_t lo01[2], lo23[2], hi01[2], hi23[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t Wd = w[h][4 + j];
+                const uint32_t p01 = prmt(Wd, kMagic, kSelLo), p23 = prmt(Wd, kMagic, kSelHi);
+                lo01[h] = hfma2(p01 & kLoNib, SCL[h], NL[h]);
+                lo23[h] = hfma2(p23 & kLoNib, SCL[h], NL[h]);
+                hi01[h] = hfma2(p01 & kHiNib, SCH[h], NH[h]);
+                hi23[h] = hfma2(p23 & kHiNib, SCH[h], NH[h]);
+            }
+#pragma unroll
+            for (int n = 0; n < MT; n++) {
+                const uint2 b0 = xq[n][(2 * j) * 8], b1 = xq[n][(2 * j + 1) * 8];
+                mma16816(c2[0][n], lo01[0], lo01[1], lo23[0], lo23[1], b0.x, b0.y);
+                mma16816(c2[1][n], hi01[0], hi01[1], hi23[0], hi23[1], b1.x, b1.y);
+            }
+        }
+#pragma unroll
+        for (int n = 0; n < MT; n++) {
+            mma16816(cm[n], MN[0], MN[1], 0u, 0u, *sq[n], 0u);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const float csb = (c2[0][n][2 * h] + c2[1][n][2 * h]) + (c2[0][n][2 * h + 1] + c2[1][n][2 * h + 1]);
+                const float cmn = cm[n][2 * h] + cm[n][2 * h + 1];
+                const float v = fmaf(-64.f * dm[h], cmn, dd[h] * csb);
+                acc[n][h] = fmaf(ut[n], v, acc[n][h]);
+            }
+        }
+    } else {
+        // Q6_K: scale per 16-element step; Q4_0 / Q8_0: scale per 32-element block (2 steps).
+        constexpr int SPG = D == kQ6_K ? 4 : 2;
+        float cacc[MT][2];
+#pragma unroll
+        for (int n = 0; n < MT; n++) cacc[n][0] = cacc[n][1] = 0.f;
+#pragma unroll
+        for (int grpi = 0; grpi < (D == kQ6_K ? 4 : 8); grpi++) {
+            // grpi: Q6_K (h,half) word triple -> 4 steps; Q4_0/Q8_0 block -> 2 steps
+            uint32_t a01[SPG][2], a23[SPG][2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const uint32_t* W = w[h];
+                if constexpr (D == kQ6_K) {
+                    const uint32_t W0 = W[3 * grpi], W1 = W[3 * grpi + 1], QH = W[3 * grpi + 2];
+                    const uint32_t p0a = prmt(W0, kMagic, kSelLo), p0b = prmt(W0, kMagic, kSelHi);
+                    const uint32_t p1a = prmt(W1, kMagic, kSelLo), p1b = prmt(W1, kMagic, kSelHi);
+                    const uint32_t qa = prmt(QH, 0u, kSelLo), qb = prmt(QH, 0u, kSelHi);
+                    const uint32_t qa4 = qa << 4, qa2 = qa << 2, qb4 = qb << 4, qb2 = qb << 2;
+                    a01[0][h] = hsub2((p0a & kLoNib) | (qa4 & 0x00300030u), kH1056);
+                    a23[0][h] = hsub2((p0b & kLoNib) | (qb4 & 0x00300030u), kH1056);
+                    a01[1][h] = hsub2((p1a & kLoNib) | (qa2 & 0x00300030u), kH1056);
+                    a23[1][h] = hsub2((p1b & kLoNib) | (qb2 & 0x00300030u), kH1056);
+                    a01[2][h] = hfma2((p0a & kHiNib) | (qa4 & 0x03000300u), kHSixteenth, kHNeg96);
+                    a23[2][h] = hfma2((p0b & kHiNib) | (qb4 & 0x03000300u), kHSixteenth, kHNeg96);
+                    a01[3][h] = hfma2((p1a & kHiNib) | (qa2 & 0x03000300u), kHSixteenth, kHNeg96);
+                    a23[3][h] = hfma2((p1b & kHiNib) | (qb2 & 0x03000300u), kHSixteenth, kHNeg96);
+                } else if constexpr (D == kQ4_0) {
+                    const uint32_t Wd = W[grpi];
+                    const uint32_t pa = prmt(Wd, kMagic, kSelLo), pb = prmt(Wd, kMagic, kSelHi);
+                    a01[0][h] = hsub2(pa & kLoNib, kH1032);
+                    a23[0][h] = hsub2(pb & kLoNib, kH1032);
+                    a01[1][h] = hfma2(pa & kHiNib, kHSixteenth, kHNeg72);
+                    a23[1][h] = hfma2(pb & kHiNib, kHSixteenth, kHNeg72);
+                } else {  // Q8_0
+#pragma unroll
+                    for (int hf = 0; hf < 2; hf++) {
+                        const uint32_t Wd = W[2 * grpi + hf] ^ 0x80808080u;
+                        a01[hf][h] = hsub2(prmt(Wd, kMagic, kSelLo), kH1152);
+                        a23[hf][h] = hsub2(prmt(Wd, kMagic, kSelHi), kH1152);
+                    }
+                }
+            }
+            float f[SPG][2];  // per-step (Q6_K) or per-block scale of rows g, g+8
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                if constexpr (D == kQ6_K) {
+                    const uint32_t* S = &w[h][12];
+#pragma unroll
+                    for (int grp = 0; grp < 4; grp++) {
+                        // sub-scale index 8h + 2grp + half with (h, half) = grpi
+                        const int idx = 8 * (grpi >> 1) + 2 * grp + (grpi & 1);
+                        f[grp][h] = (float)(int)(int8_t)(S[idx >> 2] >> (8 * (idx & 3)));
+                    }
+                } else {
+                    const uint32_t dw = w[h][(D == kQ4_0 ? 8 : 16) + (grpi >> 1)];
+                    f[0][h] = (grpi & 1) ? hi_half(dw) : lo_half(dw);
+                }
+            }
+#pragma unroll
+            for (int n = 0; n < MT; n++) {
+                float cs[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int st = 0; st < SPG; st++) {
+                    const uint2 b = xq[n][(SPG * grpi + st) * 8];
+                    if constexpr (D == kQ6_K) {
+                        float c1[4] = {0.f, 0.f, 0.f, 0.f};
+                        mma16816(c1, a01[st][0], a01[st][1], a23[st][0], a23[st][1], b.x, b.y);
+#pragma unroll
+                        for (int h = 0; h < 2; h++) cacc[n][h] = fmaf(f[st][h], c1[2 * h] + c1[2 * h + 1], cacc[n][h]);
+                    } else {
+                        mma16816(cs, a01[st][0], a01[st][1], a23[st][0], a23[st][1], b.x, b.y);
+                    }
+                }
+                if constexpr (D != kQ6_K) {
+#pragma unroll
+                    for (int h = 0; h < 2; h++) cacc[n][h] = fmaf(f[0][h], cs[2 * h] + cs[2 * h + 1], cacc[n][h]);
+                }
+            }
+        }
+        float dsb[2] = {1.f, 1.f};
+        if constexpr (D == kQ6_K) {
+            dsb[0] = __half2float(__ushort_as_half((unsigned short)db[0]));
+            dsb[1] = __half2float(__ushort_as_half((unsigned short)db[1]));
+        }
+#pragma unroll
+        for (int n = 0; n < MT; n++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) acc[n][h] = fmaf(ut[n] * dsb[h], cacc[n][h], acc[n][h]);
+    }
+}
+
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+
+// Each CTA owns tiles_per_cta consecutive 16-row tiles for one slice of up to
+// 8*MT activation rows.  The activations are staged once per pass over K; each
+// warp then streams a flat list of (tile, chunk) units -- its chunks are
+// warp, warp + WARPS, ... -- with the next unit's weights loaded while the
+// current one is computed.  Per-(warp, tile) partial sums stay in shared
+// memory and one barrier at the end precedes the cross-warp sum.
+// Launched with programmatic dependent launch: weight loads do not depend on
+// the previous kernel, so only the activation staging waits for it.
+template <int D, typename XT, int MT, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma_kernel(Params P) {
     extern __shared__ __align__(16) unsigned char smem[];
     constexpr int NW = Words<D>::n;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int64_t tile0 = (int64_t)blockIdx.x * R;
-    const int64_t tok0 = (int64_t)blockIdx.y * 8 * MT;
-    const int ntok = (int)((P.m - tok0) < 8 * MT ? (P.m - tok0) : 8 * MT);
+    const int TL = P.tiles_per_cta;
+    const int64_t tiles = (P.rows + 15) / 16;
+    const int64_t tile0 = (int64_t)blockIdx.x * TL;
+    const int tlc = (int)((tiles - tile0) < TL ? (tiles - tile0) : TL);
+    const int64_t tok0 = (int64_t)blockIdx.y * 4 * MT;
+    const int ntok = (int)((P.m - tok0) < 4 * MT ? (P.m - tok0) : 4 * MT);
     const int64_t nchunks = P.k / 256;
-    const int pc_max = P.part_chunks;
+    const int PC = P.part_chunks;
 
     uint4* xf = reinterpret_cast<uint4*>(smem);
-    uint2* sxf = reinterpret_cast<uint2*>(xf + (size_t)pc_max * 64 * ntok);
-    float* us = reinterpret_cast<float*>(sxf + (D == kQ4_K ? (size_t)pc_max * 4 * ntok : 0));
+    uint2* sxf = reinterpret_cast<uint2*>(xf + (size_t)PC * 64 * ntok);
+    float* us = reinterpret_cast<float*>(sxf + (D == kQ4_K ? (size_t)PC * 4 * ntok : 0));
+    float* part = us + (size_t)PC * ntok;  // [WARPS][TL][ntok][16]
 
-    float acc[R][MT][4];
+    // Per n-tile: the staged token of this lane's B column (4n + g/2, clamped)
+    // and the token of its accumulators (4n + t, clamped); padding is dropped.
+    int xtok[MT], utok[MT];
 #pragma unroll
-    for (int r = 0; r < R; r++)
-#pragma unroll
-        for (int n = 0; n < MT; n++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) acc[r][n][i] = 0.f;
-
-    int64_t rowA[R], rowB[R];
-#pragma unroll
-    for (int r = 0; r < R; r++) {
-        int64_t base = (tile0 + r) * 16 + g;
-        rowA[r] = base < P.rows ? base : P.rows - 1;
-        rowB[r] = base + 8 < P.rows ? base + 8 : P.rows - 1;
+    for (int n = 0; n < MT; n++) {
+        xtok[n] = min(4 * n + (g >> 1), ntok - 1);
+        utok[n] = min(4 * n + t, ntok - 1);
     }
+    const int part_sel = g & 1;  // 0: hi fragment pair, 1: lo
 
-    for (int64_t c0 = 0; c0 < nchunks; c0 += pc_max) {
-        const int pc = (int)((nchunks - c0) < pc_max ? (nchunks - c0) : pc_max);
-        __syncthreads();  // previous pass finished reading the staged activations
+    allow_dependents();
+
+    for (int64_t c0 = 0; c0 < nchunks; c0 += PC) {
+        const int pc = (int)((nchunks - c0) < PC ? (nchunks - c0) : PC);
+        const int my_chunks = warp < pc ? (pc - warp + WARPS - 1) / WARPS : 0;
+        const int nunits = tlc * my_chunks;
+
+        // unit (tl, ci): tile tile0 + tl, chunk c0 + warp + ci * WARPS
+        int ltl = -1;
+        RowPtr rpa, rpb;
+        auto load_unit = [&](int tl, int ci, uint32_t (&w)[2][NW], uint32_t (&db)[2]) {
+            if (tl != ltl) {  // warp-uniform: rows of a new tile
+                ltl = tl;
+                const int64_t base = (tile0 + tl) * 16 + g;
+                rpa = row_ptr<D>(P.p, base < P.rows ? base : P.rows - 1);
+                rpb = row_ptr<D>(P.p, base + 8 < P.rows ? base + 8 : P.rows - 1);
+            }
+            const int c = (int)c0 + warp + ci * WARPS;
+            load_chunk<D>(rpa, c, t, w[0], db[0]);
+            load_chunk<D>(rpb, c, t, w[1], db[1]);
+        };
+        uint32_t bufA[2][NW], bufB[2][NW], dbA[2] = {0, 0}, dbB[2] = {0, 0};
+        if (nunits > 0) load_unit(0, 0, bufA, dbA);  // independent of the previous kernel
+        if (c0 > 0) __syncthreads();                 // everyone finished with the previous pass
+        else grid_dependency_wait();                 // activations may come from the previous kernel
         stage_x<D, XT, WARPS>(P, c0, pc, tok0, ntok, xf, us, sxf);
         __syncthreads();
 
-        for (int cc = warp; cc < pc; cc += WARPS) {
-            const int64_t c = c0 + cc;
-            uint32_t w[R][2][NW];
-            uint32_t db[R][2];
+        float acc[MT][2];
 #pragma unroll
-            for (int r = 0; r < R; r++) {
-                load_chunk<D>(P.p, rowA[r], c, t, w[r][0], db[r][0]);
-                load_chunk<D>(P.p, rowB[r], c, t, w[r][1], db[r][1]);
-            }
-            float ut[MT][2];  // unscale of tokens 2t, 2t+1 of each n-tile
-#pragma unroll
-            for (int n = 0; n < MT; n++)
-#pragma unroll
-                for (int j = 0; j < 2; j++) {
-                    int tok = 8 * n + 2 * t + j;
-                    ut[n][j] = tok < ntok ? us[cc * ntok + tok] : 0.f;
-                }
+        for (int n = 0; n < MT; n++) acc[n][0] = acc[n][1] = 0.f;
 
-            if constexpr (D == kQ4_K) {
+        int tl = 0, ci = 0;  // current unit
+        auto run_unit = [&](const uint32_t (&w)[2][NW], const uint32_t (&db)[2]) {
+            const int cc = warp + ci * WARPS;
+            const uint2* xq[MT];
+            const uint32_t* sq[MT];
+            float ut[MT];
 #pragma unroll
-                for (int r = 0; r < R; r++) {
-                    uint32_t SCL[2], NL[2], SCH[2], NH[2], MN[2];
-                    float dd[2], dm[2];
+            for (int n = 0; n < MT; n++) {
+                xq[n] = reinterpret_cast<const uint2*>(xf + (xtok[n] * PC + cc) * 64 + t) + part_sel;
+                sq[n] = reinterpret_cast<const uint32_t*>(sxf + (xtok[n] * PC + cc) * 4 + t) + part_sel;
+                ut[n] = us[utok[n] * PC + cc];
+            }
+            compute_chunk<D, MT>(w, db, t, xq, sq, ut, acc);
+            if (++ci == my_chunks) {
+#pragma unroll
+                for (int n = 0; n < MT; n++)
 #pragma unroll
                     for (int h = 0; h < 2; h++) {
-                        const uint32_t* W = w[r][h];
-                        const int sh = 16 * (t & 1);
-                        const uint32_t A = (W[1] >> sh) & 0xFFFF, Bw = (W[2] >> sh) & 0xFFFF,
-                                       Cw = (W[3] >> sh) & 0xFFFF;
-                        const uint32_t sc = t < 2 ? (A & 0x3F3F) : ((Cw & 0x0F0F) | ((A >> 2) & 0x3030));
-                        const uint32_t mn = t < 2 ? (Bw & 0x3F3F) : (((Cw >> 4) & 0x0F0F) | ((Bw >> 2) & 0x3030));
-                        SCL[h] = hsub2(prmt(sc, kMagic, 0x4040), kH1024);
-                        SCH[h] = hsub2(prmt(sc, kMagic, 0x4141), kH1024);
-                        NL[h] = hmul2(SCL[h], kHNeg1024);
-                        NH[h] = hmul2(SCH[h], kHNeg64);
-                        SCH[h] = hmul2(SCH[h], kHSixteenth);
-                        MN[h] = hsub2(prmt(mn, kMagic, kSelLo), kH1024);
-                        dd[h] = lo_half(W[0]);
-                        dm[h] = hi_half(W[0]);
+                        const int tok = 4 * n + t;
+                        if (tok < ntok) {
+                            float* dst = &part[((warp * TL + tl) * ntok + tok) * 16 + g + 8 * h];
+                            *dst = c0 == 0 ? acc[n][h] : *dst + acc[n][h];
+                        }
+                        acc[n][h] = 0.f;
                     }
-                    float csb[MT][4], cmn[MT][4];
-#pragma unroll
-                    for (int n = 0; n < MT; n++)
-#pragma unroll
-                        for (int i = 0; i < 4; i++) csb[n][i] = cmn[n][i] = 0.f;
-#pragma unroll
-                    for (int j = 0; j < 8; j++) {
-                        uint32_t lo01[2], lo23[2], hi01[2], hi23[2];
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const uint32_t Wd = w[r][h][4 + j];
-                            const uint32_t p01 = prmt(Wd, kMagic, kSelLo), p23 = prmt(Wd, kMagic, kSelHi);
-                            lo01[h] = hfma2(p01 & kLoNib, SCL[h], NL[h]);
-                            lo23[h] = hfma2(p23 & kLoNib, SCL[h], NL[h]);
-                            hi01[h] = hfma2(p01 & kHiNib, SCH[h], NH[h]);
-                            hi23[h] = hfma2(p23 & kHiNib, SCH[h], NH[h]);
-                        }
-#pragma unroll
-                        for (int n = 0; n < MT; n++) {
-                            const int tok = 8 * n + g;
-                            const uint4 z = make_uint4(0, 0, 0, 0);
-                            const uint4 b0 = tok < ntok ? xf[((cc * 16 + 2 * j) * 4 + t) * ntok + tok] : z;
-                            const uint4 b1 = tok < ntok ? xf[((cc * 16 + 2 * j + 1) * 4 + t) * ntok + tok] : z;
-                            mma16816(csb[n], lo01[0], lo01[1], lo23[0], lo23[1], b0.x, b0.y);
-                            mma16816(csb[n], lo01[0], lo01[1], lo23[0], lo23[1], b0.z, b0.w);
-                            mma16816(csb[n], hi01[0], hi01[1], hi23[0], hi23[1], b1.x, b1.y);
-                            mma16816(csb[n], hi01[0], hi01[1], hi23[0], hi23[1], b1.z, b1.w);
-                        }
-                    }
-#pragma unroll
-                    for (int n = 0; n < MT; n++) {
-                        const int tok = 8 * n + g;
-                        const uint2 sx = tok < ntok ? sxf[(cc * 4 + t) * ntok + tok] : make_uint2(0, 0);
-                        mma16816(cmn[n], MN[0], MN[1], 0u, 0u, sx.x, 0u);
-                        mma16816(cmn[n], MN[0], MN[1], 0u, 0u, sx.y, 0u);
-#pragma unroll
-                        for (int i = 0; i < 4; i++) {
-                            const int h = i >> 1;
-                            const float v = fmaf(-64.f * dm[h], cmn[n][i], dd[h] * csb[n][i]);
-                            acc[r][n][i] = fmaf(ut[n][i & 1], v, acc[r][n][i]);
-                        }
-                    }
-                }
-            } else {
-                // Q6_K: scale per 16-element step; Q4_0 / Q8_0: scale per 32-element block (2 steps).
-#pragma unroll
-                for (int r = 0; r < R; r++) {
-                    float cacc[MT][4];
-#pragma unroll
-                    for (int n = 0; n < MT; n++)
-#pragma unroll
-                        for (int i = 0; i < 4; i++) cacc[n][i] = 0.f;
-#pragma unroll
-                    for (int grpi = 0; grpi < (D == kQ6_K ? 4 : 8); grpi++) {
-                        // grpi: Q6_K (h,half) word triple -> 4 steps; Q4_0/Q8_0 block -> 2 steps
-                        constexpr int SPG = D == kQ6_K ? 4 : 2;
-                        uint32_t a01[SPG][2], a23[SPG][2];
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            const uint32_t* W = w[r][h];
-                            if constexpr (D == kQ6_K) {
-                                const uint32_t W0 = W[3 * grpi], W1 = W[3 * grpi + 1], QH = W[3 * grpi + 2];
-                                const uint32_t p0a = prmt(W0, kMagic, kSelLo), p0b = prmt(W0, kMagic, kSelHi);
-                                const uint32_t p1a = prmt(W1, kMagic, kSelLo), p1b = prmt(W1, kMagic, kSelHi);
-                                const uint32_t qa = prmt(QH, 0u, kSelLo), qb = prmt(QH, 0u, kSelHi);
-                                const uint32_t qa4 = qa << 4, qa2 = qa << 2, qb4 = qb << 4, qb2 = qb << 2;
-                                a01[0][h] = hsub2((p0a & kLoNib) | (qa4 & 0x00300030u), kH1056);
-                                a23[0][h] = hsub2((p0b & kLoNib) | (qb4 & 0x00300030u), kH1056);
-                                a01[1][h] = hsub2((p1a & kLoNib) | (qa2 & 0x00300030u), kH1056);
-                                a23[1][h] = hsub2((p1b & kLoNib) | (qb2 & 0x00300030u), kH1056);
-                                a01[2][h] = hfma2((p0a & kHiNib) | (qa4 & 0x03000300u), kHSixteenth, kHNeg96);
-                                a23[2][h] = hfma2((p0b & kHiNib) | (qb4 & 0x03000300u), kHSixteenth, kHNeg96);
-                                a01[3][h] = hfma2((p1a & kHiNib) | (qa2 & 0x03000300u), kHSixteenth, kHNeg96);
-                                a23[3][h] = hfma2((p1b & kHiNib) | (qb2 & 0x03000300u), kHSixteenth, kHNeg96);
-                            } else if constexpr (D == kQ4_0) {
-                                const uint32_t Wd = W[grpi];
-                                const uint32_t pa = prmt(Wd, kMagic, kSelLo), pb = prmt(Wd, kMagic, kSelHi);
-                                a01[0][h] = hsub2(pa & kLoNib, kH1032);
-                                a23[0][h] = hsub2(pb & kLoNib, kH1032);
-                                a01[1][h] = hfma2(pa & kHiNib, kHSixteenth, kHNeg72);
-                                a23[1][h] = hfma2(pb & kHiNib, kHSixteenth, kHNeg72);
-                            } else {  // Q8_0
-#pragma unroll
-                                for (int hf = 0; hf < 2; hf++) {
-                                    const uint32_t Wd = W[2 * grpi + hf] ^ 0x80808080u;
-                                    a01[hf][h] = hsub2(prmt(Wd, kMagic, kSelLo), kH1152);
-                                    a23[hf][h] = hsub2(prmt(Wd, kMagic, kSelHi), kH1152);
-                                }
-                            }
-                        }
-                        float f[SPG][2];  // per-step (Q6_K) or per-block scale of rows g, g+8
-#pragma unroll
-                        for (int h = 0; h < 2; h++) {
-                            if constexpr (D == kQ6_K) {
-                                const uint32_t* S = &w[r][h][12];
-#pragma unroll
-                                for (int grp = 0; grp < 4; grp++) {
-                                    // sub-scale index 8h + 2grp + half with (h, half) = grpi
-                                    const int idx = 8 * (grpi >> 1) + 2 * grp + (grpi & 1);
-                                    f[grp][h] = (float)(int)(int8_t)(S[idx >> 2] >> (8 * (idx & 3)));
-                                }
-                            } else {
-                                const uint32_t dw = w[r][h][(D == kQ4_0 ? 8 : 16) + (grpi >> 1)];
-                                f[0][h] = (grpi & 1) ? hi_half(dw) : lo_half(dw);
-                            }
-                        }
-#pragma unroll
-                        for (int n = 0; n < MT; n++) {
-                            const int tok = 8 * n + g;
-                            float cs[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                            for (int st = 0; st < SPG; st++) {
-                                const int s = SPG * grpi + st;
-                                const uint4 b = tok < ntok ? xf[((cc * 16 + s) * 4 + t) * ntok + tok]
-                                                           : make_uint4(0, 0, 0, 0);
-                                if constexpr (D == kQ6_K) {
-#pragma unroll
-                                    for (int i = 0; i < 4; i++) cs[i] = 0.f;
-                                }
-                                mma16816(cs, a01[st][0], a01[st][1], a23[st][0], a23[st][1], b.x, b.y);
-                                mma16816(cs, a01[st][0], a01[st][1], a23[st][0], a23[st][1], b.z, b.w);
-                                if constexpr (D == kQ6_K) {
-#pragma unroll
-                                    for (int i = 0; i < 4; i++) cacc[n][i] = fmaf(f[st][i >> 1], cs[i], cacc[n][i]);
-                                }
-                            }
-                            if constexpr (D != kQ6_K) {
-#pragma unroll
-                                for (int i = 0; i < 4; i++) cacc[n][i] = fmaf(f[0][i >> 1], cs[i], cacc[n][i]);
-                            }
-                        }
-                    }
-                    float dsb[2] = {1.f, 1.f};
-                    if constexpr (D == kQ6_K) {
-                        dsb[0] = __half2float(__ushort_as_half((unsigned short)db[r][0]));
-                        dsb[1] = __half2float(__ushort_as_half((unsigned short)db[r][1]));
-                    }
-#pragma unroll
-                    for (int n = 0; n < MT; n++)
-#pragma unroll
-                        for (int i = 0; i < 4; i++)
-                            acc[r][n][i] = fmaf(ut[n][i & 1] * dsb[i >> 1], cacc[n][i], acc[r][n][i]);
-                }
+                ci = 0;
+                ++tl;
             }
+        };
+        // the unit after (tl, ci)
+        auto next_of = [&](int a_tl, int a_ci, int& n_tl, int& n_ci) {
+            n_ci = a_ci + 1;
+            n_tl = a_tl;
+            if (n_ci == my_chunks) { n_ci = 0; ++n_tl; }
+        };
+        for (int u = 0; u < nunits; u += 2) {
+            int t1, c1, t2, c2;
+            next_of(tl, ci, t1, c1);
+            if (u + 1 < nunits) load_unit(t1, c1, bufB, dbB);
+            run_unit(bufA, dbA);
+            if (u + 1 >= nunits) break;
+            next_of(t1, c1, t2, c2);
+            if (u + 2 < nunits) load_unit(t2, c2, bufA, dbA);
+            run_unit(bufB, dbB);
+        }
+        if (c0 == 0 && my_chunks == 0) {  // a warp without chunks contributes zeros
+            for (int i = lane; i < tlc * ntok * 16; i += 32) part[(warp * TL) * ntok * 16 + i] = 0.f;
         }
     }
 
-    // K-split reduction across warps through shared memory.
     __syncthreads();
-    float* red = reinterpret_cast<float*>(smem);
-#pragma unroll
-    for (int r = 0; r < R; r++)
-#pragma unroll
-        for (int n = 0; n < MT; n++)
-#pragma unroll
-            for (int i = 0; i < 4; i++) red[(((warp * R + r) * MT + n) * 4 + i) * 32 + lane] = acc[r][n][i];
-    __syncthreads();
-    for (int idx = threadIdx.x; idx < R * MT * 128; idx += WARPS * 32) {
+    for (int idx = threadIdx.x; idx < tlc * ntok * 16; idx += WARPS * 32) {
         float sum = 0.f;
 #pragma unroll 4
-        for (int wv = 0; wv < WARPS; wv++) sum += red[wv * R * MT * 128 + idx];
-        const int ln = idx & 31, i = (idx >> 5) & 3, n = (idx >> 7) % MT, r = idx / (MT * 128);
-        const int64_t row = (tile0 + r) * 16 + (ln >> 2) + 8 * (i >> 1);
-        const int64_t tok = tok0 + 8 * n + 2 * (ln & 3) + (i & 1);
-        if (row < P.rows && tok < P.m) P.out[tok * P.ldo + row] = sum;
+        for (int wv = 0; wv < WARPS; wv++) sum += part[wv * TL * ntok * 16 + idx];
+        const int r16 = idx & 15, tok = (idx >> 4) % ntok, tl = idx / (16 * ntok);
+        const int64_t row = (tile0 + tl) * 16 + r16;
+        if (row < P.rows) P.out[(tok0 + tok) * P.ldo + row] = sum;
     }
 }
 
-template <int D, typename XT, int MT, int R, int WARPS>
+int sm_count() {
+    static int count = 0;
+    if (!count) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0)
+            count = 148;
+    }
+    return count;
+}
+
+template <int D, typename XT, int MT, int WARPS>
 cudaError_t launch_one(const Params& P, cudaStream_t stream) {
     const int64_t tiles = (P.rows + 15) / 16;
-    const int ntok_max = (int)(P.m < 8 * MT ? P.m : 8 * MT);
+    const int ntok_max = (int)(P.m < 4 * MT ? P.m : 4 * MT);
     const size_t per_chunk = (size_t)ntok_max * (1024 + (D == kQ4_K ? 32 : 0) + 4);
-    const size_t red = (size_t)WARPS * R * MT * 128 * sizeof(float);
     const int64_t nchunks = P.k / 256;
     Params q = P;
-    const size_t budget = 96 * 1024;
-    int64_t pc = (int64_t)(budget / per_chunk);
+    int64_t pc = (int64_t)((64 * 1024) / per_chunk);
     if (pc < 1) pc = 1;
     if (pc > nchunks) pc = nchunks;
+    // 16 resident warps per SM; partial sums at most 32 KB
+    const int64_t slots = (16 / WARPS) * (int64_t)sm_count();
+    int64_t tl = (tiles + slots - 1) / slots;
+    const int64_t tl_cap = (32 * 1024) / ((int64_t)WARPS * ntok_max * 16 * 4);
+    if (tl > tl_cap) tl = tl_cap;
+    if (tl < 1) tl = 1;
     q.part_chunks = (int)pc;
-    size_t smem = pc * per_chunk;
-    if (smem < red) smem = red;
-    auto kern = gemv_mma_kernel<D, XT, MT, R, WARPS>;
+    q.tiles_per_cta = (int)tl;
+    const size_t smem = pc * per_chunk + (size_t)WARPS * tl * ntok_max * 16 * 4;
+    auto kern = gemv_mma_kernel<D, XT, MT, WARPS>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    dim3 grid((unsigned)((tiles + R - 1) / R), (unsigned)((P.m + 8 * MT - 1) / (8 * MT)));
+    dim3 grid((unsigned)((tiles + tl - 1) / tl), (unsigned)((P.m + 4 * MT - 1) / (4 * MT)));
     if (grid.y > 65535) return cudaErrorInvalidConfiguration;
-    kern<<<grid, WARPS * 32, smem, stream>>>(q);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(WARPS * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kern, q);
+}
+
+int gemv_warps() {
+    static int w = -1;
+    if (w < 0) {
+        const char* e = getenv("CLQ_GEMV_WARPS");  // tuning knob: 4 or 8 warps per CTA
+        w = (e && atoi(e) == 4) ? 4 : 8;
+    }
+    return w;
 }
 
 template <int D, typename XT>
 cudaError_t launch_shape(const Params& P, cudaStream_t s) {
-    const int64_t tiles = (P.rows + 15) / 16;
-    const int64_t nchunks = P.k / 256;
-    const bool two_tiles = tiles >= 4 * 148;
-    const bool many_warps = nchunks >= 16 && tiles < 8 * 148;
-    if (P.m <= 8) {
-        if (two_tiles) return many_warps ? launch_one<D, XT, 1, 2, 16>(P, s) : launch_one<D, XT, 1, 2, 8>(P, s);
-        return many_warps ? launch_one<D, XT, 1, 1, 16>(P, s) : launch_one<D, XT, 1, 1, 8>(P, s);
+    // MT n-tiles of 4 activation rows (each row uses a hi and a lo column)
+    if (gemv_warps() == 4) {
+        if (P.m <= 4) return launch_one<D, XT, 1, 4>(P, s);
+        if (P.m <= 8) return launch_one<D, XT, 2, 4>(P, s);
+        return launch_one<D, XT, 4, 4>(P, s);
     }
-    return many_warps ? launch_one<D, XT, 2, 1, 16>(P, s) : launch_one<D, XT, 2, 1, 8>(P, s);
+    if (P.m <= 4) return launch_one<D, XT, 1, 8>(P, s);
+    if (P.m <= 8) return launch_one<D, XT, 2, 8>(P, s);
+    return launch_one<D, XT, 4, 8>(P, s);
 }
 
 template <typename XT>
@@ -524,8 +664,10 @@ cudaError_t launch_gemv_mma(const WeightView& w, int64_t rows, const void* x, in
     P.ldo = ldo;
     P.x = x;
     P.out = out;
-    P.xtype = xtype;
     P.part_chunks = 1;
+    P.tiles_per_cta = 1;
+    const int esize = xtype == CLQ_X_F32 ? 4 : 2;
+    P.x_aligned = ((uintptr_t)x % 16 == 0) && ((w.k * esize) % 16 == 0);
     switch (xtype) {
     case CLQ_X_F32: return launch_dtype<float>(P, w.dtype, stream);
     case CLQ_X_BF16: return launch_dtype<__nv_bfloat16>(P, w.dtype, stream);
