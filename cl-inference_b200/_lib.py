@@ -45,6 +45,7 @@ SIGNATURES = {
     "clq_store_info": (_int, [_ptr, ctypes.POINTER(_int), ctypes.POINTER(_i64), ctypes.POINTER(_i64),
                               ctypes.POINTER(_size), ctypes.POINTER(_ptr), ctypes.POINTER(_int)]),
     "clq_linear_device": (_int, [_ptr, _i64, _i64, _ptr, _int, _i64, _ptr, _i64, _u32, _ptr]),
+    "clq_linear_group_device": (_int, [_ptr, _ptr, _ptr, _int, _ptr, _int, _i64, _ptr, _ptr, _u32, _ptr]),
     "clq_dequantize_device": (_int, [_ptr, _i64, _i64, _ptr, _int, _ptr]),
     "clq_gather_device": (_int, [_ptr, _ptr, _i64, _ptr, _ptr]),
     "clq_dequantize": (_int, [_int, _ptr, _size, _ptr]),

@@ -350,6 +350,44 @@ int clq_linear_device(const clq_store* w, int64_t row_begin, int64_t rows, const
     return CLQ_OK;
 }
 
+int clq_linear_group_device(const clq_store* const* w, const int64_t* row_begin, const int64_t* rows,
+                            int count, const void* x, int xtype, int64_t m, float* const* out,
+                            const int64_t* ldo, unsigned flags, void* stream) {
+    if (count < 1 || count > 4) return fail(CLQ_ERR_ARGUMENT, "group of %d weights (1..4 allowed)", count);
+    if (!w || !row_begin || !rows || !out || !ldo) return fail(CLQ_ERR_ARGUMENT, "null group array");
+    for (int i = 0; i < count; i++) {
+        if (!w[i]) return fail(CLQ_ERR_ARGUMENT, "null store %d in group", i);
+        if (w[i]->dtype != w[0]->dtype || w[i]->k != w[0]->k)
+            return fail(CLQ_ERR_SHAPE, "group members need one dtype and row length");
+    }
+    bool fused = m > 0 && w[0]->k > 0 && w[0]->k % 256 == 0 && !(flags & ~CLQ_MATH_FAST);
+    for (int i = 0; i < count && fused; i++)
+        fused = row_begin[i] >= 0 && rows[i] > 0 && row_begin[i] + rows[i] <= w[i]->n && ldo[i] >= rows[i] && out[i];
+    if (!fused) {  // validation and any shape the fused kernel does not cover, one call each
+        for (int i = 0; i < count; i++) {
+            int rc = clq_linear_device(w[i], row_begin[i], rows[i], x, xtype, m, out[i], ldo[i], flags, stream);
+            if (rc) return rc;
+        }
+        return CLQ_OK;
+    }
+    if (!x) return fail(CLQ_ERR_ARGUMENT, "null activations");
+    if (xtype != CLQ_X_F32 && xtype != CLQ_X_BF16 && xtype != CLQ_X_F16)
+        return fail(CLQ_ERR_ARGUMENT, "unknown activation type %d", xtype);
+    int device, rc;
+    if ((rc = current_device(&device))) return rc;
+    clq::WeightView views[4];
+    const clq::WeightView* vp[4];
+    for (int i = 0; i < count; i++) {
+        if (w[i]->device != device)
+            return fail(CLQ_ERR_ARGUMENT, "store lives on device %d, current device is %d", w[i]->device, device);
+        views[i] = view_of(w[i], row_begin[i]);
+        vp[i] = &views[i];
+    }
+    cudaError_t e = clq::launch_gemv_mma_group(vp, rows, count, x, xtype, m, out, ldo, (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "grouped linear kernel launch");
+    return CLQ_OK;
+}
+
 int clq_dequantize_device(const clq_store* w, int64_t row_begin, int64_t rows, float* out,
                           int transposed, void* stream) {
     if (!w) return fail(CLQ_ERR_ARGUMENT, "null store");

@@ -47,6 +47,10 @@ cudaError_t launch_linear(const WeightView& w, int64_t rows, const void* x, int 
 bool gemv_mma_supported(const WeightView& w, int64_t m);
 cudaError_t launch_gemv_mma(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
                             float* out, int64_t ldo, cudaStream_t stream);
+// Up to 4 weights of one dtype and K sharing x, in one launch.
+cudaError_t launch_gemv_mma_group(const WeightView* const* w, const int64_t* rows, int count, const void* x,
+                                  int xtype, int64_t m, float* const* out, const int64_t* ldo,
+                                  cudaStream_t stream);
 
 // The generic (any alignment, any M) kernel, also used as a fallback by launch_linear.
 cudaError_t launch_linear_generic(const WeightView& w, int64_t rows, const void* x, int xtype,

@@ -197,15 +197,36 @@ __device__ __forceinline__ void split2(float a, float b, uint32_t& hi, uint32_t&
     lo = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
 }
 
-struct Params {
+// Up to kGroup weights of one dtype and K that share the activations run as
+// one launch; their 16-row tiles are numbered consecutively.
+constexpr int kGroup = 4;
+
+struct Member {
     Planes p;
-    int64_t rows, k, m, ldo;
-    const void* x;
+    int64_t rows;
     float* out;
+    int64_t ldo;
+    int64_t tile_begin;  // first global tile of this member
+};
+
+struct Params {
+    Member mem[kGroup];
+    int nmem;
+    int64_t tiles;      // total tiles over the members
+    int64_t k, m;
+    const void* x;
     int x_aligned;      // x and its rows start on 16-byte boundaries
     int part_chunks;    // chunks of x staged per pass (all of K when it fits)
     int tiles_per_cta;  // 16-row tiles each CTA owns
 };
+
+__device__ __forceinline__ int member_of(const Params& P, int64_t tile) {
+    int i = 0;
+#pragma unroll
+    for (int j = 1; j < kGroup; j++)
+        if (j < P.nmem && tile >= P.mem[j].tile_begin) i = j;
+    return i;
+}
 
 // Stage chunks [c0, c0 + pc) of activation rows [tok0, tok0 + ntok) into
 // shared memory: fragments xf, unscale factors us, and (Q4_K) scaled sub-block
@@ -451,7 +472,7 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma_kernel(Params
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
     const int TL = P.tiles_per_cta;
-    const int64_t tiles = (P.rows + 15) / 16;
+    const int64_t tiles = P.tiles;
     const int64_t tile0 = (int64_t)blockIdx.x * TL;
     const int tlc = (int)((tiles - tile0) < TL ? (tiles - tile0) : TL);
     const int64_t tok0 = (int64_t)blockIdx.y * 4 * MT;
@@ -488,8 +509,11 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma_kernel(Params
             if (tl != ltl) {  // warp-uniform: rows of a new tile
                 ltl = tl;
                 const int64_t base = (tile0 + tl) * 16 + g;
-                rpa = row_ptr<D>(P.p, base < P.rows ? base : P.rows - 1);
-                rpb = row_ptr<D>(P.p, base + 8 < P.rows ? base + 8 : P.rows - 1);
+                const int mi = member_of(P, tile0 + tl);
+                const Member& M = P.mem[mi];
+                const int64_t lr = base - M.tile_begin * 16;
+                rpa = row_ptr<D>(M.p, lr < M.rows ? lr : M.rows - 1);
+                rpb = row_ptr<D>(M.p, lr + 8 < M.rows ? lr + 8 : M.rows - 1);
             }
             const int c = (int)c0 + warp + ci * WARPS;
             load_chunk<D>(rpa, c, t, w[0], db[0]);
@@ -562,9 +586,22 @@ __global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma_kernel(Params
 #pragma unroll 4
         for (int wv = 0; wv < WARPS; wv++) sum += part[wv * TL * ntok * 16 + idx];
         const int r16 = idx & 15, tok = (idx >> 4) % ntok, tl = idx / (16 * ntok);
-        const int64_t row = (tile0 + tl) * 16 + r16;
-        if (row < P.rows) P.out[(tok0 + tok) * P.ldo + row] = sum;
+        const int mi = member_of(P, tile0 + tl);
+        const Member& M = P.mem[mi];
+        const int64_t row = (tile0 + tl - M.tile_begin) * 16 + r16;
+        if (row < M.rows) M.out[(tok0 + tok) * M.ldo + row] = sum;
     }
+}
+
+// Programmatic dependent launch (on unless CLQ_PDL=0): the next kernel in the
+// stream may start its weight prefetch while this one drains.
+bool pdl_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("CLQ_PDL");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
 }
 
 int sm_count() {
@@ -580,7 +617,7 @@ int sm_count() {
 
 template <int D, typename XT, int MT, int WARPS>
 cudaError_t launch_one(const Params& P, cudaStream_t stream) {
-    const int64_t tiles = (P.rows + 15) / 16;
+    const int64_t tiles = P.tiles;
     const int ntok_max = (int)(P.m < 4 * MT ? P.m : 4 * MT);
     const size_t per_chunk = (size_t)ntok_max * (1024 + (D == kQ4_K ? 32 : 0) + 4);
     const int64_t nchunks = P.k / 256;
@@ -611,7 +648,7 @@ cudaError_t launch_one(const Params& P, cudaStream_t stream) {
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = pdl_enabled() ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, kern, q);
 }
 
@@ -654,26 +691,42 @@ bool gemv_mma_supported(const WeightView& w, int64_t m) {
     return w.k > 0 && w.k % 256 == 0 && m > 0;
 }
 
-cudaError_t launch_gemv_mma(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
-                            float* out, int64_t ldo, cudaStream_t stream) {
-    Params P;
-    P.p = Planes{w.q, w.s, w.d, w.nb};
-    P.rows = rows;
-    P.k = w.k;
+cudaError_t launch_gemv_mma_group(const WeightView* const* w, const int64_t* rows, int count, const void* x,
+                                  int xtype, int64_t m, float* const* out, const int64_t* ldo,
+                                  cudaStream_t stream) {
+    if (count < 1 || count > kGroup) return cudaErrorInvalidValue;
+    Params P = {};
+    P.nmem = count;
+    int64_t tiles = 0;
+    for (int i = 0; i < count; i++) {
+        if (w[i]->dtype != w[0]->dtype || w[i]->k != w[0]->k) return cudaErrorInvalidValue;
+        P.mem[i].p = Planes{w[i]->q, w[i]->s, w[i]->d, w[i]->nb};
+        P.mem[i].rows = rows[i];
+        P.mem[i].out = out[i];
+        P.mem[i].ldo = ldo[i];
+        P.mem[i].tile_begin = tiles;
+        tiles += (rows[i] + 15) / 16;
+    }
+    P.tiles = tiles;
+    P.k = w[0]->k;
     P.m = m;
-    P.ldo = ldo;
     P.x = x;
-    P.out = out;
     P.part_chunks = 1;
     P.tiles_per_cta = 1;
     const int esize = xtype == CLQ_X_F32 ? 4 : 2;
-    P.x_aligned = ((uintptr_t)x % 16 == 0) && ((w.k * esize) % 16 == 0);
+    P.x_aligned = ((uintptr_t)x % 16 == 0) && ((P.k * esize) % 16 == 0);
     switch (xtype) {
-    case CLQ_X_F32: return launch_dtype<float>(P, w.dtype, stream);
-    case CLQ_X_BF16: return launch_dtype<__nv_bfloat16>(P, w.dtype, stream);
-    case CLQ_X_F16: return launch_dtype<__half>(P, w.dtype, stream);
+    case CLQ_X_F32: return launch_dtype<float>(P, w[0]->dtype, stream);
+    case CLQ_X_BF16: return launch_dtype<__nv_bfloat16>(P, w[0]->dtype, stream);
+    case CLQ_X_F16: return launch_dtype<__half>(P, w[0]->dtype, stream);
     default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_gemv_mma(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
+                            float* out, int64_t ldo, cudaStream_t stream) {
+    const WeightView* wp = &w;
+    return launch_gemv_mma_group(&wp, &rows, 1, x, xtype, m, &out, &ldo, stream);
 }
 
 }  // namespace clq

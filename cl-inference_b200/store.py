@@ -107,3 +107,25 @@ class Store:
         _lib.check(_lib.lib.clq_gather_device(self.handle, ids.data_ptr(), ids.numel(), out.data_ptr(),
                                               current_stream_handle()))
         return out
+
+
+def linear_group(stores, x, outs=None, flags=0, stream=None):
+    """One launch for up to 4 stores of one dtype and K that read the same x
+    (clq_linear_group_device); returns the list of [m, rows] outputs."""
+    torch = _torch()
+    n = len(stores)
+    if not 1 <= n <= 4:
+        raise ValueError("a group holds 1 to 4 stores")
+    x = x.contiguous()
+    m = x.shape[0]
+    if outs is None:
+        outs = [torch.empty((m, s.n), dtype=torch.float32, device=x.device) for s in stores]
+    handles = (ctypes.c_void_p * n)(*[s.handle.value for s in stores])
+    begins = (ctypes.c_int64 * n)(*([0] * n))
+    rows = (ctypes.c_int64 * n)(*[o.shape[1] for o in outs])
+    optrs = (ctypes.c_void_p * n)(*[o.data_ptr() for o in outs])
+    ldos = (ctypes.c_int64 * n)(*[o.stride(0) if o.dim() == 2 else o.shape[-1] for o in outs])
+    xtype = _XTYPE.get(str(x.dtype).replace("torch.", ""))
+    _lib.check(_lib.lib.clq_linear_group_device(handles, begins, rows, n, x.data_ptr(), xtype, m, optrs, ldos,
+                                                flags, stream if stream is not None else current_stream_handle()))
+    return outs

@@ -124,6 +124,14 @@ int clq_linear_device(const clq_store *w, int64_t row_begin, int64_t rows, const
                       int xtype, int64_t m, float *out, int64_t ldo, unsigned flags,
                       void *stream);
 
+/* Up to 4 weights of one dtype and K that read the same activations X (the
+ * q/k/v projections of attention, local/blocks.lisp:334-336, or the gate/up
+ * pair of the SwiGLU MLP, :151-154) in one launch: member i computes
+ * out[i][r, j] for rows [row_begin[i], row_begin[i] + rows[i]) of w[i]. */
+int clq_linear_group_device(const clq_store *const *w, const int64_t *row_begin, const int64_t *rows,
+                            int count, const void *x, int xtype, int64_t m, float *const *out,
+                            const int64_t *ldo, unsigned flags, void *stream);
+
 /* ---- dequantize and gather ------------------------------------------------
  * Bit-exact fp32 values of packed-element (quant/packed.lisp:85-108) and the
  * Q8_0 dequantize-executor (quant/q8-0.lisp:98-123).
@@ -133,8 +141,9 @@ int clq_linear_device(const clq_store *w, int64_t row_begin, int64_t rows, const
 int clq_dequantize_device(const clq_store *w, int64_t row_begin, int64_t rows, float *out,
                           int transposed, void *stream);
 /* ct:take + dequantize of local/blocks.lisp:136-138: OUT[i, :] = row IDS[i]
- * (device int32 ids, duplicates allowed; an id outside [0, N) is an error
- * reported through *bad_id_flag-free status after the call completes). */
+ * (device int32 ids, duplicates allowed).  An id outside [0, N) cannot be
+ * reported by this asynchronous call: its output row is filled with quiet
+ * NaNs.  clq_take checks the ids on the host and returns an error instead. */
 int clq_gather_device(const clq_store *w, const int32_t *ids, int64_t count, float *out,
                       void *stream);
 /* Host-pointer forms (synchronous; the bytes are uploaded for the call only). */

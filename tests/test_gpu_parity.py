@@ -240,3 +240,24 @@ def test_activation_magnitudes_across_fp32_range(cuda, clq, synth, oracle, dtype
     assert np.all(np.isfinite(got))
     assert np.all(np.abs(got - ref) <= 1e-5 * mag + 1e-37)
     store.close()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_grouped_launch_equals_separate_launches(cuda, clq, synth, oracle, dtype):
+    """clq_linear_group_device: q/k/v-style members sharing x give the same bits
+    as one launch per member, and match the oracle."""
+    torch = cuda
+    k = 1024
+    shapes = [512, 136, 136]
+    datas = [synth.packed_blocks(dtype, n, k, seed=300 + i) for i, n in enumerate(shapes)]
+    stores = [clq.Store(dtype, n, k, d) for n, d in zip(shapes, datas)]
+    for m in (1, 3, 6):
+        x = torch.from_numpy(synth.activations(m, k, seed=310 + m)).cuda()
+        grouped = clq.linear_group(stores, x)
+        for s, g, d, n in zip(stores, grouped, datas, shapes):
+            single = s.linear(x)
+            assert torch.equal(single, g)
+            ref, mag = oracle.matmul_f64(dtype, x.cpu().numpy(), d, n)
+            assert element_bound_ok(g.cpu().numpy(), ref, mag)
+    for s in stores:
+        s.close()
