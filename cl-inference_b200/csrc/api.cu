@@ -360,7 +360,8 @@ int clq_linear_group_device(const clq_store* const* w, const int64_t* row_begin,
         if (w[i]->dtype != w[0]->dtype || w[i]->k != w[0]->k)
             return fail(CLQ_ERR_SHAPE, "group members need one dtype and row length");
     }
-    bool fused = m > 0 && w[0]->k > 0 && w[0]->k % 256 == 0 && !(flags & ~CLQ_MATH_FAST);
+    bool fused = m > 0 && w[0]->k > 0 && w[0]->k % 256 == 0 && !(flags & ~CLQ_MATH_FAST) &&
+                 !clq::uses_gemm_tc(view_of(w[0], 0), xtype, m, flags);
     for (int i = 0; i < count && fused; i++)
         fused = row_begin[i] >= 0 && rows[i] > 0 && row_begin[i] + rows[i] <= w[i]->n && ldo[i] >= rows[i] && out[i];
     if (!fused) {  // validation and any shape the fused kernel does not cover, one call each

@@ -52,6 +52,26 @@ cudaError_t launch_gemv_mma_group(const WeightView* const* w, const int64_t* row
                                   int xtype, int64_t m, float* const* out, const int64_t* ldo,
                                   cudaStream_t stream);
 
+// Tensor-core (tcgen05) prefill GEMM: tiling and scratch layout for one call.
+struct GemmPlan {
+    int tn;                // tokens per tile
+    int64_t token_tiles, row_tiles;
+    int splits;            // K splits (partials reduced in a second kernel)
+    int kb_per_split;      // 64-wide K blocks per split
+    size_t xs_bytes, us_bytes, part_bytes;
+    size_t smem;           // dynamic shared memory per CTA
+};
+GemmPlan plan_gemm_tc(int64_t rows, int64_t k, int64_t m);
+size_t gemm_tc_scratch_bytes(const GemmPlan& g);
+bool gemm_tc_supported(const WeightView& w, int64_t m);
+// SCRATCH: gemm_tc_scratch_bytes(g) device bytes, 256-byte aligned, private to
+// this call until it completes on STREAM.
+cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m, float* out,
+                           int64_t ldo, uint8_t* scratch, const GemmPlan& g, cudaStream_t stream);
+
+// Whether launch_linear takes the tensor-core GEMM for this request.
+bool uses_gemm_tc(const WeightView& w, int xtype, int64_t m, unsigned flags);
+
 // The generic (any alignment, any M) kernel, also used as a fallback by launch_linear.
 cudaError_t launch_linear_generic(const WeightView& w, int64_t rows, const void* x, int xtype,
                                   int64_t m, float* out, int64_t ldo, cudaStream_t stream);

@@ -1,0 +1,528 @@
+// gemm_tc.cu -- prefill GEMM for packed weights on the 5th-generation tensor
+// cores: tcgen05.mma (kind::f16, fp32 accumulator in tensor memory).
+//
+// out[t, r] = sum_k x[t, k] * W[r, k] for many activation rows t (prompt
+// tokens).  One CTA computes a 128-row weight tile x TN-token tile over a range
+// of K (split-K when the output has too few tiles for the machine):
+//   prep kernel  x -> fp16 scaled by a per-token power of two, written to
+//                scratch pre-swizzled (SWIZZLE_128B image of every 64-wide
+//                K block), so a plain 1-D bulk copy lands a ready MMA operand;
+//   warps 0-3    dequantize the weight tile (fp32 math, one rounding to fp16)
+//                straight into the swizzled A stage; later the epilogue;
+//   warp 4       bulk-copies the activation stage (B), mbarrier tx-count;
+//   warp 5       one thread issues the MMAs and commits stages back.
+// The MMA operands are fp16 (weights rounded once; activations rounded once
+// after the power-of-two scaling), products accumulate in fp32.
+// Every mbarrier wait is bounded; on expiry the CTA records an error code,
+// stops issuing, drains what it issued and frees its tensor memory.
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "../../include/clq.h"
+#include "clq_internal.h"
+#include "layout.cuh"
+
+namespace clq {
+namespace {
+
+constexpr int kTM = 128;          // weight rows per CTA (the MMA's M)
+constexpr int kKB = 64;           // K elements per stage (one 128-byte swizzle span of fp16)
+constexpr int kStages = 4;
+constexpr int kThreads = 192;     // warps 0-3 dequant/epilogue, 4 copy, 5 MMA
+constexpr uint32_t kWaitLimit = 1u << 26;  // polls before a wait gives up
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for the phase with PARITY; false (and *err set) when it gives up.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err) {
+    for (uint32_t i = 0; i < kWaitLimit; i++) {
+        if (mbar_test(bar, parity)) return true;
+        if (*(volatile int*)err) return false;
+        if (i > 64) __nanosleep(32);
+    }
+    atomicExch(err, 1);
+    return false;
+}
+// Bounded wait that ignores the error flag: used before teardown so that copies
+// and MMAs this CTA issued have finished before it exits.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < (1u << 22); i++) {
+        if (mbar_test(bar, parity)) return;
+        if (i > 64) __nanosleep(64);
+    }
+}
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+__device__ __forceinline__ void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor: K-major, SWIZZLE_128B, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+    return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+           ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor: fp16 A and B (K-major), fp32 D, M = 128, N = n.
+__host__ __device__ constexpr uint32_t instr_desc(int n) {
+    return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
+}
+__device__ __forceinline__ void mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u), "r"(0u), "r"(0u), "r"(0u)
+        : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                     smem_u32(bar))
+                 : "memory");
+}
+
+// Byte offset of 16-byte chunk C of row R in a SWIZZLE_128B K-major tile.
+__host__ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+__device__ __forceinline__ float nibf(uint32_t v) {  // small non-negative integer -> float, exact
+    return __uint_as_float(0x4B000000u | v) - 8388608.f;
+}
+
+// ---- activation prep ------------------------------------------------------
+
+// One CTA per activation row: power-of-two scale putting max|x| in [2^14, 2^15),
+// then the fp16 values in the swizzled tile image:
+//   xs[((tt * KBt + kb) * TN + r) * 128 + swz]   (row t = tt * TN + r)
+// and us[t] = 1 / scale.  Rows t in [m, m_pad) are written as zeros.
+template <typename XT>
+__global__ void prep_x_kernel(const XT* __restrict__ x, int64_t m, int64_t k, int tn, uint8_t* __restrict__ xs,
+                              float* __restrict__ us) {
+    const int64_t t = blockIdx.x;
+    const int64_t tt = t / tn, r = t % tn;
+    const int64_t kbt = k / kKB;
+    __shared__ float red[32];
+    float amax = 0.f;
+    if (t < m)
+        for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+            float v;
+            if constexpr (sizeof(XT) == 4) v = (float)x[t * k + i];
+            else if constexpr (std::is_same<XT, __half>::value) v = __half2float(x[t * k + i]);
+            else v = __bfloat162float(x[t * k + i]);
+            amax = fmaxf(amax, fabsf(v));
+        }
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+        for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    amax = red[0];
+    int sexp = 0;
+    if (amax > 0.f) {
+        int e = (int)((__float_as_uint(amax) >> 23) & 255) - 127;
+        sexp = 14 - e;
+        sexp = sexp < -120 ? -120 : (sexp > 120 ? 120 : sexp);
+    }
+    const float scale = __uint_as_float((uint32_t)(127 + sexp) << 23);
+    if (threadIdx.x == 0) us[t] = __uint_as_float((uint32_t)(127 - sexp) << 23);
+    // 16-byte chunks of 8 elements
+    for (int64_t cidx = threadIdx.x; cidx < k / 8; cidx += blockDim.x) {
+        const int64_t kb = cidx / 8;
+        const int c = (int)(cidx % 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (t < m) {
+            float f[8];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int64_t i = cidx * 8 + j;
+                if constexpr (sizeof(XT) == 4) f[j] = (float)x[t * k + i];
+                else if constexpr (std::is_same<XT, __half>::value) f[j] = __half2float(x[t * k + i]);
+                else f[j] = __bfloat162float(x[t * k + i]);
+                f[j] *= scale;
+            }
+            v.x = pack_half2(f[0], f[1]);
+            v.y = pack_half2(f[2], f[3]);
+            v.z = pack_half2(f[4], f[5]);
+            v.w = pack_half2(f[6], f[7]);
+        }
+        *reinterpret_cast<uint4*>(xs + (tt * kbt + kb) * tn * 128 + swz((uint32_t)r, (uint32_t)c)) = v;
+    }
+}
+
+// ---- weight dequantization into the swizzled A stage -----------------------
+
+// Row `row` (local 0..127 of the tile, clamped global row `grow`), K block kb:
+// 64 fp16 values written as 8 swizzled 16-byte chunks at a + swz(row, c).
+template <int D>
+__device__ __forceinline__ void dequant_row(const Planes& p, int64_t grow, int64_t kb, uint32_t row, uint8_t* a) {
+    uint32_t h[32];  // 64 halves
+    if constexpr (D == kQ4_K) {
+        const int64_t c = kb >> 2;
+        const int qt = (int)(kb & 3);
+        const uint8_t* b = p.q + (grow * p.nb + c) * 144;
+        const uint4 hd = *reinterpret_cast<const uint4*>(b);
+        const uint4 c0 = *reinterpret_cast<const uint4*>(b + 16 + 32 * qt);
+        const uint4 c1 = *reinterpret_cast<const uint4*>(b + 32 + 32 * qt);
+        const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFF)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+        // scale byte i of the 12 (quant/packed.lisp:91-98)
+        const uint32_t sw[3] = {hd.y, hd.z, hd.w};
+        auto sbyte = [&](int i) -> int { return (int)((sw[i >> 2] >> (8 * (i & 3))) & 0xFF); };
+        float ds[2], dm[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int g = 2 * qt + u;
+            int sc, mn;
+            if (g < 4) {
+                sc = sbyte(g) & 63;
+                mn = sbyte(g + 4) & 63;
+            } else {
+                sc = (sbyte(g + 4) & 15) | ((sbyte(g - 4) & 192) >> 2);
+                mn = (sbyte(g + 4) >> 4) | ((sbyte(g) & 192) >> 2);
+            }
+            ds[u] = d * (float)sc;
+            dm[u] = dmin * (float)mn;
+        }
+        const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+        for (int wi = 0; wi < 8; wi++) {
+#pragma unroll
+            for (int bp = 0; bp < 2; bp++) {  // bytes 2bp, 2bp+1 of the word
+                const uint32_t b0 = (wv[wi] >> (16 * bp)) & 0xFF, b1 = (wv[wi] >> (16 * bp + 8)) & 0xFF;
+                const int l = 4 * wi + 2 * bp;  // element index in the sub-block
+                h[l / 2] = pack_half2(fmaf(ds[0], nibf(b0 & 15), -dm[0]), fmaf(ds[0], nibf(b1 & 15), -dm[0]));
+                h[16 + l / 2] = pack_half2(fmaf(ds[1], nibf(b0 >> 4), -dm[1]), fmaf(ds[1], nibf(b1 >> 4), -dm[1]));
+            }
+        }
+    } else if constexpr (D == kQ6_K) {
+        const int64_t blk = grow * p.nb + (kb >> 2);
+        const int qt = (int)(kb & 3);
+        const int hh = qt >> 1, odd = qt & 1;  // 128-element half, group pair {2odd, 2odd+1}
+        const uint8_t* q = p.q + blk * 192;
+        const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(p.d + 2 * blk)));
+        const uint4 sv = *reinterpret_cast<const uint4*>(p.s + blk * 16);
+        auto sc = [&](int i) -> int {  // int8 sub-scale i (runtime index: select, no local array)
+            const int wsel = i >> 2;
+            const uint32_t w = wsel == 0 ? sv.x : wsel == 1 ? sv.y : wsel == 2 ? sv.z : sv.w;
+            return (int)(int8_t)((w >> (8 * (i & 3))) & 0xFF);
+        };
+#pragma unroll
+        for (int u = 0; u < 2; u++) {  // group grp = 2odd + u, elements 32u .. 32u+31 of the block
+            const int grp = 2 * odd + u;
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const float fs = d * (float)sc(8 * hh + 2 * grp + half);
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const uint8_t* base = q + t * 48 + (2 * hh + half) * 12;
+                    const uint32_t ql = *reinterpret_cast<const uint32_t*>(base + 4 * (grp & 1));
+                    const uint32_t qh = *reinterpret_cast<const uint32_t*>(base + 8);
+                    float v[4];
+#pragma unroll
+                    for (int bw = 0; bw < 4; bw++) {
+                        const uint32_t lo = (ql >> (8 * bw + 4 * (grp >> 1))) & 15;
+                        const uint32_t hi = (qh >> (8 * bw + 2 * grp)) & 3;
+                        v[bw] = fs * (nibf(lo | (hi << 4)) - 32.f);
+                    }
+                    const int l = 16 * half + 4 * t;  // element in the group
+                    h[16 * u + l / 2] = pack_half2(v[0], v[1]);
+                    h[16 * u + l / 2 + 1] = pack_half2(v[2], v[3]);
+                }
+            }
+        }
+    } else {
+        // Q4_0 / Q8_0: two 32-element blocks, element by element
+#pragma unroll
+        for (int i = 0; i < 32; i++)
+            h[i] = pack_half2(element_planar<D>(p, grow, kb * kKB + 2 * i), element_planar<D>(p, grow, kb * kKB + 2 * i + 1));
+    }
+#pragma unroll
+    for (int c = 0; c < 8; c++)
+        *reinterpret_cast<uint4*>(a + swz(row, c)) = make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+}
+
+struct GemmParams {
+    Planes p;
+    int64_t rows, k, m;
+    const uint8_t* xs;  // swizzled fp16 activations
+    const float* us;    // per-token unscale
+    float* out;         // final output (splits == 1) or partials [split][m][rows]
+    int64_t ldo;
+    int tn;             // tokens per tile (power of two, 32..256)
+    int kb_per_split;
+    int* err;
+};
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzle atoms
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int tn = P.tn;
+    uint8_t* A = smem;                                   // kStages x 16 KB
+    uint8_t* B = A + kStages * kTM * 128;                // kStages x tn * 128
+    uint64_t* full_a = reinterpret_cast<uint64_t*>(B + (size_t)kStages * tn * 128);
+    uint64_t* full_b = full_a + kStages;
+    uint64_t* empty = full_b + kStages;
+    uint64_t* done = empty + kStages;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t tt = blockIdx.x;                 // token tile
+    const int64_t row0 = (int64_t)blockIdx.y * kTM;
+    const int split = blockIdx.z;
+    const int64_t kbt = P.k / kKB;
+    const int64_t kb0 = (int64_t)split * P.kb_per_split;
+    const int64_t kb1 = (kb0 + P.kb_per_split) < kbt ? (kb0 + P.kb_per_split) : kbt;
+    const int nk = (int)(kb1 - kb0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full_a[s], 4);
+            mbar_init(&full_b[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {  // tensor memory: tn fp32 columns x 128 lanes
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(tn)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    int* err = P.err;
+
+    if (warp < 4) {
+        // ---- weight tiles ----
+        const uint32_t row = (uint32_t)threadIdx.x;  // 0..127
+        const int64_t grow_u = row0 + row;
+        const int64_t grow = grow_u < P.rows ? grow_u : P.rows - 1;
+        for (int it = 0; it < nk; it++) {
+            const int s = it % kStages;
+            if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, err)) break;
+            dequant_row<D>(P.p, grow, kb0 + it, row, A + s * kTM * 128);
+            fence_async_shared();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full_a[s]);
+        }
+        // ---- epilogue: tensor memory -> out ----
+        const bool ok = mbar_wait(done, 0, err);
+        tc_fence_after();
+        if (ok) {
+            const int64_t r = row0 + 32 * warp + lane;
+            const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16);
+            for (int c0 = 0; c0 < tn; c0 += 32) {
+                uint32_t v[32];
+                asm volatile(
+                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+                      "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
+                      "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
+                      "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
+                      "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+                    : "r"(taddr + (uint32_t)c0));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (r < P.rows) {
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        const int64_t t = tt * tn + c0 + j;
+                        if (t < P.m) {
+                            const float val = __uint_as_float(v[j]) * P.us[t];
+                            if (gridDim.z == 1) P.out[t * P.ldo + r] = val;
+                            else P.out[((int64_t)split * P.m + t) * P.rows + r] = val;
+                        }
+                    }
+                }
+            }
+        }
+    } else if (warp == 4) {
+        // ---- activation tiles: one bulk copy per stage ----
+        if (lane == 0) {
+            const uint32_t bytes = (uint32_t)tn * 128;
+            for (int it = 0; it < nk; it++) {
+                const int s = it % kStages;
+                if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, err)) break;
+                mbar_arrive_tx(&full_b[s], bytes);
+                bulk_copy(B + (size_t)s * tn * 128, P.xs + ((tt * kbt + kb0 + it) * tn) * 128, bytes, &full_b[s]);
+            }
+        }
+    } else {
+        // ---- MMA issue ----
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(tn);
+            int it = 0;
+            for (; it < nk; it++) {
+                const int s = it % kStages;
+                const uint32_t ph = (it / kStages) & 1;
+                if (!mbar_wait(&full_a[s], ph, err) || !mbar_wait(&full_b[s], ph, err)) break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(A + s * kTM * 128), b_addr = smem_u32(B + (size_t)s * tn * 128);
+#pragma unroll
+                for (int j = 0; j < kKB / 16; j++)
+                    mma_f16(tmem, smem_desc(a_addr + 32 * j), smem_desc(b_addr + 32 * j), idesc, (it > 0 || j > 0) ? 1u : 0u);
+                mma_commit(&empty[s]);
+            }
+            mma_commit(done);  // arrives once every MMA issued above has completed
+            mbar_drain(done, 0);
+        }
+    }
+    // Bulk copies in flight must land before the CTA exits.
+    if (warp == 4 && lane == 0) {
+        for (int it = nk - kStages < 0 ? 0 : nk - kStages; it < nk; it++)
+            mbar_drain(&full_b[it % kStages], (it / kStages) & 1);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tn) : "memory");
+    }
+}
+
+// out[t * ldo + r] = sum over splits of part[split][t][r], fixed order.
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t m, int64_t rows,
+                                     float* __restrict__ out, int64_t ldo) {
+    const int64_t total = m * rows;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        float s = 0.f;
+        for (int j = 0; j < splits; j++) s += part[j * total + i];
+        const int64_t t = i / rows, r = i % rows;
+        out[t * ldo + r] = s;
+    }
+}
+
+int sm_count_gemm() {
+    static int count = 0;
+    if (!count) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0)
+            count = 148;
+    }
+    return count;
+}
+
+}  // namespace
+
+GemmPlan plan_gemm_tc(int64_t rows, int64_t k, int64_t m) {
+    GemmPlan g;
+    int tn = 32;
+    while (tn < 256 && tn < m) tn *= 2;
+    g.tn = tn;
+    g.token_tiles = (m + tn - 1) / tn;
+    g.row_tiles = (rows + kTM - 1) / kTM;
+    const int64_t kbt = k / kKB;
+    const int64_t ctas = g.token_tiles * g.row_tiles;
+    int64_t splits = 1;
+    const int64_t want = sm_count_gemm();
+    while (ctas * splits < want && kbt / (splits * 2) >= 4) splits *= 2;
+    while (splits > 1 && kbt % splits) splits /= 2;  // every split gets the same, non-zero K range
+    g.splits = (int)splits;
+    g.kb_per_split = (int)((kbt + splits - 1) / splits);
+    g.xs_bytes = (size_t)g.token_tiles * tn * k * 2;
+    g.us_bytes = (size_t)g.token_tiles * tn * sizeof(float);
+    g.part_bytes = splits > 1 ? (size_t)splits * m * rows * sizeof(float) : 0;
+    g.smem = 1024 + (size_t)kStages * (kTM * 128 + tn * 128) + 256;
+    return g;
+}
+
+size_t gemm_tc_scratch_bytes(const GemmPlan& g) {
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    return al(sizeof(int)) + al(g.xs_bytes) + al(g.us_bytes) + al(g.part_bytes);
+}
+
+bool gemm_tc_supported(const WeightView& w, int64_t m) { return w.k > 0 && w.k % 256 == 0 && m > 0; }
+
+cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m, float* out,
+                           int64_t ldo, uint8_t* scratch, const GemmPlan& g, cudaStream_t stream) {
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    int* err = reinterpret_cast<int*>(scratch);
+    uint8_t* xs = scratch + al(sizeof(int));
+    float* us = reinterpret_cast<float*>(xs + al(g.xs_bytes));
+    float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(us) + al(g.us_bytes));
+    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), stream);
+    if (e != cudaSuccess) return e;
+    const unsigned prep_grid = (unsigned)(g.token_tiles * g.tn);
+    switch (xtype) {
+    case CLQ_X_F32: prep_x_kernel<float><<<prep_grid, 256, 0, stream>>>((const float*)x, m, w.k, g.tn, xs, us); break;
+    case CLQ_X_BF16:
+        prep_x_kernel<__nv_bfloat16><<<prep_grid, 256, 0, stream>>>((const __nv_bfloat16*)x, m, w.k, g.tn, xs, us);
+        break;
+    case CLQ_X_F16: prep_x_kernel<__half><<<prep_grid, 256, 0, stream>>>((const __half*)x, m, w.k, g.tn, xs, us); break;
+    default: return cudaErrorInvalidValue;
+    }
+    if ((e = cudaGetLastError()) != cudaSuccess) return e;
+    GemmParams P;
+    P.p = Planes{w.q, w.s, w.d, w.nb};
+    P.rows = rows;
+    P.k = w.k;
+    P.m = m;
+    P.xs = xs;
+    P.us = us;
+    P.out = g.splits > 1 ? part : out;
+    P.ldo = ldo;
+    P.tn = g.tn;
+    P.kb_per_split = g.kb_per_split;
+    P.err = err;
+    dim3 grid((unsigned)g.token_tiles, (unsigned)g.row_tiles, (unsigned)g.splits);
+    auto launch = [&](auto kern) -> cudaError_t {
+        cudaError_t r = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)g.smem);
+        if (r != cudaSuccess) return r;
+        kern<<<grid, kThreads, g.smem, stream>>>(P);
+        return cudaGetLastError();
+    };
+    switch (w.dtype) {
+    case kQ4_K: e = launch(gemm_tc_kernel<kQ4_K>); break;
+    case kQ6_K: e = launch(gemm_tc_kernel<kQ6_K>); break;
+    case kQ4_0: e = launch(gemm_tc_kernel<kQ4_0>); break;
+    case kQ8_0: e = launch(gemm_tc_kernel<kQ8_0>); break;
+    default: return cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess || g.splits == 1) return e;
+    const int64_t total = m * rows;
+    const int rb = (int)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
+    splitk_reduce_kernel<<<rb, 256, 0, stream>>>(part, g.splits, m, rows, out, ldo);
+    return cudaGetLastError();
+}
+
+}  // namespace clq

@@ -1,0 +1,96 @@
+"""The tensor-core prefill GEMM (tcgen05) against the fp64 oracle (needs a B200).
+
+Taken for many activation rows (prompt tokens) with 16-bit activations, or
+with CLQ_MATH_FAST for fp32 ones.  Its operands are fp16 (each dequantized
+weight and each power-of-two-scaled activation rounded once), so the gate is
+the linear-output tolerance -- max over rows of ||y - y64|| / ||y64|| <= 1e-3 --
+plus a per-element bound of 1e-3 * sum|x*w| for the two fp16 roundings.
+"""
+import numpy as np
+import pytest
+
+from helpers import NORM_REL, max_row_relative_error
+
+pytestmark = pytest.mark.gpu
+FAST = 1
+
+
+def check(out, ref, mag):
+    assert np.all(np.isfinite(out))
+    assert max_row_relative_error(out, ref) <= NORM_REL
+    assert np.all(np.abs(out.astype(np.float64) - ref) <= 1e-3 * mag + 1e-6)
+
+
+@pytest.mark.parametrize("dtype", ["q4_k", "q6_k", "q4_0", "q8_0"])
+@pytest.mark.parametrize("n,k,m", [(200, 512, 64), (128, 1024, 100), (384, 768, 300)])
+def test_gemm_small_shapes(cuda, clq, synth, oracle, dtype, n, k, m):
+    torch = cuda
+    data = synth.packed_blocks(dtype, n, k, seed=n + k + m)
+    x = torch.from_numpy(synth.activations(m, k, seed=m)).cuda().to(torch.bfloat16)
+    store = clq.Store(dtype, n, k, data)
+    out = store.linear(x).cpu().numpy()
+    ref, mag = oracle.matmul_f64(dtype, x.float().cpu().numpy(), data, n)
+    check(out, ref, mag)
+    store.close()
+
+
+@pytest.mark.parametrize("xtype", ["float16", "float32"])
+def test_gemm_activation_types(cuda, clq, synth, oracle, xtype):
+    torch = cuda
+    n, k, m = 256, 1024, 128
+    data = synth.packed_blocks("q4_k", n, k, seed=7)
+    x = torch.from_numpy(synth.activations(m, k, seed=8)).cuda().to(getattr(torch, xtype))
+    store = clq.Store("q4_k", n, k, data)
+    out = store.linear(x, flags=FAST).cpu().numpy()
+    ref, mag = oracle.matmul_f64("q4_k", x.float().cpu().numpy(), data, n)
+    check(out, ref, mag)
+    store.close()
+
+
+def test_gemm_extreme_activation_magnitudes(cuda, clq, synth, oracle):
+    """Per-token power-of-two scaling keeps tiny and huge rows in fp16 range."""
+    torch = cuda
+    n, k, m = 256, 1024, 64
+    data = synth.packed_blocks("q6_k", n, k, seed=9)
+    x = synth.activations(m, k, seed=10)
+    x[0] *= np.float32(1e-20)
+    x[1] *= np.float32(1e20)
+    x[2] = 0.0
+    store = clq.Store("q6_k", n, k, data)
+    out = store.linear(torch.from_numpy(x).cuda(), flags=FAST).cpu().numpy().astype(np.float64)
+    ref, mag = oracle.matmul_f64("q6_k", x, data, n)
+    assert np.all(np.isfinite(out))
+    assert np.all(np.abs(out - ref) <= 1e-3 * mag + 1e-30)
+    store.close()
+
+
+@pytest.mark.parametrize("dtype,n,k,m", [
+    ("q4_k", 4096, 4096, 512),    # Llama-3-8B q/o projection, 512-token prompt
+    ("q4_k", 14336, 4096, 128),   # gate/up, 128-token prompt
+    ("q6_k", 4096, 14336, 256),   # down projection (Q6_K in Q4_K_M)
+])
+def test_gemm_prefill_shapes(cuda, clq, synth, oracle, dtype, n, k, m):
+    torch = cuda
+    data = synth.packed_blocks(dtype, n, k, seed=4000 + n)
+    x = torch.from_numpy(synth.activations(m, k, seed=4100 + m)).cuda().to(torch.bfloat16)
+    store = clq.Store(dtype, n, k, data)
+    out = store.linear(x).cpu().numpy()
+    rows = 384  # fp64 check on a slice of weight rows at the start, middle and end
+    rb = k // clq.DTYPES[dtype].block_size * clq.DTYPES[dtype].block_bytes
+    xf = x.float().cpu().numpy()
+    for start in (0, n // 2, n - rows):
+        ref, mag = oracle.matmul_f64(dtype, xf, data[start * rb:(start + rows) * rb], rows)
+        check(out[:, start:start + rows], ref, mag)
+    store.close()
+
+
+def test_gemm_repeats_bit_identically(cuda, clq, synth):
+    torch = cuda
+    n, k, m = 512, 2048, 200
+    data = synth.packed_blocks("q4_k", n, k, seed=11)
+    x = torch.from_numpy(synth.activations(m, k, seed=12)).cuda().to(torch.bfloat16)
+    store = clq.Store("q4_k", n, k, data)
+    a = store.linear(x)
+    b = store.linear(x)
+    assert torch.equal(a, b)
+    store.close()
