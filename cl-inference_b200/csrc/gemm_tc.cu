@@ -28,7 +28,7 @@ namespace {
 constexpr int kTM = 128;          // weight rows per CTA (the MMA's M)
 constexpr int kKB = 64;           // K elements per stage (one 128-byte swizzle span of fp16)
 constexpr int kStages = 4;
-constexpr int kThreads = 192;     // warps 0-3 dequant/epilogue, 4 copy, 5 MMA
+constexpr int kThreads = 320;     // warps 0-7 dequant/epilogue, 8 copy, 9 MMA
 constexpr uint32_t kWaitLimit = 1u << 26;  // polls before a wait gives up
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -184,95 +184,182 @@ __global__ void prep_x_kernel(const XT* __restrict__ x, int64_t m, int64_t k, in
 }
 
 // ---- weight dequantization into the swizzled A stage -----------------------
+//
+// Two threads per weight row of the tile, each converting half of a 64-wide K
+// block (32 values, 4 swizzled 16-byte chunks).  load_raw fetches the
+// quantized bytes into registers one stage ahead; convert_raw decodes them
+// with exact fp16 integer tricks (code bits ORed into the mantissa of 1024.0,
+// one fused multiply-add to remove the bias and apply a sub-scale) and rounds
+// each weight to fp16 at most twice.
 
-// Row `row` (local 0..127 of the tile, clamped global row `grow`), K block kb:
-// 64 fp16 values written as 8 swizzled 16-byte chunks at a + swz(row, c).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+    return r;
+}
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t d;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t hmul2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t dup_half(float v) {  // (fp16(v), fp16(v))
+    const uint32_t h = __half_as_ushort(__float2half_rn(v));
+    return h | (h << 16);
+}
+constexpr uint32_t kMagic = 0x64646464u;
+constexpr uint32_t kH1024 = 0x64006400u;
+constexpr uint32_t kH1056 = 0x64206420u;  // 1024 + 32
+constexpr uint32_t kHSixteenth = 0x2C002C00u;
+constexpr uint32_t kHNeg96 = 0xD600D600u;
+constexpr uint32_t kHNeg1024 = 0xE400E400u;
+constexpr uint32_t kHNeg64 = 0xD400D400u;
+constexpr uint32_t kLoNib = 0x640F640Fu;
+constexpr uint32_t kHiNib = 0x64F064F0u;
+
+template <int D> struct Raw;
+template <> struct Raw<kQ4_K> { uint4 hd, cw; };                          // header, 16 code bytes
+template <> struct Raw<kQ6_K> { uint32_t w[12]; uint4 sv; uint32_t d; };  // lane quads 2hv, 2hv+1: 6 words each
+template <> struct Raw<kQ4_0> { int dummy; };
+template <> struct Raw<kQ8_0> { int dummy; };
+
 template <int D>
-__device__ __forceinline__ void dequant_row(const Planes& p, int64_t grow, int64_t kb, uint32_t row, uint8_t* a) {
-    uint32_t h[32];  // 64 halves
+__device__ __forceinline__ void load_raw(const Planes& p, int64_t grow, int64_t kb, int hv, Raw<D>& r) {
     if constexpr (D == kQ4_K) {
-        const int64_t c = kb >> 2;
+        const uint8_t* b = p.q + (grow * p.nb + (kb >> 2)) * 144;
         const int qt = (int)(kb & 3);
-        const uint8_t* b = p.q + (grow * p.nb + c) * 144;
-        const uint4 hd = *reinterpret_cast<const uint4*>(b);
-        const uint4 c0 = *reinterpret_cast<const uint4*>(b + 16 + 32 * qt);
-        const uint4 c1 = *reinterpret_cast<const uint4*>(b + 32 + 32 * qt);
-        const float d = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xFFFF)));
-        const float dmin = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
-        // scale byte i of the 12 (quant/packed.lisp:91-98)
-        const uint32_t sw[3] = {hd.y, hd.z, hd.w};
-        auto sbyte = [&](int i) -> int { return (int)((sw[i >> 2] >> (8 * (i & 3))) & 0xFF); };
-        float ds[2], dm[2];
-#pragma unroll
-        for (int u = 0; u < 2; u++) {
-            const int g = 2 * qt + u;
-            int sc, mn;
-            if (g < 4) {
-                sc = sbyte(g) & 63;
-                mn = sbyte(g + 4) & 63;
-            } else {
-                sc = (sbyte(g + 4) & 15) | ((sbyte(g - 4) & 192) >> 2);
-                mn = (sbyte(g + 4) >> 4) | ((sbyte(g) & 192) >> 2);
-            }
-            ds[u] = d * (float)sc;
-            dm[u] = dmin * (float)mn;
-        }
-        const uint32_t wv[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-        for (int wi = 0; wi < 8; wi++) {
-#pragma unroll
-            for (int bp = 0; bp < 2; bp++) {  // bytes 2bp, 2bp+1 of the word
-                const uint32_t b0 = (wv[wi] >> (16 * bp)) & 0xFF, b1 = (wv[wi] >> (16 * bp + 8)) & 0xFF;
-                const int l = 4 * wi + 2 * bp;  // element index in the sub-block
-                h[l / 2] = pack_half2(fmaf(ds[0], nibf(b0 & 15), -dm[0]), fmaf(ds[0], nibf(b1 & 15), -dm[0]));
-                h[16 + l / 2] = pack_half2(fmaf(ds[1], nibf(b0 >> 4), -dm[1]), fmaf(ds[1], nibf(b1 >> 4), -dm[1]));
-            }
-        }
+        r.hd = *reinterpret_cast<const uint4*>(b);
+        r.cw = *reinterpret_cast<const uint4*>(b + 16 + 32 * qt + 16 * hv);
     } else if constexpr (D == kQ6_K) {
         const int64_t blk = grow * p.nb + (kb >> 2);
+        // lane-major plane (layout.cuh): lane quad t's words for (hh, half) sit at
+        // t*48 + (2hh + half)*12; the 24 bytes of one hh start 16-byte aligned
+        // when hh = 0 and 8 bytes past alignment when hh = 1 (warp-uniform).
+        const int hh = (int)((kb & 3) >> 1);
+#pragma unroll
+        for (int tq = 0; tq < 2; tq++) {
+            const uint8_t* q = p.q + blk * 192 + (2 * hv + tq) * 48 + 24 * hh;
+            uint32_t* w = &r.w[6 * tq];
+            if (hh == 0) {
+                const uint4 a = *reinterpret_cast<const uint4*>(q);
+                const uint2 b = *reinterpret_cast<const uint2*>(q + 16);
+                w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y;
+            } else {
+                const uint2 a = *reinterpret_cast<const uint2*>(q);
+                const uint4 b = *reinterpret_cast<const uint4*>(q + 8);
+                w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y; w[4] = b.z; w[5] = b.w;
+            }
+        }
+        r.sv = *reinterpret_cast<const uint4*>(p.s + blk * 16);
+        r.d = *reinterpret_cast<const unsigned short*>(p.d + 2 * blk);
+    }
+}
+
+// Half hv of row `row`: four of its eight 16-byte chunks -- {2hv, 2hv+1,
+// 4+2hv, 5+2hv} for Q4_K/Q4_0/Q8_0 (elements 16hv..16hv+15 of each 32),
+// {hv, 2+hv, 4+hv, 6+hv} for Q6_K (lane quads 2hv, 2hv+1).
+template <int D>
+__device__ __forceinline__ void convert_raw(const Planes& p, int64_t grow, int64_t kb, int hv, const Raw<D>& rw,
+                                            uint32_t row, uint8_t* a) {
+    uint4 ch[4];
+    int ci[4] = {2 * hv, 2 * hv + 1, 4 + 2 * hv, 5 + 2 * hv};
+    if constexpr (D == kQ4_K) {
         const int qt = (int)(kb & 3);
-        const int hh = qt >> 1, odd = qt & 1;  // 128-element half, group pair {2odd, 2odd+1}
-        const uint8_t* q = p.q + blk * 192;
-        const float d = __half2float(__ushort_as_half(*reinterpret_cast<const unsigned short*>(p.d + 2 * blk)));
-        const uint4 sv = *reinterpret_cast<const uint4*>(p.s + blk * 16);
-        auto sc = [&](int i) -> int {  // int8 sub-scale i (runtime index: select, no local array)
+        auto sbyte = [&](int i) -> uint32_t {  // scale byte i of the 12, runtime index
             const int wsel = i >> 2;
-            const uint32_t w = wsel == 0 ? sv.x : wsel == 1 ? sv.y : wsel == 2 ? sv.z : sv.w;
+            const uint32_t w = wsel == 0 ? rw.hd.y : wsel == 1 ? rw.hd.z : rw.hd.w;
+            return (w >> (8 * (i & 3))) & 0xFF;
+        };
+        uint32_t sc[2], mn[2];
+#pragma unroll
+        for (int u = 0; u < 2; u++) {  // quant/packed.lisp:91-98
+            const int g = 2 * qt + u;
+            if (g < 4) {
+                sc[u] = sbyte(g) & 63;
+                mn[u] = sbyte(g + 4) & 63;
+            } else {
+                sc[u] = (sbyte(g + 4) & 15) | ((sbyte(g - 4) & 192) >> 2);
+                mn[u] = (sbyte(g + 4) >> 4) | ((sbyte(g) & 192) >> 2);
+            }
+        }
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(rw.hd.x >> 16)));
+        const uint32_t D2 = prmt(rw.hd.x, rw.hd.x, 0x1010);  // (d, d)
+        const uint32_t SC0 = hsub2(prmt(sc[0], kMagic, 0x4040), kH1024), SC1 = hsub2(prmt(sc[1], kMagic, 0x4040), kH1024);
+        const uint32_t N0 = hmul2(SC0, kHNeg1024), N1 = hmul2(SC1, kHNeg64), S1 = hmul2(SC1, kHSixteenth);
+        const uint32_t M0 = dup_half(-dmin * (float)mn[0]), M1 = dup_half(-dmin * (float)mn[1]);
+        const uint32_t cw[4] = {rw.cw.x, rw.cw.y, rw.cw.z, rw.cw.w};
+        uint32_t g0[8], g1[8];
+#pragma unroll
+        for (int wi = 0; wi < 4; wi++) {
+            const uint32_t p01 = prmt(cw[wi], kMagic, 0x4140), p23 = prmt(cw[wi], kMagic, 0x4342);
+            // sc*q exact in fp16, then one fused d*(sc*q) - dmin*m
+            g0[2 * wi] = hfma2(hfma2(p01 & kLoNib, SC0, N0), D2, M0);
+            g0[2 * wi + 1] = hfma2(hfma2(p23 & kLoNib, SC0, N0), D2, M0);
+            g1[2 * wi] = hfma2(hfma2(p01 & kHiNib, S1, N1), D2, M1);
+            g1[2 * wi + 1] = hfma2(hfma2(p23 & kHiNib, S1, N1), D2, M1);
+        }
+        ch[0] = make_uint4(g0[0], g0[1], g0[2], g0[3]);
+        ch[1] = make_uint4(g0[4], g0[5], g0[6], g0[7]);
+        ch[2] = make_uint4(g1[0], g1[1], g1[2], g1[3]);
+        ch[3] = make_uint4(g1[4], g1[5], g1[6], g1[7]);
+    } else if constexpr (D == kQ6_K) {
+        const int odd = (int)(kb & 1);  // group pair {2odd, 2odd+1} of the 128-element half hh
+        const int hh = (int)((kb & 3) >> 1);
+        const float d = __half2float(__ushort_as_half((unsigned short)rw.d));
+        auto sc = [&](int i) -> int {
+            const int wsel = i >> 2;
+            const uint32_t w = wsel == 0 ? rw.sv.x : wsel == 1 ? rw.sv.y : wsel == 2 ? rw.sv.z : rw.sv.w;
             return (int)(int8_t)((w >> (8 * (i & 3))) & 0xFF);
         };
+        // words of (t = 2hv + tq, half): wv[6 tq + 3 half + {0: ql p0, 1: ql p1, 2: qh}]
+        const uint32_t* wv = rw.w;
 #pragma unroll
-        for (int u = 0; u < 2; u++) {  // group grp = 2odd + u, elements 32u .. 32u+31 of the block
+        for (int u = 0; u < 2; u++) {
             const int grp = 2 * odd + u;
+            const int lo_shift = 4 * (grp >> 1);  // low or high nibble of ql
+            const int qsh = 2 * grp;              // qh bit position
 #pragma unroll
             for (int half = 0; half < 2; half++) {
-                const float fs = d * (float)sc(8 * hh + 2 * grp + half);
+                // (d * sc) rounded to fp16 once; the product with (q - 32) rounds once more
+                const uint32_t FS = dup_half(d * (float)sc(8 * hh + 2 * grp + half));
+                uint32_t pr[4];
 #pragma unroll
-                for (int t = 0; t < 4; t++) {
-                    const uint8_t* base = q + t * 48 + (2 * hh + half) * 12;
-                    const uint32_t ql = *reinterpret_cast<const uint32_t*>(base + 4 * (grp & 1));
-                    const uint32_t qh = *reinterpret_cast<const uint32_t*>(base + 8);
-                    float v[4];
-#pragma unroll
-                    for (int bw = 0; bw < 4; bw++) {
-                        const uint32_t lo = (ql >> (8 * bw + 4 * (grp >> 1))) & 15;
-                        const uint32_t hi = (qh >> (8 * bw + 2 * grp)) & 3;
-                        v[bw] = fs * (nibf(lo | (hi << 4)) - 32.f);
-                    }
-                    const int l = 16 * half + 4 * t;  // element in the group
-                    h[16 * u + l / 2] = pack_half2(v[0], v[1]);
-                    h[16 * u + l / 2 + 1] = pack_half2(v[2], v[3]);
+                for (int tq = 0; tq < 2; tq++) {
+                    const uint32_t* w3 = &wv[6 * tq + 3 * half];
+                    // four 6-bit codes (elements l = 16 half + 4 (2hv + tq) + 0..3), one per byte lane
+                    const uint32_t q = ((w3[u] >> lo_shift) & 0x0F0F0F0Fu) | (((w3[2] >> qsh) & 0x03030303u) << 4);
+                    pr[2 * tq] = hmul2(hsub2(prmt(q, kMagic, 0x4140), kH1056), FS);
+                    pr[2 * tq + 1] = hmul2(hsub2(prmt(q, kMagic, 0x4342), kH1056), FS);
                 }
+                ch[2 * u + half] = make_uint4(pr[0], pr[1], pr[2], pr[3]);
+                ci[2 * u + half] = 4 * u + 2 * half + hv;
             }
         }
     } else {
-        // Q4_0 / Q8_0: two 32-element blocks, element by element
+        // Q4_0 / Q8_0: element by element (two 32-element blocks)
+        uint32_t g0[8], g1[8];
 #pragma unroll
-        for (int i = 0; i < 32; i++)
-            h[i] = pack_half2(element_planar<D>(p, grow, kb * kKB + 2 * i), element_planar<D>(p, grow, kb * kKB + 2 * i + 1));
+        for (int j = 0; j < 8; j++) {
+            const int64_t e0 = kb * kKB + 16 * hv + 2 * j, e1 = e0 + 32;
+            g0[j] = pack_half2(element_planar<D>(p, grow, e0), element_planar<D>(p, grow, e0 + 1));
+            g1[j] = pack_half2(element_planar<D>(p, grow, e1), element_planar<D>(p, grow, e1 + 1));
+        }
+        ch[0] = make_uint4(g0[0], g0[1], g0[2], g0[3]);
+        ch[1] = make_uint4(g0[4], g0[5], g0[6], g0[7]);
+        ch[2] = make_uint4(g1[0], g1[1], g1[2], g1[3]);
+        ch[3] = make_uint4(g1[4], g1[5], g1[6], g1[7]);
     }
 #pragma unroll
-    for (int c = 0; c < 8; c++)
-        *reinterpret_cast<uint4*>(a + swz(row, c)) = make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+    for (int i = 0; i < 4; i++) *reinterpret_cast<uint4*>(a + swz(row, (uint32_t)ci[i])) = ch[i];
 }
 
 struct GemmParams {
@@ -312,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) {
-            mbar_init(&full_a[s], 4);
+            mbar_init(&full_a[s], 8);
             mbar_init(&full_b[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -331,40 +418,47 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
     const uint32_t tmem = *tmem_slot;
     int* err = P.err;
 
-    if (warp < 4) {
-        // ---- weight tiles ----
-        const uint32_t row = (uint32_t)threadIdx.x;  // 0..127
+    if (warp < 8) {
+        // ---- weight tiles: thread i converts half (i / 128) of row (i % 128) ----
+        const uint32_t row = (uint32_t)(threadIdx.x & 127);
+        const int hv = threadIdx.x >> 7;
         const int64_t grow_u = row0 + row;
         const int64_t grow = grow_u < P.rows ? grow_u : P.rows - 1;
+        Raw<D> r0, r1, r2;  // stages it, it+1, it+2
+        if (nk > 0) load_raw<D>(P.p, grow, kb0, hv, r0);
+        if (nk > 1) load_raw<D>(P.p, grow, kb0 + 1, hv, r1);
         for (int it = 0; it < nk; it++) {
             const int s = it % kStages;
+            if (it + 2 < nk) load_raw<D>(P.p, grow, kb0 + it + 2, hv, r2);  // two stages in flight
             if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, err)) break;
-            dequant_row<D>(P.p, grow, kb0 + it, row, A + s * kTM * 128);
+            convert_raw<D>(P.p, grow, kb0 + it, hv, r0, row, A + s * kTM * 128);
             fence_async_shared();
             __syncwarp();
             if (lane == 0) mbar_arrive(&full_a[s]);
+            r0 = r1;
+            r1 = r2;
         }
-        // ---- epilogue: tensor memory -> out ----
+        // ---- epilogue: tensor memory -> out; warp w: lanes 32 (w % 4).., column half w / 4 ----
         const bool ok = mbar_wait(done, 0, err);
         tc_fence_after();
         if (ok) {
-            const int64_t r = row0 + 32 * warp + lane;
-            const uint32_t taddr = tmem + ((uint32_t)(32 * warp) << 16);
-            for (int c0 = 0; c0 < tn; c0 += 32) {
-                uint32_t v[32];
+            const int q = warp & 3, ch = warp >> 2;
+            const int64_t r = row0 + 32 * q + lane;
+            const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
+            const int cbeg = ch * (tn / 2), cend = cbeg + tn / 2;
+            for (int c0 = cbeg; c0 < cend; c0 += 16) {
+                uint32_t v[16];
                 asm volatile(
-                    "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-                    "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+                    "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                    "[%16];"
                     : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
                       "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
-                      "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]),
-                      "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]),
-                      "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+                      "=r"(v[15])
                     : "r"(taddr + (uint32_t)c0));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 if (r < P.rows) {
 #pragma unroll
-                    for (int j = 0; j < 32; j++) {
+                    for (int j = 0; j < 16; j++) {
                         const int64_t t = tt * tn + c0 + j;
                         if (t < P.m) {
                             const float val = __uint_as_float(v[j]) * P.us[t];
@@ -375,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
                 }
             }
         }
-    } else if (warp == 4) {
+    } else if (warp == 8) {
         // ---- activation tiles: one bulk copy per stage ----
         if (lane == 0) {
             const uint32_t bytes = (uint32_t)tn * 128;
@@ -407,7 +501,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
         }
     }
     // Bulk copies in flight must land before the CTA exits.
-    if (warp == 4 && lane == 0) {
+    if (warp == 8 && lane == 0) {
         for (int it = nk - kStages < 0 ? 0 : nk - kStages; it < nk; it++)
             mbar_drain(&full_b[it % kStages], (it / kStages) & 1);
     }

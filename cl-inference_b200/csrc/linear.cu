@@ -1,5 +1,5 @@
-// linear.cu -- chooses the kernel for one packed linear, and owns the
-// per-stream scratch the prefill GEMM stages its activations in.
+// linear.cu -- chooses the kernel for one packed linear, and provides the
+// scratch the prefill GEMM stages its activations in.
 #include <cstdlib>
 #include <map>
 #include <mutex>
@@ -23,30 +23,23 @@ int64_t gemm_min_m() {
     return v;
 }
 
-// Grow-only device scratch per (device, stream).  Calls on one stream are
-// ordered, so they can share it; growing frees the old buffer (cudaFree waits
-// for the device), which cannot happen while a graph is being captured.
-std::mutex g_scratch_mu;
-std::map<std::pair<int, cudaStream_t>, std::pair<void*, size_t>> g_scratch;
-
-cudaError_t scratch_for(cudaStream_t stream, size_t bytes, uint8_t** out) {
+// Scratch for one GEMM call comes from the device's stream-ordered pool: it is
+// allocated and released on the call's stream (graph memory nodes when the
+// stream is being captured), so concurrent streams never share it.  The pool
+// keeps released memory for reuse instead of returning it at each sync.
+cudaError_t keep_pool_memory() {
+    static std::mutex mu;
+    static std::map<int, bool> done;
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
-    std::lock_guard<std::mutex> lock(g_scratch_mu);
-    auto& slot = g_scratch[{dev, stream}];
-    if (slot.second < bytes) {
-        cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-        if (cudaStreamIsCapturing(stream, &cap) == cudaSuccess && cap != cudaStreamCaptureStatusNone)
-            return cudaErrorStreamCaptureUnsupported;
-        if (slot.first) cudaFree(slot.first);
-        slot = {nullptr, 0};
-        const size_t want = bytes + bytes / 4;
-        void* p = nullptr;
-        if ((e = cudaMalloc(&p, want)) != cudaSuccess) return e;
-        slot = {p, want};
-    }
-    *out = (uint8_t*)slot.first;
+    std::lock_guard<std::mutex> lock(mu);
+    if (done[dev]) return cudaSuccess;
+    cudaMemPool_t pool;
+    if ((e = cudaDeviceGetDefaultMemPool(&pool, dev)) != cudaSuccess) return e;
+    uint64_t keep = UINT64_MAX;
+    if ((e = cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &keep)) != cudaSuccess) return e;
+    done[dev] = true;
     return cudaSuccess;
 }
 
@@ -61,10 +54,13 @@ cudaError_t launch_linear(const WeightView& w, int64_t rows, const void* x, int 
                           float* out, int64_t ldo, unsigned flags, cudaStream_t stream) {
     if (uses_gemm_tc(w, xtype, m, flags)) {
         const GemmPlan g = plan_gemm_tc(rows, w.k, m);
-        uint8_t* scratch = nullptr;
-        cudaError_t e = scratch_for(stream, gemm_tc_scratch_bytes(g), &scratch);
+        cudaError_t e = keep_pool_memory();
         if (e != cudaSuccess) return e;
-        return launch_gemm_tc(w, rows, x, xtype, m, out, ldo, scratch, g, stream);
+        void* scratch = nullptr;
+        if ((e = cudaMallocAsync(&scratch, gemm_tc_scratch_bytes(g), stream)) != cudaSuccess) return e;
+        e = launch_gemm_tc(w, rows, x, xtype, m, out, ldo, (uint8_t*)scratch, g, stream);
+        cudaError_t f = cudaFreeAsync(scratch, stream);
+        return e != cudaSuccess ? e : f;
     }
     if (gemv_mma_supported(w, m)) return launch_gemv_mma(w, rows, x, xtype, m, out, ldo, stream);
     return launch_linear_generic(w, rows, x, xtype, m, out, ldo, stream);
