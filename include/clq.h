@@ -51,7 +51,7 @@ enum clq_status {
 #define CLQ_STORE_DEFAULT 0u
 
 /* Product flags. */
-#define CLQ_MATH_DEFAULT 0u   /* fp32-class results (all M)                          */
+#define CLQ_MATH_DEFAULT 0u   /* fp32-class results for fp32 activations             */
 #define CLQ_MATH_FAST 1u      /* prefill GEMM may round dequantized weights to fp16  */
 #define CLQ_NO_CACHE 2u       /* host-pointer calls: upload, use and drop the weight */
 
@@ -98,9 +98,11 @@ int clq_clear_cache(void);
 int clq_cache_stats(int64_t *count, int64_t *device_bytes);
 
 /* ---- device-resident packed-weight store ----------------------------------
- * Uploads N x K packed blocks once, in their native GGUF byte layout, to the
- * current device, after checking that every fp16 scale is finite (the load-time
- * check of mlx/gguf/weights.lisp:19-23).  The store owns the device copy.
+ * Uploads N x K packed blocks (native GGUF byte layout) once to the current
+ * device, checks that every fp16 scale is finite (the load-time check of
+ * mlx/gguf/weights.lisp:19-23), and re-tiles them on the device into aligned
+ * planes; re-tiling only moves bytes, so every decoded value is unchanged.  The
+ * store owns the device copy.
  */
 typedef struct clq_store clq_store;
 
