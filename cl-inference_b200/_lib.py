@@ -46,6 +46,7 @@ SIGNATURES = {
                               ctypes.POINTER(_size), ctypes.POINTER(_ptr), ctypes.POINTER(_int)]),
     "clq_linear_device": (_int, [_ptr, _i64, _i64, _ptr, _int, _i64, _ptr, _i64, _u32, _ptr]),
     "clq_linear_group_device": (_int, [_ptr, _ptr, _ptr, _int, _ptr, _int, _i64, _ptr, _ptr, _u32, _ptr]),
+    "clq_linear_device_noalloc": (_int, [_ptr, _i64, _i64, _ptr, _int, _i64, _ptr, _i64, _ptr]),
     "clq_dequantize_device": (_int, [_ptr, _i64, _i64, _ptr, _int, _ptr]),
     "clq_gather_device": (_int, [_ptr, _ptr, _i64, _ptr, _ptr]),
     "clq_dequantize": (_int, [_int, _ptr, _size, _ptr]),

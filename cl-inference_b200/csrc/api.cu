@@ -562,3 +562,69 @@ int clq_take(int dtype, const uint8_t* bytes, int64_t n, int64_t k, const int32_
 }
 
 }  // extern "C"
+
+// ---- prefill GEMM on a fixed, preallocated scratch buffer ------------------
+//
+// Some callers cannot allocate device memory when they call in: a process
+// whose device memory is reserved up front by another framework's allocator
+// (a call-time cudaMalloc could fail at an unpredictable moment), or a
+// latency-bound loop that cannot afford the device-wide synchronization that
+// cudaMalloc/cudaFree may imply.  clq_linear_device_noalloc runs the same
+// tensor-core GEMM as clq_linear_device's prefill path, but stages its
+// activations and split-K partials in this file-scope device array, which
+// every GPU that loads the library holds until the process exits.
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[CLQ_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+// The device address of g_noalloc_scratch for the current device, looked up
+// once per device with that device current (in host code the symbol is only a
+// host-side stand-in, never a device address).
+int noalloc_scratch(int device, uint8_t** out) {
+    static std::mutex mu;
+    static std::vector<uint8_t*> addr;
+    std::lock_guard<std::mutex> lock(mu);
+    if ((int)addr.size() <= device) addr.resize(device + 1, nullptr);
+    if (!addr[device]) {
+        void* p = nullptr;
+        cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(noalloc scratch)");
+        addr[device] = (uint8_t*)p;
+    }
+    *out = addr[device];
+    return CLQ_OK;
+}
+
+}  // namespace
+
+extern "C" int clq_linear_device_noalloc(const clq_store* w, int64_t row_begin, int64_t rows, const void* x,
+                                         int xtype, int64_t m, float* out, int64_t ldo, void* stream) {
+    if (!w) return fail(CLQ_ERR_ARGUMENT, "null store");
+    if (xtype != CLQ_X_F32 && xtype != CLQ_X_BF16 && xtype != CLQ_X_F16)
+        return fail(CLQ_ERR_ARGUMENT, "unknown activation type %d", xtype);
+    if (row_begin < 0 || rows < 0 || row_begin + rows > w->n || m < 0)
+        return fail(CLQ_ERR_SHAPE, "rows [%lld, %lld) / m %lld outside a (%lld %lld) weight",
+                    (long long)row_begin, (long long)(row_begin + rows), (long long)m,
+                    (long long)w->n, (long long)w->k);
+    if (ldo < rows) return fail(CLQ_ERR_SHAPE, "output stride %lld < rows %lld", (long long)ldo, (long long)rows);
+    if (m == 0 || rows == 0) return CLQ_OK;
+    if (!x || !out) return fail(CLQ_ERR_ARGUMENT, "null activation or output pointer");
+    if (w->k % 256) return fail(CLQ_ERR_UNSUPPORTED, "row length %lld is not a multiple of 256", (long long)w->k);
+    int device, rc;
+    if ((rc = current_device(&device))) return rc;
+    if (device != w->device)
+        return fail(CLQ_ERR_ARGUMENT, "store lives on device %d, current device is %d", w->device, device);
+    const clq::GemmPlan g = clq::plan_gemm_tc_capped(rows, w->k, m, CLQ_NOALLOC_SCRATCH_BYTES);
+    if (g.splits == 0)
+        return fail(CLQ_ERR_SHAPE,
+                    "%lld activation rows x %lld columns need %zu bytes of staging; the fixed buffer holds %u",
+                    (long long)m, (long long)w->k, clq::gemm_tc_scratch_bytes(clq::plan_gemm_tc_capped(rows, w->k, m, (size_t)-1)),
+                    (unsigned)CLQ_NOALLOC_SCRATCH_BYTES);
+    uint8_t* scratch = nullptr;
+    if ((rc = noalloc_scratch(device, &scratch))) return rc;
+    cudaError_t e = clq::launch_gemm_tc(view_of(w, row_begin), rows, x, xtype, m, out, ldo, scratch, g,
+                                        (cudaStream_t)stream);
+    if (e != cudaSuccess) return cuda_fail(e, "prefill kernel launch");
+    return CLQ_OK;
+}

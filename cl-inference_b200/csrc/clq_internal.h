@@ -63,6 +63,9 @@ struct GemmPlan {
 };
 GemmPlan plan_gemm_tc(int64_t rows, int64_t k, int64_t m);
 size_t gemm_tc_scratch_bytes(const GemmPlan& g);
+// plan_gemm_tc with fewer K splits until the scratch fits in CAP bytes;
+// splits = 0 when it cannot fit.
+GemmPlan plan_gemm_tc_capped(int64_t rows, int64_t k, int64_t m, size_t cap);
 bool gemm_tc_supported(const WeightView& w, int64_t m);
 // SCRATCH: gemm_tc_scratch_bytes(g) device bytes, 256-byte aligned, private to
 // this call until it completes on STREAM.

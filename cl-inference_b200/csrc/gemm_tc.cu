@@ -560,6 +560,18 @@ GemmPlan plan_gemm_tc(int64_t rows, int64_t k, int64_t m) {
     return g;
 }
 
+GemmPlan plan_gemm_tc_capped(int64_t rows, int64_t k, int64_t m, size_t cap) {
+    GemmPlan g = plan_gemm_tc(rows, k, m);
+    while (g.splits > 1 && gemm_tc_scratch_bytes(g) > cap) {
+        g.splits /= 2;
+        const int64_t kbt = k / kKB;
+        g.kb_per_split = (int)((kbt + g.splits - 1) / g.splits);
+        g.part_bytes = g.splits > 1 ? (size_t)g.splits * m * rows * sizeof(float) : 0;
+    }
+    if (gemm_tc_scratch_bytes(g) > cap) g.splits = 0;  // does not fit even unsplit
+    return g;
+}
+
 size_t gemm_tc_scratch_bytes(const GemmPlan& g) {
     auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
     return al(sizeof(int)) + al(g.xs_bytes) + al(g.us_bytes) + al(g.part_bytes);

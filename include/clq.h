@@ -134,6 +134,24 @@ int clq_linear_group_device(const clq_store *const *w, const int64_t *row_begin,
                             int count, const void *x, int xtype, int64_t m, float *const *out,
                             const int64_t *ldo, unsigned flags, void *stream);
 
+/* No counterpart in the reference.  For callers that cannot allocate device
+ * memory at call time -- a process whose device memory another framework's
+ * allocator reserved up front, where a call-time cudaMalloc could fail, or a
+ * latency-bound loop that cannot take the device synchronization cudaMalloc
+ * and cudaFree may imply.  Same product as clq_linear_device's prefill path
+ * (the tcgen05 GEMM; activations rounded to fp16 after a power-of-two scale,
+ * weights dequantized to fp16), but it allocates nothing: its staging lives in
+ * one fixed device buffer of CLQ_NOALLOC_SCRATCH_BYTES that every GPU loading
+ * the library holds until exit.  Requests whose staging (about 2*m*K bytes
+ * plus split-K partials) does not fit are rejected with CLQ_ERR_SHAPE; K must
+ * be a multiple of 256.  The first call on a device looks up the buffer's
+ * device address: make it before any stream capture.  All calls share the
+ * buffer, so calls that overlap on the GPU (other streams, other threads)
+ * race; serialize them on one stream. */
+#define CLQ_NOALLOC_SCRATCH_BYTES (32u << 20)
+int clq_linear_device_noalloc(const clq_store *w, int64_t row_begin, int64_t rows, const void *x,
+                              int xtype, int64_t m, float *out, int64_t ldo, void *stream);
+
 /* ---- dequantize and gather ------------------------------------------------
  * Bit-exact fp32 values of packed-element (quant/packed.lisp:85-108) and the
  * Q8_0 dequantize-executor (quant/q8-0.lisp:98-123).
