@@ -31,6 +31,7 @@ for _p in (ROOT, ROOT / "oracle"):
 
 METRIC = "quant GEMV HBM GB/s (%peak) + 8B-shape Q4_K decode tok/s @1/2/4/8 GPU"
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 
 
 def parse():
@@ -41,6 +42,10 @@ def parse():
     ap.add_argument("--impl", choices=["clq", "reference"], default="clq")
     ap.add_argument("--model", choices=["8b", "70b"], default="8b")
     ap.add_argument("--m", type=int, default=1, help="activation rows (tokens) per step")
+    ap.add_argument("--xtype", choices=["f32", "bf16", "f16"], default=None,
+                    help="activation type; default f32 for decode (M < 64), bf16 for prefill")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decoder layers per step (default: the model's); fewer for profiling captures")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -94,6 +99,42 @@ class ClockSampler(threading.Thread):
                 "samples": len(self.samples)}
 
 
+def peak_tflops():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        try:
+            v = json.loads(f.read_text()).get("bf16_tflops")
+            if v:
+                return float(v), "measured"
+        except (ValueError, OSError):
+            pass
+    return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def count_kernel_nodes(graph):
+    """(our kernels, all kernels) among the kernel nodes of a captured graph;
+    ours are the functions whose name carries the clq namespace."""
+    from cuda.bindings import driver as cu
+    g = cu.CUgraph(graph.raw_cuda_graph())
+    _, _, n = cu.cuGraphGetNodes(g, 0)
+    _, nodes, n = cu.cuGraphGetNodes(g, n)
+    ours = total = 0
+    for node in nodes[:n]:
+        _, kind = cu.cuGraphNodeGetType(node)
+        if kind != cu.CUgraphNodeType.CU_GRAPH_NODE_TYPE_KERNEL:
+            continue
+        total += 1
+        _, prm = cu.cuGraphKernelNodeGetParams(node)
+        name = b""
+        if int(prm.func):
+            _, name = cu.cuFuncGetName(prm.func)
+        elif int(prm.kern):
+            _, name = cu.cuKernelGetName(prm.kern)
+        if name and b"clq" in name:
+            ours += 1
+    return ours, total
+
+
 def dist_setup(torch):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -139,8 +180,13 @@ def run_clq(args):
     tp = importlib.import_module("cl-inference_b200.tp")
     rank, world, local = dist_setup(torch)
     dist = torch.distributed if world > 1 else None
-    cfg = tp.LLAMA3_8B if args.model == "8b" else tp.LLAMA3_70B
+    cfg = dict(tp.LLAMA3_8B if args.model == "8b" else tp.LLAMA3_70B)
+    if args.layers:
+        cfg["layers"] = args.layers
     m = args.m
+    xtype = args.xtype or ("f32" if m < 64 else "bf16")
+    xdtype = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[xtype]
+    prefill = m >= 64 and xtype != "f32"
     linears = tp.model_linears(cfg)
     q_dim = cfg["heads"] * cfg["head_dim"]
 
@@ -165,6 +211,7 @@ def run_clq(args):
         "attn": torch.randn(m, attn_cols[1] - attn_cols[0], device="cuda", generator=gen),
         "ffn": torch.randn(m, ffn_cols[1] - ffn_cols[0], device="cuda", generator=gen),
     }
+    inputs = {key: v.to(xdtype) for key, v in inputs.items()}
     outs = [torch.empty(m, st.n, device="cuda") for (_, st, *_r) in stores]
     logits = torch.empty(world, m, stores[-1][1].n, device="cuda")
     # one launch per group of linears reading the same activations: per layer
@@ -196,7 +243,7 @@ def run_clq(args):
 
     # algorithmic bytes (W + x + out) of this rank's step, summed over ranks
     def lin_bytes(st, dtype):
-        return tp.weight_bytes(dtype, st.n, st.k) + 4 * m * st.k + 4 * m * st.n
+        return tp.weight_bytes(dtype, st.n, st.k) + inputs["hidden"].element_size() * m * st.k + 4 * m * st.n
     step_bytes = float(sum(lin_bytes(st, dt) for (_, st, dt, *_r) in stores))
     if dist is not None:
         t = torch.tensor([step_bytes], dtype=torch.float64, device="cuda")
@@ -213,9 +260,15 @@ def run_clq(args):
             step()
     torch.cuda.current_stream().wait_stream(side)
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
+    graph = torch.cuda.CUDAGraph(keep_graph=True)
     with torch.cuda.graph(graph):
         step()
+    try:
+        ours_per_step, kernels_per_step = count_kernel_nodes(graph)
+    except Exception as exc:  # launch count unavailable: say so rather than guess
+        ours_per_step, kernels_per_step = None, None
+        print(f"kernel-node count failed: {exc!r}", file=sys.stderr)
+    graph.instantiate()
     for _ in range(max(args.warmup, 3)):
         graph.replay()
     torch.cuda.synchronize()
@@ -262,6 +315,8 @@ def run_clq(args):
     k_ms = ks.elapsed_time(ke) / (reps * len(q4k_groups))
     k_bytes = sum(lin_bytes(stores[j][1], "q4_k") for idx in q4k_groups for j in idx) / len(q4k_groups)
     k_gbs = k_bytes / (k_ms * 1e-3) / 1e9
+    k_flops = sum(2.0 * m * stores[j][1].n * stores[j][1].k for idx in q4k_groups for j in idx) / len(q4k_groups)
+    step_flops = sum(2.0 * m * st.n * st.k for (_, st, *_r) in stores)
     traffic = None
     tfile = ROOT / "profiles" / "q4k_gemv_traffic.json"
     if tfile.exists():
@@ -270,7 +325,7 @@ def run_clq(args):
     # ---- end to end -------------------------------------------------------------
     e2e = None
     if not args.no_e2e:
-        e2e = e2e_dropin(args, clq, stores, host_copies, m, job_bytes) if world == 1 else \
+        e2e = e2e_dropin(args, clq, stores, host_copies, m, job_bytes, prefill) if world == 1 else \
             e2e_tp(args, torch, dist, graph, inputs, logits, job_bytes)
 
     del graph, kgraph
@@ -282,21 +337,35 @@ def run_clq(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {
-                "workload": f"llama3-{args.model}-shape Q4_K-M decode linears, M={m}: "
-                            f"{cfg['layers']} layers x (q,k,v,o,gate,up Q4_K; down Q6_K) + Q6_K output",
-                "m": m, "parallelism": f"tp{world}", "weights_gb": round(job_bytes / 1e9, 3),
+                "workload": f"llama3-{args.model}-shape Q4_K-M {'prefill' if prefill else 'decode'} linears, "
+                            f"M={m}, {xtype} activations: {cfg['layers']} layers x (q,k,v,o,gate,up Q4_K; "
+                            f"down Q6_K) + Q6_K output",
+                "m": m, "xtype": xtype, "layers": cfg["layers"], "parallelism": f"tp{world}",
+                "weights_gb": round(job_bytes / 1e9, 3),
                 "l2": "weights per step far above the 126 MB L2; no flush",
             },
-            "tok_per_s": round(1000.0 / ms, 2),
+            "tok_per_s": round(1000.0 * m / ms, 2),
             "hbm_frac": round(gbs / world / peak, 4),
-            "roofline": {"bound": "hbm", "kernel": "Q4_K GEMV launches (q/k/v group, o, gate/up group), M=%d" % m,
-                         "achieved": round(k_gbs, 1), "peak": peak, "peak_kind": peak_kind,
-                         "unit": "GB/s", "frac": round(k_gbs / peak, 4), "traffic": traffic,
-                         "algorithmic_bytes_per_launch": round(k_bytes),
-                         "us_per_launch": round(k_ms * 1e3, 3)},
-            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches": ours_per_step * args.steps if ours_per_step is not None else None,
+            "gpu_launches_per_step": {"clq": ours_per_step, "all_kernel_nodes": kernels_per_step},
             "clocks": clock,
         }
+        if prefill:
+            tpeak, tpeak_kind = peak_tflops()
+            k_tf = k_flops / (k_ms * 1e-3) / 1e12
+            result["tflops"] = round(step_flops * world / (ms * 1e-3) / 1e12, 1)
+            result["roofline"] = {
+                "bound": "tensor", "kernel": "Q4_K linears (activation prep + tcgen05 GEMM + split-K reduce), "
+                                            "M=%d" % m,
+                "achieved": round(k_tf, 1), "peak": tpeak, "peak_kind": tpeak_kind + " (burst, dense bf16)",
+                "unit": "TFLOP/s", "frac": round(k_tf / tpeak, 4), "traffic": None,
+                "algorithmic_flops_per_launch": round(k_flops), "us_per_launch": round(k_ms * 1e3, 3)}
+        else:
+            result["roofline"] = {
+                "bound": "hbm", "kernel": "Q4_K GEMV launches (q/k/v group, o, gate/up group), M=%d" % m,
+                "achieved": round(k_gbs, 1), "peak": peak, "peak_kind": peak_kind,
+                "unit": "GB/s", "frac": round(k_gbs / peak, 4), "traffic": traffic,
+                "algorithmic_bytes_per_launch": round(k_bytes), "us_per_launch": round(k_ms * 1e3, 3)}
         if e2e:
             result["e2e"] = e2e
         if world == 1 and not args.no_cpu:
@@ -308,12 +377,19 @@ def run_clq(args):
         print(json.dumps(result), flush=True)
 
 
-def e2e_dropin(args, clq, stores, host_copies, m, job_bytes):
-    """The host-buffer C ABI (clq_q4_k_matmul & co.), one synchronous call per linear."""
+def e2e_dropin(args, clq, stores, host_copies, m, job_bytes, prefill=False):
+    """The host-buffer C ABI (clq_q4_k_matmul & co.), one synchronous call per linear.
+    Prefill passes CLQ_MATH_FAST through clq_matmul so the fp32 host activations
+    take the tensor-core GEMM."""
+    import functools
     import numpy as np
     lib = clq._lib.lib
-    fns = {"q4_k": lib.clq_q4_k_matmul, "q6_k": lib.clq_q6_k_matmul,
-           "q8_0": lib.clq_q8_0_matmul, "q4_0": lib.clq_q4_0_matmul}
+    if prefill:
+        ggml = {"q4_0": 2, "q8_0": 8, "q4_k": 12, "q6_k": 14}
+        fns = {d: functools.partial(lambda t, *a: lib.clq_matmul(t, *a, 1), g) for d, g in ggml.items()}
+    else:
+        fns = {"q4_k": lib.clq_q4_k_matmul, "q6_k": lib.clq_q6_k_matmul,
+               "q8_0": lib.clq_q8_0_matmul, "q4_0": lib.clq_q4_0_matmul}
     rng = np.random.default_rng(3)
     xs = {}
     outs = []
@@ -345,7 +421,8 @@ def e2e_dropin(args, clq, stores, host_copies, m, job_bytes):
     lib.clq_clear_cache()
     return {"value": round(job_bytes / sec / 1e9, 1), "unit": "GB/s", "ms_per_step": round(sec * 1e3, 4),
             "tok_per_s": round(1.0 / sec, 2), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "api": "clq_q4_k_matmul/clq_q6_k_matmul, host buffers, one synchronous call per linear",
+            "api": ("clq_matmul(CLQ_MATH_FAST)" if prefill else "clq_q4_k_matmul/clq_q6_k_matmul")
+                   + ", host buffers, one synchronous call per linear",
             "steps": steps}
 
 

@@ -30,6 +30,7 @@ _size = ctypes.c_size_t
 SIGNATURES = {
     "clq_abi_version": (_int, []),
     "clq_last_error": (_int, [ctypes.c_char_p, _size]),
+    "clq_device_status": (_int, [_ptr]),
     "clq_block_geometry": (_int, [_int, ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
     "clq_q8_0_matmul": (_int, [_ptr, _ptr, _ptr, _i64, _i64, _i64]),
     "clq_q4_0_matmul": (_int, [_ptr, _ptr, _ptr, _i64, _i64, _i64]),

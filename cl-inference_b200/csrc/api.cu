@@ -263,9 +263,46 @@ int cached_store(int dtype, int64_t n, int64_t k, const uint8_t* bytes, int devi
 
 }  // namespace
 
+// Sticky per-device status word: a kernel whose bounded wait expires records a
+// CLQ_ERR_* code here and every later wait on the device falls through at once;
+// clq_device_status reads and clears it.
+static __device__ int g_device_status;
+
+int* clq::device_status_word() {
+    static std::mutex mu;
+    static std::vector<int*> addr;
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess) return nullptr;
+    std::lock_guard<std::mutex> lock(mu);
+    if ((int)addr.size() <= device) addr.resize(device + 1, nullptr);
+    if (!addr[device]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+        addr[device] = static_cast<int*>(p);
+    }
+    return addr[device];
+}
+
 // ---------------------------------------------------------------------------
 
 extern "C" {
+
+int clq_device_status(int* status) {
+    if (!status) return fail(CLQ_ERR_ARGUMENT, "null status pointer");
+    *status = CLQ_OK;
+    int device, rc;
+    if ((rc = current_device(&device))) return rc;
+    int* word = clq::device_status_word();
+    if (!word) return fail(CLQ_ERR_CUDA, "device status word not found on device %d", device);
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceSynchronize");
+    int v = 0;
+    if ((e = cudaMemcpy(&v, word, sizeof v, cudaMemcpyDeviceToHost)) != cudaSuccess)
+        return cuda_fail(e, "reading the device status");
+    if (v && (e = cudaMemset(word, 0, sizeof v)) != cudaSuccess) return cuda_fail(e, "clearing the device status");
+    *status = v;
+    return CLQ_OK;
+}
 
 int clq_abi_version(void) { return CLQ_ABI_VERSION; }
 

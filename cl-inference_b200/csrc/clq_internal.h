@@ -45,6 +45,15 @@ cudaError_t launch_linear(const WeightView& w, int64_t rows, const void* x, int 
 
 // Tensor-core fused dequant + GEMV (K a multiple of 256).
 bool gemv_mma_supported(const WeightView& w, int64_t m);
+bool gemv_pdl_enabled();
+// The bulk-copy decode GEMV (m <= 8); cudaErrorNotSupported for shapes it does
+// not take, before anything is launched.
+cudaError_t launch_gemv_bulk_group(const WeightView* const* w, const int64_t* rows, int count, const void* x,
+                                   int xtype, int64_t m, float* const* out, const int64_t* ldo,
+                                   cudaStream_t stream);
+// Device address of the current device's sticky status word (0 = no kernel
+// reported a problem; else a CLQ_ERR_* code), or nullptr if it cannot be found.
+int* device_status_word();
 cudaError_t launch_gemv_mma(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
                             float* out, int64_t ldo, cudaStream_t stream);
 // Up to 4 weights of one dtype and K sharing x, in one launch.

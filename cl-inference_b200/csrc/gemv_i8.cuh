@@ -1,0 +1,319 @@
+// gemv_i8.cuh -- decode GEMV compute on the integer tensor-core MMA for Q4_K and
+// Q6_K at one or two activation rows.
+//
+// Codes become unsigned bytes with one AND (and a shift for high nibbles, an OR
+// for Q6_K's high bits) per four weights -- no conversion to fp16 -- and run
+// through mma.sync m16n8k32 (Q4_K, one 32-element sub-block per MMA) or
+// m16n8k16 (Q6_K, one 16-element sub-scale group per MMA), u8 x s8 -> s32.
+// The activations of a 256-column chunk are scaled by a power of two per
+// (chunk, token) to a 30-bit integer image X = rint(x * 2^e) and split into
+// four balanced base-256 digits, X = D3 2^24 + D2 2^16 + D1 2^8 + D0; MMA column
+// n carries token n / 4, digit 3 - n % 4, so lane t's two accumulator columns
+// are (D3, D2) for even t and (D1, D0) for odd t of token t / 2.  Every integer
+// product and sum is exact; the sub-block scales are applied as one integer
+// multiply-add per accumulator (|sum| < 2^31), and the chunk's fp16 scales in
+// fp32.  Q4_K's min term (dmin * sum_s m_s X_s) and Q6_K's offset term
+// (-32 d sum_j sc_j X_j) are one fp16 MMA per chunk on hi + lo halves of the
+// sub-block sums, as in gemv_common.cuh.  The result carries fp32-class error:
+// the fixed-point image keeps 30 bits relative to the chunk's largest
+// activation, and the digit and term sums are formed in fp32.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "gemv_common.cuh"
+
+namespace clq {
+namespace {
+
+__device__ __forceinline__ void imma_k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+__device__ __forceinline__ void imma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(b0), "r"(0));
+}
+
+// Staged activations of one (chunk, token): digit fragments (1024 bytes), the
+// sub-block / group sum fragments of the fp16 correction MMA, and the unscale
+// factor (padded to 16 bytes).
+template <int D> struct I8Block;
+template <> struct I8Block<kQ4_K> { static constexpr int sf = 32, bytes = 1024 + 32 + 16; };
+template <> struct I8Block<kQ6_K> { static constexpr int sf = 64, bytes = 1024 + 64 + 16; };
+
+// Stage chunks [c0, c0 + pc) of activation rows 0..ntok-1 (ntok <= 2); block
+// (cc, u) at STAGE + (cc * ntok + u) * I8Block<D>::bytes holds
+//   [0, 1024)   digit dg (0 = most significant) of each element, as the MMA's
+//               B fragment: Q4_K uint2 at ((s*4 + tt)*4 + dg) = elements
+//               8tt..8tt+7 of sub-block s (k-slots 4tt.. and 16+4tt..); Q6_K
+//               uint32 at ((j*4 + tt)*4 + dg) = elements 16 half + 4tt.. of
+//               group j = (2h + half)*4 + grp (k-slots 4tt..4tt+3);
+//   [1024, +sf) hi / lo fp16 halves of the sums S of X over the sub-blocks
+//               (Q4_K: uint32 pair (S_2t, S_2t+1) at (t*2 + part)) or groups
+//               (Q6_K: uint2 at (t*2 + part), pairs (2t, 2t+1) and (8+2t, 9+2t)),
+//               times 2^-21;
+//   [.., +4)    the unscale 2^-e.
+template <int D, typename XT, int WARPS>
+__device__ void stage_x_i8(const void* xv, int64_t k, int x_aligned, int64_t c0, int pc, int ntok,
+                           unsigned char* stage) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const XT* x = reinterpret_cast<const XT*>(xv);
+    constexpr int TB = I8Block<D>::bytes;
+    for (int w = warp; w < pc * ntok; w += WARPS) {
+        const int cc = w / ntok, u = w - cc * ntok;
+        unsigned char* base = stage + (size_t)w * TB;
+        const XT* src = x + (int64_t)u * k + (c0 + cc) * 256 + 8 * lane;
+        float v[8];
+        if (x_aligned) {
+            xload8(src, v);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = xload(src + i);
+        }
+        float amax = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        int e = 0;
+        if (amax > 0.f) {
+            // amax * 2^e in [2^29, 2^30): four balanced digits always suffice
+            e = 29 - ((int)((__float_as_uint(amax) >> 23) & 255) - 127);
+            e = e < -100 ? -100 : (e > 120 ? 120 : e);
+        }
+        const float sc = __uint_as_float((uint32_t)(127 + e) << 23);  // 2^e, a normal float for e in [-100, 120]
+        // balanced base-256 digits: the digit's byte is the low byte of the
+        // remainder, and the next remainder is (r + 128) >> 8
+        uint32_t dg[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};  // [digit 3..0][elements 0-3, 4-7]
+        long long lsum = 0;  // this lane's share of the sub-block / group sum of X
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const int Xi = __float2int_rn(v[i] * sc);  // exact scaling, one rounding
+            lsum += Xi;
+            int r = Xi;
+#pragma unroll
+            for (int d = 3; d >= 0; d--) {
+                dg[d][i >> 2] |= ((uint32_t)r & 0xFFu) << (8 * (i & 3));
+                r = (r + 128) >> 8;
+            }
+        }
+        float* us = reinterpret_cast<float*>(base + 1024 + I8Block<D>::sf);
+        if constexpr (D == kQ4_K) {
+            const int s = lane >> 2, tt = lane & 3;  // sub-block s, elements 8tt..
+            uint2* xq = reinterpret_cast<uint2*>(base);
+#pragma unroll
+            for (int d = 0; d < 4; d++) xq[(s * 4 + tt) * 4 + d] = make_uint2(dg[d][0], dg[d][1]);
+            lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
+            lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);  // lanes 4s..4s+3: S_s
+            const float S = (float)lsum * 4.76837158203125e-07f;  // 2^-21
+            const float So = __shfl_down_sync(0xffffffffu, S, 4);  // S_{s+1}
+            if ((lane & 7) == 0) {  // s even: the pair for k-slots 2t', 2t'+1, t' = s / 2
+                uint32_t hi, lo;
+                split2(S, So, hi, lo);
+                uint32_t* sf = reinterpret_cast<uint32_t*>(base + 1024);
+                sf[(lane >> 3) * 2] = hi;
+                sf[(lane >> 3) * 2 + 1] = lo;
+            }
+        } else {
+            // lane L: h = L / 16, grp = (L % 16) / 4, half = (L % 4) / 2, elements 8 (L % 2)..
+            const int h = lane >> 4, grp = (lane >> 2) & 3, half = (lane >> 1) & 1, tt = 2 * (lane & 1);
+            const int j = (2 * h + half) * 4 + grp;
+            uint32_t* xq = reinterpret_cast<uint32_t*>(base);
+#pragma unroll
+            for (int d = 0; d < 4; d++) {
+                xq[(j * 4 + tt) * 4 + d] = dg[d][0];
+                xq[(j * 4 + tt + 1) * 4 + d] = dg[d][1];
+            }
+            lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);  // lanes L, L^1: S_j
+            const float S = (float)lsum * 4.76837158203125e-07f;
+            const float So = __shfl_down_sync(0xffffffffu, S, 4);  // group j + 1 (grp + 1)
+            if ((lane & 1) == 0 && (grp & 1) == 0) {
+                const int tp = (j & 7) >> 1, reg = j >> 3;  // pair (j, j+1) -> b0 (j < 8) or b1
+                uint32_t hi, lo;
+                split2(S, So, hi, lo);
+                uint32_t* sf = reinterpret_cast<uint32_t*>(base + 1024);
+                sf[(tp * 2) * 2 + reg] = hi;
+                sf[(tp * 2 + 1) * 2 + reg] = lo;
+            }
+        }
+        if (lane == 0) *us = __uint_as_float((uint32_t)(127 - e) << 23);
+    }
+}
+
+// Per-lane constants of the i8 product.  Lane (g, t) reads B column g = token
+// g / 4 (clamped to the staged tokens), digit g % 4; its accumulators are
+// columns 2t, 2t+1 = token t / 2, digits (3, 2) or (1, 0); the correction MMA's
+// columns 2t, 2t+1 are token t's hi and lo parts.  Tokens that do not exist
+// read token 0's block and their results are dropped.
+struct I8Lane {
+    int t, g;
+    float wa, wb;       // weights of the lane's two digit columns
+    uint32_t m_sel;     // Q4_K: prmt selector of bytes (2t, 2t+1) of the 8 min bytes
+    uint32_t s_sel;     // Q6_K: bytes t/2 and t/2 + 2 of a word, each under a magic byte
+    int xb, xm;         // byte offsets of this lane's B column and correction column blocks
+    int ua, um;         // byte offsets of the unscale of token t/2 and of token t
+};
+
+template <int D>
+__device__ __forceinline__ I8Lane i8_lane(int ntok) {
+    I8Lane L;
+    const int lane = threadIdx.x & 31;
+    constexpr int TB = I8Block<D>::bytes;
+    L.t = lane & 3;
+    L.g = lane >> 2;
+    L.wa = (L.t & 1) ? 256.f : 16777216.f;
+    L.wb = (L.t & 1) ? 1.f : 65536.f;
+    L.m_sel = (uint32_t)(2 * L.t) | ((uint32_t)(2 * L.t + 1) << 4);
+    const uint32_t b0 = (uint32_t)(L.t >> 1), b1 = b0 + 2;
+    L.s_sel = b0 | (4u << 4) | (b1 << 8) | (4u << 12);
+    const int tb = min(L.g >> 2, ntok - 1), tm = min(L.g >> 1, ntok - 1);
+    const int dgt = L.g & 3, part = L.g & 1;
+    if constexpr (D == kQ4_K) {
+        L.xb = tb * TB + (L.t * 4 + dgt) * 8;
+        L.xm = tm * TB + 1024 + (L.t * 2 + part) * 4;
+    } else {
+        L.xb = tb * TB + (L.t * 4 + dgt) * 4;
+        L.xm = tm * TB + 1024 + (L.t * 2 + part) * 8;
+    }
+    L.ua = min(L.t >> 1, ntok - 1) * TB + 1024 + I8Block<D>::sf;
+    L.um = min(L.t, ntok - 1) * TB + 1024 + I8Block<D>::sf;
+    return L;
+}
+
+// Unsigned / sign-extended byte B of W, one permute each.
+__device__ __forceinline__ int ubyte(uint32_t w, int b) { return (int)prmt(w, 0u, 0x4440u | (uint32_t)b); }
+__device__ __forceinline__ int sbyte(uint32_t w, int b) {
+    const uint32_t s = 8u | (uint32_t)b;
+    return (int)prmt(w, 0u, (uint32_t)b | (s << 4) | (s << 8) | (s << 12));
+}
+
+// Q4_K, one chunk: HD[h] = 16-byte header of row g + 8h; CW[h][j] = bytes
+// 8t..8t+7 of code group j; XS = the chunk's first staged block.  Adds to accm
+// (digit-weighted, token t/2) and accn (min term of token t, to be subtracted).
+__device__ __forceinline__ void q4k_i8_chunk(const I8Lane& L, const uint32_t (&HD)[2][4], const uint2 (&CW)[2][4],
+                                             const unsigned char* xs, float (&accm)[2], float (&accn)[2]) {
+    const unsigned char* xb = xs + L.xb;
+    uint32_t sc03[2], sc47[2], m03[2], m47[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        sc03[h] = HD[h][1] & 0x3F3F3F3Fu;
+        sc47[h] = (HD[h][3] & 0x0F0F0F0Fu) | ((HD[h][1] >> 2) & 0x30303030u);
+        m03[h] = HD[h][2] & 0x3F3F3F3Fu;
+        m47[h] = ((HD[h][3] >> 4) & 0x0F0F0F0Fu) | ((HD[h][2] >> 2) & 0x30303030u);
+    }
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+#pragma unroll
+        for (int hn = 0; hn < 2; hn++) {  // low nibbles: sub-block 2j; high: 2j + 1
+            const int s = 2 * j + hn;
+            const uint32_t a0 = hn ? (CW[0][j].x >> 4) & 0x0F0F0F0Fu : CW[0][j].x & 0x0F0F0F0Fu;
+            const uint32_t a2 = hn ? (CW[0][j].y >> 4) & 0x0F0F0F0Fu : CW[0][j].y & 0x0F0F0F0Fu;
+            const uint32_t a1 = hn ? (CW[1][j].x >> 4) & 0x0F0F0F0Fu : CW[1][j].x & 0x0F0F0F0Fu;
+            const uint32_t a3 = hn ? (CW[1][j].y >> 4) & 0x0F0F0F0Fu : CW[1][j].y & 0x0F0F0F0Fu;
+            const uint2 b = *reinterpret_cast<const uint2*>(xb + s * 128);
+            int c[4];
+            imma_k32(c, a0, a1, a2, a3, b.x, b.y);
+            const int s0 = ubyte(s < 4 ? sc03[0] : sc47[0], s & 3);
+            const int s1 = ubyte(s < 4 ? sc03[1] : sc47[1], s & 3);
+            acc[0] += s0 * c[0];
+            acc[1] += s0 * c[1];
+            acc[2] += s1 * c[2];
+            acc[3] += s1 * c[3];
+        }
+    }
+    // min term: A = (m_{2t}, m_{2t+1}) per row, k-slots 8.. are zero
+    uint32_t am[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) am[h] = hsub2(prmt(prmt(m03[h], m47[h], L.m_sel), kMagic, kSelLo), kH1024);
+    float cm[4] = {0.f, 0.f, 0.f, 0.f};
+    mma16816(cm, am[0], am[1], 0u, 0u, *reinterpret_cast<const uint32_t*>(xs + L.xm), 0u);
+    const float ut = *reinterpret_cast<const float*>(xs + L.ua);
+    const float umin = *reinterpret_cast<const float*>(xs + L.um) * 2097152.f;  // times 2^21
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const float d = lo_half(HD[h][0]), dm = hi_half(HD[h][0]);
+        const float f = fmaf((float)acc[2 * h], L.wa, (float)acc[2 * h + 1] * L.wb);
+        accm[h] = fmaf(d * ut, f, accm[h]);
+        accn[h] = fmaf(dm * umin, cm[2 * h] + cm[2 * h + 1], accn[h]);
+    }
+}
+
+// Q6_K, one chunk: QW[h][12] = this lane's 48 code bytes of row g + 8h (the
+// lane-major plane: per (h, half) words ql lo, ql hi, qh); SW[h] = the 16 int8
+// sub-scales; DB[h] = fp16 d bits.  Adds the main term to accm and the offset
+// term 32 d sum_j sc_j S_j (to be subtracted) to accn.
+__device__ __forceinline__ void q6k_i8_chunk(const I8Lane& L, const uint32_t (&QW)[2][12], const uint4 (&SW)[2],
+                                             const uint32_t (&DB)[2], const unsigned char* xs, float (&accm)[2],
+                                             float (&accn)[2]) {
+    const unsigned char* xb = xs + L.xb;
+    const uint32_t sw[2][4] = {{SW[0].x, SW[0].y, SW[0].z, SW[0].w}, {SW[1].x, SW[1].y, SW[1].z, SW[1].w}};
+    int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int hh = 0; hh < 4; hh++) {  // (h, half)
+        const int h6 = hh >> 1, half = hh & 1;
+        uint32_t q[2][4];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const uint32_t W0 = QW[r][3 * hh], W1 = QW[r][3 * hh + 1], QH = QW[r][3 * hh + 2];
+            q[r][0] = (W0 & 0x0F0F0F0Fu) | ((QH << 4) & 0x30303030u);
+            q[r][1] = (W1 & 0x0F0F0F0Fu) | ((QH << 2) & 0x30303030u);
+            q[r][2] = ((W0 >> 4) & 0x0F0F0F0Fu) | (QH & 0x30303030u);
+            q[r][3] = ((W1 >> 4) & 0x0F0F0F0Fu) | ((QH >> 2) & 0x30303030u);
+        }
+#pragma unroll
+        for (int grp = 0; grp < 4; grp++) {
+            const int j = hh * 4 + grp;
+            int c[4];
+            imma_k16(c, q[0][grp], q[1][grp], *reinterpret_cast<const uint32_t*>(xb + j * 64));
+            const int idx = 8 * h6 + 2 * grp + half;  // sub-scale of this group
+            const int s0 = sbyte(sw[0][idx >> 2], idx & 3), s1 = sbyte(sw[1][idx >> 2], idx & 3);
+            acc[0] += s0 * c[0];
+            acc[1] += s0 * c[1];
+            acc[2] += s1 * c[2];
+            acc[3] += s1 * c[3];
+        }
+    }
+    // offset term: A[row][j] = sc of group j; a0: j = 2t, 2t+1 -> bytes t/2, t/2 + 2 of
+    // word t & 1; a2: j = 8 + 2t, 9 + 2t -> same bytes of word 2 + (t & 1)
+    uint32_t a[2][2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const bool odd = (L.t & 1) != 0;  // a select, not an index: keeps sw in registers
+        a[r][0] = hsub2(prmt((odd ? sw[r][1] : sw[r][0]) ^ 0x80808080u, kMagic, L.s_sel), kH1152);
+        a[r][1] = hsub2(prmt((odd ? sw[r][3] : sw[r][2]) ^ 0x80808080u, kMagic, L.s_sel), kH1152);
+    }
+    const uint2 bs = *reinterpret_cast<const uint2*>(xs + L.xm);
+    float co[4] = {0.f, 0.f, 0.f, 0.f};
+    mma16816(co, a[0][0], a[1][0], a[0][1], a[1][1], bs.x, bs.y);
+    const float ut = *reinterpret_cast<const float*>(xs + L.ua);
+    const float uo = *reinterpret_cast<const float*>(xs + L.um) * 67108864.f;  // times 32 * 2^21
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const float d = __half2float(__ushort_as_half((unsigned short)DB[h]));
+        const float f = fmaf((float)acc[2 * h], L.wa, (float)acc[2 * h + 1] * L.wb);
+        accm[h] = fmaf(d * ut, f, accm[h]);
+        accn[h] = fmaf(d * uo, co[2 * h] + co[2 * h + 1], accn[h]);
+    }
+}
+
+// End of a tile: lane (g, t) holds accm for token t/2 (its digit half) and
+// accn for token t.  Returns the row g + 8h sum for token t/2 (lanes with even
+// t hold it; odd lanes return the same value).
+__device__ __forceinline__ float i8_finish(const I8Lane& L, float accm, float accn) {
+    const float m = accm + __shfl_xor_sync(0xffffffffu, accm, 1);
+    const int lane = threadIdx.x & 31;
+    const float n = __shfl_sync(0xffffffffu, accn, (lane & ~3) | (L.t >> 1));
+    return m - n;
+}
+
+}  // namespace
+}  // namespace clq

@@ -62,6 +62,12 @@ int clq_abi_version(void);
 int clq_last_error(char *buf, size_t len);
 /* Elements and bytes per block of DTYPE. */
 int clq_block_geometry(int dtype, int64_t *elements, int64_t *block_bytes);
+/* No counterpart in the reference (its kernels run on the calling thread).
+ * Waits for all work on the current device, then stores in *STATUS the code a
+ * kernel recorded since the last call -- CLQ_OK, or CLQ_ERR_TIMEOUT when a
+ * pipeline wait inside a kernel expired (that launch's outputs are invalid, and
+ * launches that run while the code is set may stop early) -- and clears it. */
+int clq_device_status(int *status);
 
 /* ---- drop-in kernels ------------------------------------------------------
  * Same arguments and meaning as the trivial-simd kernels the packed dtypes

@@ -73,6 +73,9 @@ def test_calls_needing_a_device_fail_loudly_without_one(clq):
     with pytest.raises(clq.ClqError) as err:
         clq.linear(x.reshape(1, 256), clq.make_tensor_view(clq.make_q4_k_storage(w), (2, 256)))
     assert err.value.status == "CLQ_ERR_NO_DEVICE"
+    status = ctypes.c_int(-1)
+    assert lib.clq_device_status(ctypes.byref(status)) == 8
+    assert status.value == 0
 
 
 def test_cache_starts_empty_and_forget_is_safe(clq):
