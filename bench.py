@@ -319,7 +319,7 @@ def run_clq(args):
     step_flops = sum(2.0 * m * st.n * st.k for (_, st, *_r) in stores)
     traffic = None
     tfile = ROOT / "profiles" / "q4k_gemv_traffic.json"
-    if tfile.exists():
+    if tfile.exists() and world == 1 and m == 1 and args.model == "8b":  # the capture's shapes
         traffic = json.loads(tfile.read_text()).get("dram_bytes_per_launch_8b_step_avg")
 
     # ---- end to end -------------------------------------------------------------
@@ -454,6 +454,15 @@ def e2e_tp(args, torch, dist, graph, inputs, logits, job_bytes):
             "steps": steps}
 
 
+def host_threads():
+    """Every host core this process may run on (torchrun sets OMP_NUM_THREADS=1,
+    so OpenMP's own default would undercount)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def cpu_sample(tp, cfg, m):
     """One decoder layer's seven linears at full size, host bytes (numpy seeded)."""
     import numpy as np
@@ -482,7 +491,7 @@ def time_cpu(sample, nbytes, seconds, threads):
 def cpu_baseline(args, tp, cfg, m):
     import oracle
     sample, nbytes = cpu_sample(tp, cfg, m)
-    threads = oracle.max_threads()
+    threads = host_threads()
     gbs, runs, el = time_cpu(sample, nbytes, args.cpu_seconds, threads)
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
             "sample": f"one layer's 7 linears ({nbytes/1e6:.1f} MB) x {runs} in {el:.1f} s, "
@@ -498,7 +507,7 @@ def run_reference(args):
     import oracle
     cfg = tp.LLAMA3_8B if args.model == "8b" else tp.LLAMA3_70B
     sample, nbytes = cpu_sample(tp, cfg, args.m)
-    threads = oracle.max_threads()
+    threads = host_threads()
     for _ in range(args.warmup):
         for dtype, n, k, data, x in sample[:1]:
             oracle.matmul_f32(dtype, x, data, n, threads)

@@ -1,7 +1,7 @@
 // pipeline.cuh -- shared-memory pipelines fed by the bulk-copy (TMA) engine:
 // mbarrier set-up, arrival, bounded waits, and 1-D cp.async.bulk copies from
-// global to shared memory.  No tensor maps and no cluster multicast: every
-// copy reads this GPU's own memory into this CTA's shared memory.
+// global to shared memory.  No tensor maps; every copy has one destination,
+// this CTA's shared memory, and reads this GPU's own memory.
 //
 // Every wait is bounded.  When a wait gives up it sets the sticky error word
 // (the library's device status, read by clq_device_status) and returns false;
