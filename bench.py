@@ -31,6 +31,28 @@ for _p in (ROOT, ROOT / "oracle"):
 
 METRIC = "quant GEMV HBM GB/s (%peak) + 8B-shape Q4_K decode tok/s @1/2/4/8 GPU"
 FALLBACK_HBM_GBS = 6650.0
+
+# GEMV sweeps (one GPU): (dtype, out rows, in columns) per shape.  A step runs
+# every shape once over distinct weight copies, enough copies that the step's
+# weights exceed four times the 126 MB L2.
+SWEEPS = {
+    "q8_0-4096": [("q8_0", 4096, 4096)],
+    "q4-llama32-1b": [(d, n, k) for d in ("q4_0", "q4_k")
+                      for n, k in ((2048, 2048), (512, 2048), (8192, 2048), (8192, 2048), (2048, 8192))],
+    "q6k-vocab-qwen3-8b": [("q6_k", 128256, 4096)] + [("q6_k", n, k) for n, k in
+                           ((4096, 4096), (1024, 4096), (1024, 4096), (12288, 4096), (12288, 4096), (4096, 12288))],
+}
+
+
+def workload_linears(args, tp, cfg):
+    """(name, dtype, n, k, tp kind, input buffer) of one step of the workload."""
+    if args.workload == "step":
+        return tp.model_linears(cfg)
+    shapes = SWEEPS[args.workload]
+    once = sum(tp.weight_bytes(d, n, k) for d, n, k in shapes)
+    copies = max(1, -(-4 * 126 * 2**20 // once))
+    return [(f"{d}.{n}x{k}.{c}.{i}", d, n, k, "rows", f"k{k}")
+            for c in range(copies) for i, (d, n, k) in enumerate(shapes)]
 FALLBACK_BF16_TFLOPS = 1590.0
 
 
@@ -41,6 +63,9 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["clq", "reference"], default="clq")
     ap.add_argument("--model", choices=["8b", "70b"], default="8b")
+    ap.add_argument("--workload", choices=["step"] + sorted(SWEEPS), default="step",
+                    help="step: every linear of one decode step of --model (the headline); "
+                         "q8_0-4096 / q4-llama32-1b / q6k-vocab-qwen3-8b: GEMV sweeps over those shapes")
     ap.add_argument("--m", type=int, default=1, help="activation rows (tokens) per step")
     ap.add_argument("--xtype", choices=["f32", "bf16", "f16"], default=None,
                     help="activation type; default f32 for decode (M < 64), bf16 for prefill")
@@ -187,7 +212,9 @@ def run_clq(args):
     xtype = args.xtype or ("f32" if m < 64 else "bf16")
     xdtype = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[xtype]
     prefill = m >= 64 and xtype != "f32"
-    linears = tp.model_linears(cfg)
+    if args.workload != "step" and world > 1:
+        raise SystemExit("GEMV sweeps run on one GPU")
+    linears = workload_linears(args, tp, cfg)
     q_dim = cfg["heads"] * cfg["head_dim"]
 
     # ---- this rank's shards --------------------------------------------------
@@ -206,23 +233,26 @@ def run_clq(args):
     gen.manual_seed(7)
     attn_cols = tp.split(q_dim, world, rank, 256)
     ffn_cols = tp.split(cfg["ffn"], world, rank, 256)
-    inputs = {
-        "hidden": torch.randn(m, cfg["hidden"], device="cuda", generator=gen),
-        "attn": torch.randn(m, attn_cols[1] - attn_cols[0], device="cuda", generator=gen),
-        "ffn": torch.randn(m, ffn_cols[1] - ffn_cols[0], device="cuda", generator=gen),
-    }
+    widths = {"hidden": cfg["hidden"], "attn": attn_cols[1] - attn_cols[0], "ffn": ffn_cols[1] - ffn_cols[0]}
+    for (_, st, dt, kind, src, name) in stores:
+        widths.setdefault(src, st.k)
+    inputs = {src: torch.randn(m, w, device="cuda", generator=gen) for src, w in widths.items()}
     inputs = {key: v.to(xdtype) for key, v in inputs.items()}
+    x_bytes = inputs[stores[0][4]].element_size()
     outs = [torch.empty(m, st.n, device="cuda") for (_, st, *_r) in stores]
     logits = torch.empty(world, m, stores[-1][1].n, device="cuda")
     # one launch per group of linears reading the same activations: per layer
     # (q, k, v), (o), (gate, up), (down); then the output head
     groups, i = [], 0
-    per_layer = len(tp.layer_linears(cfg))
-    for layer in range(cfg["layers"]):
-        base = layer * per_layer
-        for members in ((0, 1, 2), (3,), (4, 5), (6,)):
-            groups.append([base + j for j in members])
-    groups.append([len(stores) - 1])
+    if args.workload == "step":
+        per_layer = len(tp.layer_linears(cfg))
+        for layer in range(cfg["layers"]):
+            base = layer * per_layer
+            for members in ((0, 1, 2), (3,), (4, 5), (6,)):
+                groups.append([base + j for j in members])
+        groups.append([len(stores) - 1])
+    else:
+        groups = [[j] for j in range(len(stores))]
     launches_per_step = len(groups)
 
     def run_group(idx):
@@ -243,7 +273,7 @@ def run_clq(args):
 
     # algorithmic bytes (W + x + out) of this rank's step, summed over ranks
     def lin_bytes(st, dtype):
-        return tp.weight_bytes(dtype, st.n, st.k) + inputs["hidden"].element_size() * m * st.k + 4 * m * st.n
+        return tp.weight_bytes(dtype, st.n, st.k) + x_bytes * m * st.k + 4 * m * st.n
     step_bytes = float(sum(lin_bytes(st, dt) for (_, st, dt, *_r) in stores))
     if dist is not None:
         t = torch.tensor([step_bytes], dtype=torch.float64, device="cuda")
@@ -297,7 +327,11 @@ def run_clq(args):
     peak, peak_kind = peaks()
 
     # ---- dominant kernel: the Q4_K GEMV launches alone, back to back ----------
-    q4k_groups = [idx for idx in groups if stores[idx[0]][2] == "q4_k"]
+    by_dtype = {}
+    for (_, st, dt, *_r) in stores:
+        by_dtype[dt] = by_dtype.get(dt, 0) + tp.weight_bytes(dt, st.n, st.k)
+    top = "q4_k" if "q4_k" in by_dtype and args.workload == "step" else max(by_dtype, key=by_dtype.get)
+    q4k_groups = [idx for idx in groups if stores[idx[0]][2] == top]
     kgraph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(kgraph):
         for idx in q4k_groups:
@@ -313,7 +347,7 @@ def run_clq(args):
     ke.record()
     torch.cuda.synchronize()
     k_ms = ks.elapsed_time(ke) / (reps * len(q4k_groups))
-    k_bytes = sum(lin_bytes(stores[j][1], "q4_k") for idx in q4k_groups for j in idx) / len(q4k_groups)
+    k_bytes = sum(lin_bytes(stores[j][1], top) for idx in q4k_groups for j in idx) / len(q4k_groups)
     k_gbs = k_bytes / (k_ms * 1e-3) / 1e9
     k_flops = sum(2.0 * m * stores[j][1].n * stores[j][1].k for idx in q4k_groups for j in idx) / len(q4k_groups)
     step_flops = sum(2.0 * m * st.n * st.k for (_, st, *_r) in stores)
@@ -337,9 +371,11 @@ def run_clq(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
             "config": {
-                "workload": f"llama3-{args.model}-shape Q4_K-M {'prefill' if prefill else 'decode'} linears, "
-                            f"M={m}, {xtype} activations: {cfg['layers']} layers x (q,k,v,o,gate,up Q4_K; "
-                            f"down Q6_K) + Q6_K output",
+                "workload": (f"llama3-{args.model}-shape Q4_K-M {'prefill' if prefill else 'decode'} linears, "
+                             f"M={m}, {xtype} activations: {cfg['layers']} layers x (q,k,v,o,gate,up Q4_K; "
+                             f"down Q6_K) + Q6_K output") if args.workload == "step" else
+                            (f"GEMV sweep {args.workload}: " + ", ".join(f"{d} {n}x{k}" for d, n, k in SWEEPS[args.workload])
+                             + f"; M={m}, {xtype} activations; {len(stores) // len(SWEEPS[args.workload])} weight copies"),
                 "m": m, "xtype": xtype, "layers": cfg["layers"], "parallelism": f"tp{world}",
                 "weights_gb": round(job_bytes / 1e9, 3),
                 "l2": "weights per step far above the 126 MB L2; no flush",
@@ -362,7 +398,8 @@ def run_clq(args):
                 "algorithmic_flops_per_launch": round(k_flops), "us_per_launch": round(k_ms * 1e3, 3)}
         else:
             result["roofline"] = {
-                "bound": "hbm", "kernel": "Q4_K GEMV launches (q/k/v group, o, gate/up group), M=%d" % m,
+                "bound": "hbm", "kernel": ("Q4_K GEMV launches (q/k/v group, o, gate/up group), M=%d" % m)
+                if args.workload == "step" else f"{top.upper()} GEMV launches of the sweep, M={m}",
                 "achieved": round(k_gbs, 1), "peak": peak, "peak_kind": peak_kind,
                 "unit": "GB/s", "frac": round(k_gbs / peak, 4), "traffic": traffic,
                 "algorithmic_bytes_per_launch": round(k_bytes), "us_per_launch": round(k_ms * 1e3, 3)}
@@ -463,12 +500,13 @@ def host_threads():
         return os.cpu_count() or 1
 
 
-def cpu_sample(tp, cfg, m):
-    """One decoder layer's seven linears at full size, host bytes (numpy seeded)."""
-    import numpy as np
+def cpu_sample(tp, cfg, m, workload="step"):
+    """Host bytes (numpy seeded) of a bounded sample of the workload: one decoder
+    layer's seven linears for the decode step, one copy of each shape for a sweep."""
     synth = importlib.import_module("cl-inference_b200.synth")
     sample = []
-    for i, (name, dtype, n, k, kind, src) in enumerate(tp.layer_linears(cfg)):
+    shapes = [(d, n, k) for (_, d, n, k, _, _) in tp.layer_linears(cfg)] if workload == "step" else SWEEPS[workload]
+    for i, (dtype, n, k) in enumerate(shapes):
         data = synth.packed_blocks(dtype, n, k, seed=8000 + i)
         x = synth.activations(m, k, seed=8100 + i)
         sample.append((dtype, n, k, data, x))
@@ -488,13 +526,16 @@ def time_cpu(sample, nbytes, seconds, threads):
             return runs * nbytes / el / 1e9, runs, el
 
 
+def sample_name(workload):
+    return "one layer's 7 linears" if workload == "step" else f"one copy of each {workload} shape"
+
+
 def cpu_baseline(args, tp, cfg, m):
-    import oracle
-    sample, nbytes = cpu_sample(tp, cfg, m)
+    sample, nbytes = cpu_sample(tp, cfg, m, args.workload)
     threads = host_threads()
     gbs, runs, el = time_cpu(sample, nbytes, args.cpu_seconds, threads)
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"one layer's 7 linears ({nbytes/1e6:.1f} MB) x {runs} in {el:.1f} s, "
+            "sample": f"{sample_name(args.workload)} ({nbytes/1e6:.1f} MB) x {runs} in {el:.1f} s, "
                       f"fp32 CPU port of the packed kernel contract, OpenMP"}
 
 
@@ -506,7 +547,7 @@ def run_reference(args):
     tp = importlib.import_module("cl-inference_b200.tp")
     import oracle
     cfg = tp.LLAMA3_8B if args.model == "8b" else tp.LLAMA3_70B
-    sample, nbytes = cpu_sample(tp, cfg, args.m)
+    sample, nbytes = cpu_sample(tp, cfg, args.m, args.workload)
     threads = host_threads()
     for _ in range(args.warmup):
         for dtype, n, k, data, x in sample[:1]:
@@ -526,10 +567,11 @@ def run_reference(args):
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": len(times), "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"llama3-{args.model}-shape Q4_K-M decode linears, M={args.m}; "
-                               "each step one layer's 7 linears (bounded sample)", "m": args.m},
+        "config": {"workload": (f"llama3-{args.model}-shape Q4_K-M decode linears, M={args.m}"
+                                if args.workload == "step" else f"GEMV sweep {args.workload}, M={args.m}")
+                               + f"; each step {sample_name(args.workload)} (bounded sample)", "m": args.m},
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"one layer's 7 linears ({nbytes/1e6:.1f} MB) per step"},
+                         "sample": f"{sample_name(args.workload)} ({nbytes/1e6:.1f} MB) per step"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "cl-inference's CPU kernels (trivial-simd, Common Lisp host) cannot be built here; "
                 "this is the C port of their contract (oracle/clq_oracle.c)",
