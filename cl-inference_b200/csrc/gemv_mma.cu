@@ -38,7 +38,9 @@ struct Params {
 // Launched with programmatic dependent launch: weight loads do not depend on
 // the previous kernel, so only the activation staging waits for it.
 template <int D, typename XT, int MT, int WARPS>
-__global__ void __launch_bounds__(WARPS * 32, 16 / WARPS) gemv_mma_kernel(Params P) {
+// Four token tiles (9-16 activation rows) need more registers than two CTAs of
+// 8 warps leave: one CTA per SM for them.
+__global__ void __launch_bounds__(WARPS * 32, MT >= 4 ? 8 / WARPS : 16 / WARPS) gemv_mma_kernel(Params P) {
     extern __shared__ __align__(16) unsigned char smem[];
     constexpr int NW = Words<D>::n;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -198,7 +200,7 @@ cudaError_t launch_one(const Params& P, cudaStream_t stream) {
     if (pc < 1) pc = 1;
     if (pc > nchunks) pc = nchunks;
     // 16 resident warps per SM; partial sums at most 32 KB
-    const int64_t slots = (16 / WARPS) * (int64_t)sm_count();
+    const int64_t slots = ((MT >= 4 ? 8 : 16) / WARPS) * (int64_t)sm_count();
     int64_t tl = (tiles + slots - 1) / slots;
     const int64_t tl_cap = (32 * 1024) / ((int64_t)WARPS * ntok_max * 16 * 4);
     if (tl > tl_cap) tl = tl_cap;
