@@ -71,6 +71,9 @@ def parse():
                     help="activation type; default f32 for decode (M < 64), bf16 for prefill")
     ap.add_argument("--layers", type=int, default=None,
                     help="decoder layers per step (default: the model's); fewer for profiling captures")
+    ap.add_argument("--allreduce", choices=["fused", "nccl"], default="fused",
+                    help="tensor parallel: row-parallel linears all-reduce inside the GEMV over NVLink "
+                         "(fused) or through NCCL after it")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -263,8 +266,22 @@ def run_clq(args):
             src = stores[idx[0]][4]
             clq.linear_group([stores[j][0] for j in idx], inputs[src], outs=[outs[j] for j in idx])
 
+    comm = None
+    if dist is not None and args.allreduce == "fused":
+        tpcomm = importlib.import_module("cl-inference_b200.tpcomm")
+
+        def exchange(obj):
+            got = [None] * world
+            dist.all_gather_object(got, obj)
+            return got
+        comm = tpcomm.TpComm(rank, world, exchange, cap=max(4096, 16 * m * (cfg["hidden"] // 16 // 100 + 1)))
+
     def step():
         for idx in groups:
+            if comm is not None and stores[idx[0]][3] == "cols":
+                store = stores[idx[0]][0]
+                comm.linear_allreduce(store, inputs[stores[idx[0]][4]], out=outs[idx[0]])
+                continue
             run_group(idx)
             if dist is not None and stores[idx[0]][3] == "cols":
                 dist.all_reduce(outs[idx[0]])
@@ -363,6 +380,9 @@ def run_clq(args):
             e2e_tp(args, torch, dist, graph, inputs, logits, job_bytes)
 
     del graph, kgraph
+    if comm is not None:
+        torch.cuda.synchronize()
+        comm.close(barrier=dist.barrier)
     result = None
     if rank == 0:
         result = {
@@ -377,6 +397,7 @@ def run_clq(args):
                             (f"GEMV sweep {args.workload}: " + ", ".join(f"{d} {n}x{k}" for d, n, k in SWEEPS[args.workload])
                              + f"; M={m}, {xtype} activations; {len(stores) // len(SWEEPS[args.workload])} weight copies"),
                 "m": m, "xtype": xtype, "layers": cfg["layers"], "parallelism": f"tp{world}",
+                "allreduce": (args.allreduce if world > 1 else None),
                 "weights_gb": round(job_bytes / 1e9, 3),
                 "l2": "weights per step far above the 126 MB L2; no flush",
             },

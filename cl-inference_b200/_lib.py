@@ -48,6 +48,14 @@ SIGNATURES = {
     "clq_linear_device": (_int, [_ptr, _i64, _i64, _ptr, _int, _i64, _ptr, _i64, _u32, _ptr]),
     "clq_linear_group_device": (_int, [_ptr, _ptr, _ptr, _int, _ptr, _int, _i64, _ptr, _ptr, _u32, _ptr]),
     "clq_linear_device_noalloc": (_int, [_ptr, _i64, _i64, _ptr, _int, _i64, _ptr, _i64, _ptr]),
+    "clq_tp_buffers": (_int, [_int, _i64, ctypes.POINTER(_ptr), ctypes.POINTER(_ptr)]),
+    "clq_tp_buffers_free": (_int, [_ptr, _ptr]),
+    "clq_ipc_handle": (_int, [_ptr, _ptr]),
+    "clq_ipc_open": (_int, [_ptr, ctypes.POINTER(_ptr)]),
+    "clq_ipc_close": (_int, [_ptr]),
+    "clq_tp_create": (_int, [_int, _int, _i64, _ptr, _ptr, ctypes.POINTER(_ptr)]),
+    "clq_tp_free": (_int, [_ptr]),
+    "clq_linear_allreduce_device": (_int, [_ptr, _i64, _i64, _ptr, _int, _i64, _ptr, _i64, _ptr, _ptr]),
     "clq_dequantize_device": (_int, [_ptr, _i64, _i64, _ptr, _int, _ptr]),
     "clq_gather_device": (_int, [_ptr, _ptr, _i64, _ptr, _ptr]),
     "clq_dequantize": (_int, [_int, _ptr, _size, _ptr]),

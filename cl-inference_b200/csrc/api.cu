@@ -6,6 +6,7 @@
 #include <cstring>
 #include <memory>
 #include <mutex>
+#include <new>
 #include <string>
 #include <vector>
 
@@ -665,3 +666,131 @@ extern "C" int clq_linear_device_noalloc(const clq_store* w, int64_t row_begin, 
     if (e != cudaSuccess) return cuda_fail(e, "prefill kernel launch");
     return CLQ_OK;
 }
+
+// ---- tensor-parallel groups: GEMV with the all-reduce over peer memory ------
+
+struct clq_tp {
+    clq::TpLink link;
+    int device;
+};
+
+namespace {
+
+size_t tp_recv_bytes(int world, int64_t cap) { return (size_t)2 * world * clq::kMaxTpCtas * cap * sizeof(uint2); }
+constexpr size_t kTpFlagBytes = clq::kMaxTpCtas * sizeof(uint32_t);  // per-CTA call epochs
+
+}  // namespace
+
+extern "C" {
+
+int clq_tp_buffers(int world, int64_t cap, void** recv, void** flags) {
+    if (!recv || !flags) return fail(CLQ_ERR_ARGUMENT, "null result pointer");
+    *recv = *flags = nullptr;
+    if (world < 1 || world > clq::kMaxRanks) return fail(CLQ_ERR_ARGUMENT, "world %d outside 1..%d", world, clq::kMaxRanks);
+    if (cap < 1) return fail(CLQ_ERR_ARGUMENT, "capacity %lld", (long long)cap);
+    int device, rc;
+    if ((rc = current_device(&device))) return rc;
+    cudaError_t e = cudaMalloc(recv, tp_recv_bytes(world, cap));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(tensor-parallel recv)");
+    if ((e = cudaMalloc(flags, kTpFlagBytes)) != cudaSuccess) {
+        cudaFree(*recv);
+        *recv = nullptr;
+        return cuda_fail(e, "cudaMalloc(tensor-parallel flags)");
+    }
+    if ((e = cudaMemset(*recv, 0, tp_recv_bytes(world, cap))) != cudaSuccess ||
+        (e = cudaMemset(*flags, 0, kTpFlagBytes)) != cudaSuccess || (e = cudaDeviceSynchronize()) != cudaSuccess) {
+        cudaFree(*recv);
+        cudaFree(*flags);
+        *recv = *flags = nullptr;
+        return cuda_fail(e, "clearing tensor-parallel buffers");
+    }
+    return CLQ_OK;
+}
+
+int clq_tp_buffers_free(void* recv, void* flags) {
+    cudaError_t e = cudaSuccess;
+    if (recv) e = cudaFree(recv);
+    if (flags && e == cudaSuccess) e = cudaFree(flags);
+    return e == cudaSuccess ? CLQ_OK : cuda_fail(e, "cudaFree(tensor-parallel buffers)");
+}
+
+int clq_ipc_handle(const void* dev_ptr, uint8_t* handle) {
+    if (!dev_ptr || !handle) return fail(CLQ_ERR_ARGUMENT, "null pointer");
+    cudaIpcMemHandle_t h;
+    cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(dev_ptr));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+    static_assert(sizeof(h) == 64, "IPC handles are 64 bytes");
+    std::memcpy(handle, &h, sizeof h);
+    return CLQ_OK;
+}
+
+int clq_ipc_open(const uint8_t* handle, void** dev_ptr) {
+    if (!dev_ptr || !handle) return fail(CLQ_ERR_ARGUMENT, "null pointer");
+    *dev_ptr = nullptr;
+    int device, rc;
+    if ((rc = current_device(&device))) return rc;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof h);
+    cudaError_t e = cudaIpcOpenMemHandle(dev_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+    return CLQ_OK;
+}
+
+int clq_ipc_close(void* dev_ptr) {
+    if (!dev_ptr) return CLQ_OK;
+    cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+    return e == cudaSuccess ? CLQ_OK : cuda_fail(e, "cudaIpcCloseMemHandle");
+}
+
+int clq_tp_create(int rank, int world, int64_t cap, void* const* recv, void* const* flags, clq_tp** out) {
+    if (!out || !recv || !flags) return fail(CLQ_ERR_ARGUMENT, "null pointer");
+    *out = nullptr;
+    if (world < 1 || world > clq::kMaxRanks || rank < 0 || rank >= world)
+        return fail(CLQ_ERR_ARGUMENT, "rank %d of world %d (1..%d ranks)", rank, world, clq::kMaxRanks);
+    if (cap < 1) return fail(CLQ_ERR_ARGUMENT, "capacity %lld", (long long)cap);
+    for (int r = 0; r < world; r++)
+        if (!recv[r] || !flags[r]) return fail(CLQ_ERR_ARGUMENT, "null buffer of rank %d", r);
+    int device, rc;
+    if ((rc = current_device(&device))) return rc;
+    clq_tp* t = new (std::nothrow) clq_tp();
+    if (!t) return fail(CLQ_ERR_OUT_OF_MEMORY, "tensor-parallel group");
+    t->device = device;
+    clq::TpLink& L = t->link;
+    L.rank = rank;
+    L.world = world;
+    L.cap = cap;
+    for (int r = 0; r < world; r++) L.peer_recv[r] = static_cast<uint2*>(recv[r]);
+    L.my_recv = L.peer_recv[rank];
+    L.epochs = static_cast<uint32_t*>(flags[rank]);
+    *out = t;
+    return CLQ_OK;
+}
+
+int clq_tp_free(clq_tp* tp) {
+    delete tp;
+    return CLQ_OK;
+}
+
+int clq_linear_allreduce_device(const clq_store* w, int64_t row_begin, int64_t rows, const void* x, int xtype,
+                                int64_t m, float* out, int64_t ldo, clq_tp* tp, void* stream) {
+    if (!w || !tp) return fail(CLQ_ERR_ARGUMENT, "null store or group");
+    if (xtype != CLQ_X_F32 && xtype != CLQ_X_BF16 && xtype != CLQ_X_F16)
+        return fail(CLQ_ERR_ARGUMENT, "unknown activation type %d", xtype);
+    if (row_begin < 0 || rows < 1 || row_begin + rows > w->n || m < 1 || ldo < rows)
+        return fail(CLQ_ERR_SHAPE, "rows [%lld, %lld), m %lld, ldo %lld for a (%lld %lld) weight", (long long)row_begin,
+                    (long long)(row_begin + rows), (long long)m, (long long)ldo, (long long)w->n, (long long)w->k);
+    if (!x || !out) return fail(CLQ_ERR_ARGUMENT, "null activation or output pointer");
+    int device, rc;
+    if ((rc = current_device(&device))) return rc;
+    if (device != w->device || device != tp->device)
+        return fail(CLQ_ERR_ARGUMENT, "store, group and current device differ");
+    cudaError_t e = clq::launch_gemv_bulk_allreduce(view_of(w, row_begin), rows, x, xtype, m, out, ldo, tp->link,
+                                                    (cudaStream_t)stream);
+    if (e == cudaErrorNotSupported)
+        return fail(CLQ_ERR_UNSUPPORTED,
+                    "the fused all-reduce GEMV takes Q4_K / Q6_K, K %% 256 == 0, m <= 8, and at most CAP outputs per SM");
+    if (e != cudaSuccess) return cuda_fail(e, "all-reduce linear kernel launch");
+    return CLQ_OK;
+}
+
+}  // extern "C"

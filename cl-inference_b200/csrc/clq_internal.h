@@ -51,6 +51,26 @@ bool gemv_pdl_enabled();
 cudaError_t launch_gemv_bulk_group(const WeightView* const* w, const int64_t* rows, int count, const void* x,
                                    int xtype, int64_t m, float* const* out, const int64_t* ldo,
                                    cudaStream_t stream);
+// Peer-memory links of one rank of a tensor-parallel group (max 8 ranks), for
+// the GEMV whose epilogue all-reduces over NVLink.  recv buffers hold 8-byte
+// (epoch, value) words, [2 parities][world writer ranks][kMaxTpCtas][cap]: a
+// fixed region per CTA index, written and read only by that CTA index on every
+// rank.  epochs holds one call counter per CTA index (local only).
+constexpr int kMaxRanks = 8;
+constexpr int kMaxTpCtas = 160;
+struct TpLink {
+    uint2* peer_recv[kMaxRanks];    // each rank's recv buffer, mapped here
+    uint2* my_recv;
+    uint32_t* epochs;               // [kMaxTpCtas]
+    int rank, world;
+    int64_t cap;                    // words per (parity, writer, CTA) region
+};
+// out = sum over ranks of x_r W_r^T (the row-parallel shard product of each
+// rank), computed by the bulk GEMV with the reduction over peer memory fused
+// into its epilogue.  cudaErrorNotSupported for shapes it does not take.
+cudaError_t launch_gemv_bulk_allreduce(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
+                                       float* out, int64_t ldo, const TpLink& tp, cudaStream_t stream);
+
 // Device address of the current device's sticky status word (0 = no kernel
 // reported a problem; else a CLQ_ERR_* code), or nullptr if it cannot be found.
 int* device_status_word();

@@ -68,7 +68,21 @@ struct BulkParams {
     uint32_t stage_bytes, qs, ds, d_off;          // one stage: row strides and d-region offset
     uint32_t x_off, part_off, acc_off, ring_off;  // shared-memory regions
     int* err;
+    int tp_on;         // all-reduce the output over the ranks of tp (single weight only)
+    TpLink tp;
 };
+
+// One 8-byte (epoch, value) word to / from another GPU's memory: the store and
+// the load are single-copy atomic, so a word carrying the expected epoch also
+// carries its value -- no fences or flags.
+__device__ __forceinline__ void st_word(uint2* p, uint32_t ep, float v) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(ep), "r"(__float_as_uint(v)) : "memory");
+}
+__device__ __forceinline__ uint2 ld_word(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+    return v;
+}
 
 template <int D>
 __device__ __forceinline__ void stage_words(const unsigned char* st, const BulkParams& P, int r, int ci, int t,
@@ -162,6 +176,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + kMaxStages;
     int* issued_sh = reinterpret_cast<int*>(empty + kMaxStages);
+    uint32_t* tp_sh = reinterpret_cast<uint32_t*>(issued_sh + 1);  // this CTA's epoch for the call
     unsigned char* ring = smem + P.ring_off;
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -238,7 +253,10 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
             const int c0 = pass * P.pc;
             const int pcn = min(P.pc, nchunks - c0);
             const int nks = (pcn + kCW - 1) / kCW;
-            if (pass == 0) grid_dependency_wait();        // activations may come from the previous kernel
+            if (pass == 0) {
+                grid_dependency_wait();  // activations may come from the previous kernel
+                if (P.tp_on && threadIdx.x == 0) tp_sh[0] = P.tp.epochs[blockIdx.x] + 1u;
+            }
             else __syncthreads();                         // everyone is done with the previous pass's x
             if constexpr (I8) stage_x_i8<D, XT, kCW>(P.x, P.k, P.x_aligned, c0, pcn, ntok, xstage);
             else stage_x<D, XT, kCW>(P.x, P.k, P.x_aligned, P.pc, c0, pcn, 0, ntok, xf, us, sxf);
@@ -368,7 +386,16 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
                     }
                     const Member& M = P.mem[member_of(P, (int64_t)tile)];
                     const int64_t row = (int64_t)(tile - (int)M.tile_begin) * 16 + (idx & 15);
-                    if (ok && row < M.rows) M.out[(int64_t)(idx >> 4) * M.ldo + row] = sum;
+                    if (!ok || row >= M.rows) continue;
+                    if (P.tp_on) {  // this rank's partial, into this CTA's region of every rank
+                        const uint32_t ep = tp_sh[0];
+                        const int64_t off =
+                            (((int64_t)(ep & 1u) * P.tp.world + P.tp.rank) * kMaxTpCtas + blockIdx.x) * P.tp.cap +
+                            (int64_t)(tile - t_begin) * ntok * 16 + idx;
+                        for (int q = 0; q < P.tp.world; q++) st_word(P.tp.peer_recv[q] + off, ep, sum);
+                    } else {
+                        M.out[(int64_t)(idx >> 4) * M.ldo + row] = sum;
+                    }
                 }
                 par ^= 1;
             }
@@ -376,6 +403,39 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
     }
 
 #undef CLQ_SIDE_FETCH
+    if (P.tp_on) {
+        // ---- all-reduce over the ranks: every rank partitions the tiles the
+        // same way, so this CTA's counterparts on the other ranks produce the
+        // same outputs; wait for their words (bounded) and sum in rank order ----
+        __syncthreads();
+        const uint32_t ep = tp_sh[0];
+        const Member& M = P.mem[0];
+        const uint2* slots = P.tp.my_recv + ((int64_t)(ep & 1u) * P.tp.world * kMaxTpCtas + blockIdx.x) * P.tp.cap;
+        const int64_t rank_stride = (int64_t)kMaxTpCtas * P.tp.cap;
+        const int64_t per_tile = (int64_t)ntok * 16;
+        const int64_t n_el = (int64_t)(t_end - t_begin) * per_tile;
+        for (int64_t i = threadIdx.x; i < n_el; i += blockDim.x) {
+            const int tile = t_begin + (int)(i / per_tile);
+            const int idx = (int)(i - (int64_t)(tile - t_begin) * per_tile);
+            const int64_t row = (int64_t)(tile - (int)M.tile_begin) * 16 + (idx & 15);
+            if (row >= M.rows) continue;
+            float sum = 0.f;
+            for (int q = 0; q < P.tp.world; q++) {  // fixed rank order
+                const uint2* src = slots + q * rank_stride + i;
+                uint2 w = ld_word(src);
+                for (uint32_t it = 0; w.x != ep && it < (1u << 22); it++) {
+                    if (*(volatile int*)P.err) break;
+                    if (it > 32) __nanosleep(32);
+                    w = ld_word(src);
+                }
+                if (w.x != ep) atomicExch(P.err, CLQ_ERR_TIMEOUT);
+                sum += __uint_as_float(w.y);
+            }
+            M.out[(int64_t)(idx >> 4) * M.ldo + row] = sum;
+        }
+        if (threadIdx.x == 0) P.tp.epochs[blockIdx.x] = ep;
+    }
+
     // copies still in flight (only after an expired wait) land before the CTA exits
     if (warp == 0 && lane == 0) *issued_sh = pr.u;
     __syncthreads();
@@ -522,9 +582,29 @@ cudaError_t launch_bulk_dtype(const BulkParams& P, int dtype, cudaStream_t s) {
 
 }  // namespace
 
+cudaError_t launch_gemv_bulk_impl(const WeightView* const* w, const int64_t* rows, int count, const void* x,
+                                  int xtype, int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
+                                  cudaStream_t stream);
+
+cudaError_t launch_gemv_bulk_allreduce(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
+                                       float* out, int64_t ldo, const TpLink& tp, cudaStream_t stream) {
+    const int64_t sms = bulk_sm_count(), tiles = (rows + 15) / 16;
+    const int64_t grid = tiles < sms ? tiles : sms;
+    if (tp.world < 1 || tp.world > kMaxRanks || sms > kMaxTpCtas || (tiles + grid - 1) / grid * 16 * m > tp.cap)
+        return cudaErrorNotSupported;
+    const WeightView* wp = &w;
+    return launch_gemv_bulk_impl(&wp, &rows, 1, x, xtype, m, &out, &ldo, &tp, stream);
+}
+
 cudaError_t launch_gemv_bulk_group(const WeightView* const* w, const int64_t* rows, int count, const void* x,
                                    int xtype, int64_t m, float* const* out, const int64_t* ldo,
                                    cudaStream_t stream) {
+    return launch_gemv_bulk_impl(w, rows, count, x, xtype, m, out, ldo, nullptr, stream);
+}
+
+cudaError_t launch_gemv_bulk_impl(const WeightView* const* w, const int64_t* rows, int count, const void* x,
+                                  int xtype, int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
+                                  cudaStream_t stream) {
     if (!bulk_enabled() || m < 1 || m > 8 || count < 1 || count > kGroup) return cudaErrorNotSupported;
     int* err = device_status_word();
     if (!err) return cudaErrorNotSupported;
@@ -552,6 +632,10 @@ cudaError_t launch_gemv_bulk_group(const WeightView* const* w, const int64_t* ro
     P.m = (int)m;
     P.x = x;
     P.err = err;
+    if (tp) {
+        P.tp_on = 1;
+        P.tp = *tp;
+    }
     const int esize = xtype == CLQ_X_F32 ? 4 : 2;
     P.x_aligned = ((uintptr_t)x % 16 == 0) && ((P.k * esize) % 16 == 0);
     switch (xtype) {

@@ -158,6 +158,39 @@ int clq_linear_group_device(const clq_store *const *w, const int64_t *row_begin,
 int clq_linear_device_noalloc(const clq_store *w, int64_t row_begin, int64_t rows, const void *x,
                               int xtype, int64_t m, float *out, int64_t ldo, void *stream);
 
+/* ---- tensor-parallel groups ----------------------------------------------
+ * No counterpart in the reference (it has no multi-GPU path).  One process per
+ * GPU; a group maps each rank's receive buffer into every rank through CUDA
+ * IPC, and clq_linear_allreduce_device runs a row-parallel shard product whose
+ * epilogue writes each output straight into every rank's buffer over NVLink
+ * (plain peer stores of 8-byte (epoch, value) words, so no fences or flags),
+ * then each CTA waits for its counterparts' words and sums the ranks in a
+ * fixed order -- the GEMV and the all-reduce in one kernel.
+ *
+ * Set-up: each rank calls clq_tp_buffers (its receive buffer of 2 x world x
+ * 160 x CAP words of 8 bytes, and a local block of per-CTA epochs), exports
+ * the receive buffer with clq_ipc_handle, exchanges the 64-byte handles with
+ * the other ranks, maps theirs with clq_ipc_open and calls clq_tp_create with
+ * all ranks' receive buffers (its own as allocated) and its own epoch block
+ * (other ranks' entries of FLAGS are not read).  Every rank must make the same
+ * sequence of clq_linear_allreduce_device calls with the same shapes; a wait
+ * that expires records CLQ_ERR_TIMEOUT in clq_device_status. */
+typedef struct clq_tp clq_tp;
+int clq_tp_buffers(int world, int64_t cap, void **recv, void **flags);
+int clq_tp_buffers_free(void *recv, void *flags);
+int clq_ipc_handle(const void *device_ptr, uint8_t handle[64]);
+int clq_ipc_open(const uint8_t handle[64], void **device_ptr);
+int clq_ipc_close(void *device_ptr);
+int clq_tp_create(int rank, int world, int64_t cap, void *const *recv, void *const *flags, clq_tp **out);
+int clq_tp_free(clq_tp *tp);
+/* out[i, j] = sum over ranks r of rank r's clq_linear_device product for rows
+ * [row_begin, row_begin + rows) of its store (each rank holds a K-slice of the
+ * weight, a row-parallel shard).  Q4_K / Q6_K, K a multiple of 256, m <= 8,
+ * and at most CAP outputs per SM; otherwise CLQ_ERR_UNSUPPORTED.  Asynchronous
+ * on STREAM. */
+int clq_linear_allreduce_device(const clq_store *w, int64_t row_begin, int64_t rows, const void *x, int xtype,
+                                int64_t m, float *out, int64_t ldo, clq_tp *tp, void *stream);
+
 /* ---- dequantize and gather ------------------------------------------------
  * Bit-exact fp32 values of packed-element (quant/packed.lisp:85-108) and the
  * Q8_0 dequantize-executor (quant/q8-0.lisp:98-123).
