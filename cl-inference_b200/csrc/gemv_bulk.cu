@@ -257,10 +257,16 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
                 grid_dependency_wait();  // activations may come from the previous kernel
                 if (P.tp_on && threadIdx.x == 0) tp_sh[0] = P.tp.epochs[blockIdx.x] + 1u;
             }
-            else __syncthreads();                         // everyone is done with the previous pass's x
-            if constexpr (I8) stage_x_i8<D, XT, kCW>(P.x, P.k, P.x_aligned, c0, pcn, ntok, xstage);
-            else stage_x<D, XT, kCW>(P.x, P.k, P.x_aligned, P.pc, c0, pcn, 0, ntok, xf, us, sxf);
-            __syncthreads();
+            if constexpr (I8) {
+                // each warp restages only its own chunks (after its own units of
+                // the previous pass) and reads only those: no CTA barrier
+                stage_x_i8<D, XT, kCW>(P.x, P.k, P.x_aligned, c0, pcn, ntok, xstage);
+                __syncwarp();
+            } else {
+                if (pass > 0) __syncthreads();  // everyone is done with the previous pass's x
+                stage_x<D, XT, kCW>(P.x, P.k, P.x_aligned, P.pc, c0, pcn, 0, ntok, xf, us, sxf);
+                __syncthreads();
+            }
             for (int tile = t_begin; tile < t_end; tile++) {
                 float acc[MT][2], accm[2] = {0.f, 0.f}, accn[2] = {0.f, 0.f};
 #pragma unroll

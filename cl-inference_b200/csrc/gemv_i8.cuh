@@ -49,7 +49,7 @@ template <int D> struct I8Block;
 template <> struct I8Block<kQ4_K> { static constexpr int sf = 32, bytes = 1024 + 32 + 16; };
 template <> struct I8Block<kQ6_K> { static constexpr int sf = 64, bytes = 1024 + 64 + 16; };
 
-// Stage chunks [c0, c0 + pc) of activation rows 0..ntok-1 (ntok <= 2); block
+// Stage chunks [c0, c0 + pc) of activation rows 0..ntok-1; block
 // (cc, u) at STAGE + (cc * ntok + u) * I8Block<D>::bytes holds
 //   [0, 1024)   digit dg (0 = most significant) of each element, as the MMA's
 //               B fragment: Q4_K uint2 at ((s*4 + tt)*4 + dg) = elements
@@ -67,8 +67,11 @@ __device__ void stage_x_i8(const void* xv, int64_t k, int x_aligned, int64_t c0,
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const XT* x = reinterpret_cast<const XT*>(xv);
     constexpr int TB = I8Block<D>::bytes;
-    for (int w = warp; w < pc * ntok; w += WARPS) {
-        const int cc = w / ntok, u = w - cc * ntok;
+    // warp w stages chunks w, w + WARPS, ...: exactly the chunks it multiplies
+    // later, so no other warp waits for its staging
+    for (int cc = warp; cc < pc; cc += WARPS)
+    for (int u = 0; u < ntok; u++) {
+        const int w = cc * ntok + u;
         unsigned char* base = stage + (size_t)w * TB;
         const XT* src = x + (int64_t)u * k + (c0 + cc) * 256 + 8 * lane;
         float v[8];
