@@ -184,10 +184,27 @@ struct DeviceBuffer {
     }
 };
 
+// Page-locked host staging: pageable copies make the driver stage through its
+// own buffer on every call, which dominates small decode-sized products.
+struct PinnedBuffer {
+    void* ptr = nullptr;
+    size_t cap = 0;
+    cudaError_t ensure(size_t bytes) {
+        if (bytes <= cap) return cudaSuccess;
+        if (ptr) cudaFreeHost(ptr);
+        ptr = nullptr; cap = 0;
+        size_t want = bytes < 65536 ? 65536 : bytes + bytes / 4;
+        cudaError_t e = cudaMallocHost(&ptr, want);
+        if (e == cudaSuccess) cap = want;
+        return e;
+    }
+};
+
 struct ThreadContext {
     int device = -1;
     cudaStream_t stream = nullptr;
     DeviceBuffer x, out, ids;
+    PinnedBuffer hx, hout;  // host staging of x and out for small products
 };
 
 struct ThreadContexts {
@@ -200,6 +217,8 @@ struct ThreadContexts {
             if (c->x.ptr) cudaFree(c->x.ptr);
             if (c->out.ptr) cudaFree(c->out.ptr);
             if (c->ids.ptr) cudaFree(c->ids.ptr);
+            if (c->hx.ptr) cudaFreeHost(c->hx.ptr);
+            if (c->hout.ptr) cudaFreeHost(c->hout.ptr);
             delete c;
         }
     }
@@ -476,14 +495,25 @@ int clq_matmul(int dtype, float* out, const float* x, const uint8_t* bytes, int6
     cudaError_t e;
     if ((e = ctx->x.ensure(xbytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(x)");
     if ((e = ctx->out.ensure(obytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(out)");
-    if ((e = cudaMemcpyAsync(ctx->x.ptr, x, xbytes, cudaMemcpyHostToDevice, ctx->stream)) != cudaSuccess)
+    // small products (decode) go through page-locked staging; large ones copy
+    // straight from and to the caller's memory
+    const bool staged = xbytes + obytes <= ((size_t)8 << 20);
+    if (staged) {
+        if ((e = ctx->hx.ensure(xbytes)) != cudaSuccess) return cuda_fail(e, "cudaMallocHost(x)");
+        if ((e = ctx->hout.ensure(obytes)) != cudaSuccess) return cuda_fail(e, "cudaMallocHost(out)");
+        std::memcpy(ctx->hx.ptr, x, xbytes);
+    }
+    if ((e = cudaMemcpyAsync(ctx->x.ptr, staged ? ctx->hx.ptr : x, xbytes, cudaMemcpyHostToDevice, ctx->stream)) !=
+        cudaSuccess)
         return cuda_fail(e, "copy x to device");
     if ((e = clq::launch_linear(view_of(store.get(), row_begin), n, ctx->x.ptr, CLQ_X_F32, m,
                                 (float*)ctx->out.ptr, n, flags & CLQ_MATH_FAST, ctx->stream)) != cudaSuccess)
         return cuda_fail(e, "linear kernel launch");
-    if ((e = cudaMemcpyAsync(out, ctx->out.ptr, obytes, cudaMemcpyDeviceToHost, ctx->stream)) != cudaSuccess)
+    if ((e = cudaMemcpyAsync(staged ? ctx->hout.ptr : out, ctx->out.ptr, obytes, cudaMemcpyDeviceToHost,
+                             ctx->stream)) != cudaSuccess)
         return cuda_fail(e, "copy out to host");
     if ((e = cudaStreamSynchronize(ctx->stream)) != cudaSuccess) return cuda_fail(e, "linear");
+    if (staged) std::memcpy(out, ctx->hout.ptr, obytes);
     return CLQ_OK;
 }
 

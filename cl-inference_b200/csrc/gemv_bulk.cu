@@ -23,6 +23,7 @@
 // g + 1 fall in different banks.  Every wait is bounded (see pipeline.cuh); on
 // expiry the kernel stops issuing, the consumers skip their work but still meet
 // at every barrier, and the CTA drains the copies in flight before it exits.
+#include <atomic>
 #include <cstdlib>
 
 #include <cuda_bf16.h>
@@ -42,7 +43,8 @@ using namespace pipe;
 constexpr int kCW = 16;                // warps = chunks per stage; warp 0 also issues the copies
 constexpr int kBulkThreads = kCW * 32;
 constexpr int kMaxStages = 8;
-constexpr int kHeader = 256;           // barriers + issued count
+constexpr int kHeader = 256;           // barriers, issued count, epoch
+constexpr int kMaxDevices = 64;
 
 // Bytes per row per chunk of the staged planes, and the row padding that keeps
 // the consumers' reads of rows g and g + 1 in different banks (the int8 Q4_K
@@ -551,8 +553,18 @@ cudaError_t launch_bulk(BulkParams P, cudaStream_t stream) {
     size_t smem = 0;
     if (!plan<D, I8>(P, P.m, P.tiles, grid, smem_budget(), &smem)) return cudaErrorNotSupported;
     auto kern = gemv_bulk_kernel<D, XT, MT, I8>;
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
+    // the attribute is per device; the largest plan of this variant so far is kept
+    static std::atomic<int> set_for[kMaxDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    if ((int)smem > set_for[dev].load(std::memory_order_relaxed)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        int seen = set_for[dev].load(std::memory_order_relaxed);
+        while ((int)smem > seen && !set_for[dev].compare_exchange_weak(seen, (int)smem)) {
+        }
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)grid);
     cfg.blockDim = dim3(kBulkThreads);
