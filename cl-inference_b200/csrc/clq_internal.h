@@ -71,6 +71,15 @@ struct TpLink {
 cudaError_t launch_gemv_bulk_allreduce(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
                                        float* out, int64_t ldo, const TpLink& tp, cudaStream_t stream);
 
+// The decode GEMV with one weight stream per warp (Q4_K / Q6_K, m <= 2), with
+// the all-reduce over TP's ranks fused in when TP is non-null;
+// cudaErrorNotSupported for shapes it does not take, before anything is launched.
+cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, int count, const void* x, int xtype,
+                             int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
+                             cudaStream_t stream);
+// Streaming multiprocessors of the current device (cached).
+int sm_count();
+
 // Device address of the current device's sticky status word (0 = no kernel
 // reported a problem; else a CLQ_ERR_* code), or nullptr if it cannot be found.
 int* device_status_word();

@@ -74,18 +74,6 @@ struct BulkParams {
     TpLink tp;
 };
 
-// One 8-byte (epoch, value) word to / from another GPU's memory: the store and
-// the load are single-copy atomic, so a word carrying the expected epoch also
-// carries its value -- no fences or flags.
-__device__ __forceinline__ void st_word(uint2* p, uint32_t ep, float v) {
-    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(ep), "r"(__float_as_uint(v)) : "memory");
-}
-__device__ __forceinline__ uint2 ld_word(const uint2* p) {
-    uint2 v;
-    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-    return v;
-}
-
 template <int D>
 __device__ __forceinline__ void stage_words(const unsigned char* st, const BulkParams& P, int r, int ci, int t,
                                             uint32_t (&w)[Words<D>::n]) {
@@ -396,11 +384,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
                     const int64_t row = (int64_t)(tile - (int)M.tile_begin) * 16 + (idx & 15);
                     if (!ok || row >= M.rows) continue;
                     if (P.tp_on) {  // this rank's partial, into this CTA's region of every rank
-                        const uint32_t ep = tp_sh[0];
-                        const int64_t off =
-                            (((int64_t)(ep & 1u) * P.tp.world + P.tp.rank) * kMaxTpCtas + blockIdx.x) * P.tp.cap +
-                            (int64_t)(tile - t_begin) * ntok * 16 + idx;
-                        for (int q = 0; q < P.tp.world; q++) st_word(P.tp.peer_recv[q] + off, ep, sum);
+                        tp_put(P.tp, tp_sh[0], tile - t_begin, ntok, idx, sum);
                     } else {
                         M.out[(int64_t)(idx >> 4) * M.ldo + row] = sum;
                     }
@@ -417,30 +401,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
         // same outputs; wait for their words (bounded) and sum in rank order ----
         __syncthreads();
         const uint32_t ep = tp_sh[0];
-        const Member& M = P.mem[0];
-        const uint2* slots = P.tp.my_recv + ((int64_t)(ep & 1u) * P.tp.world * kMaxTpCtas + blockIdx.x) * P.tp.cap;
-        const int64_t rank_stride = (int64_t)kMaxTpCtas * P.tp.cap;
-        const int64_t per_tile = (int64_t)ntok * 16;
-        const int64_t n_el = (int64_t)(t_end - t_begin) * per_tile;
-        for (int64_t i = threadIdx.x; i < n_el; i += blockDim.x) {
-            const int tile = t_begin + (int)(i / per_tile);
-            const int idx = (int)(i - (int64_t)(tile - t_begin) * per_tile);
-            const int64_t row = (int64_t)(tile - (int)M.tile_begin) * 16 + (idx & 15);
-            if (row >= M.rows) continue;
-            float sum = 0.f;
-            for (int q = 0; q < P.tp.world; q++) {  // fixed rank order
-                const uint2* src = slots + q * rank_stride + i;
-                uint2 w = ld_word(src);
-                for (uint32_t it = 0; w.x != ep && it < (1u << 22); it++) {
-                    if (*(volatile int*)P.err) break;
-                    if (it > 32) __nanosleep(32);
-                    w = ld_word(src);
-                }
-                if (w.x != ep) atomicExch(P.err, CLQ_ERR_TIMEOUT);
-                sum += __uint_as_float(w.y);
-            }
-            M.out[(int64_t)(idx >> 4) * M.ldo + row] = sum;
-        }
+        tp_gather_sum(P.tp, P.mem[0], t_begin, t_end, ntok, ep, err);
         if (threadIdx.x == 0) P.tp.epochs[blockIdx.x] = ep;
     }
 
@@ -453,16 +414,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
     }
 }
 
-int bulk_sm_count() {
-    static int count = 0;
-    if (!count) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        if (cudaDeviceGetAttribute(&count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || count <= 0)
-            count = 148;
-    }
-    return count;
-}
+int bulk_sm_count() { return sm_count(); }
 
 bool bulk_enabled() {
     static int on = -1;
@@ -550,6 +502,8 @@ template <int D, typename XT, int MT, bool I8>
 cudaError_t launch_bulk(BulkParams P, cudaStream_t stream) {
     const int64_t sms = bulk_sm_count();
     const int64_t grid = P.tiles < sms ? P.tiles : sms;
+    if (P.tp_on && (grid > kMaxTpCtas || (P.tiles + grid - 1) / grid * 16 * P.m > P.tp.cap))
+        return cudaErrorNotSupported;
     size_t smem = 0;
     if (!plan<D, I8>(P, P.m, P.tiles, grid, smem_budget(), &smem)) return cudaErrorNotSupported;
     auto kern = gemv_bulk_kernel<D, XT, MT, I8>;
@@ -600,16 +554,24 @@ cudaError_t launch_bulk_dtype(const BulkParams& P, int dtype, cudaStream_t s) {
 
 }  // namespace
 
+int sm_count() {
+    static int count = 0;
+    if (!count) {
+        int dev = 0, c = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&c, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || c <= 0) c = 148;
+        count = c;
+    }
+    return count;
+}
+
 cudaError_t launch_gemv_bulk_impl(const WeightView* const* w, const int64_t* rows, int count, const void* x,
                                   int xtype, int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
                                   cudaStream_t stream);
 
 cudaError_t launch_gemv_bulk_allreduce(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
                                        float* out, int64_t ldo, const TpLink& tp, cudaStream_t stream) {
-    const int64_t sms = bulk_sm_count(), tiles = (rows + 15) / 16;
-    const int64_t grid = tiles < sms ? tiles : sms;
-    if (tp.world < 1 || tp.world > kMaxRanks || sms > kMaxTpCtas || (tiles + grid - 1) / grid * 16 * m > tp.cap)
-        return cudaErrorNotSupported;
+    if (tp.world < 1 || tp.world > kMaxRanks) return cudaErrorNotSupported;
     const WeightView* wp = &w;
     return launch_gemv_bulk_impl(&wp, &rows, 1, x, xtype, m, &out, &ldo, &tp, stream);
 }
@@ -624,6 +586,9 @@ cudaError_t launch_gemv_bulk_impl(const WeightView* const* w, const int64_t* row
                                   int xtype, int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
                                   cudaStream_t stream) {
     if (!bulk_enabled() || m < 1 || m > 8 || count < 1 || count > kGroup) return cudaErrorNotSupported;
+    // one and two activation rows of Q4_K / Q6_K: the per-warp streams when their plan fits
+    const cudaError_t ew = launch_gemv_warp(w, rows, count, x, xtype, m, out, ldo, tp, stream);
+    if (ew != cudaErrorNotSupported) return ew;
     int* err = device_status_word();
     if (!err) return cudaErrorNotSupported;
     BulkParams P = {};

@@ -18,6 +18,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include "../../include/clq.h"
+#include "clq_internal.h"
 #include "layout.cuh"
 
 namespace clq {
@@ -439,6 +441,60 @@ __device__ __forceinline__ void compute_chunk(const uint32_t (&w)[2][Words<D>::n
 #pragma unroll
             for (int h = 0; h < 2; h++) acc[n][h] = fmaf(ut[n] * dsb[h], cacc[n][h], acc[n][h]);
     }
+}
+
+// One 8-byte (epoch, value) word to / from another GPU's memory: the store and
+// the load are single-copy atomic, so a word carrying the expected epoch also
+// carries its value -- no fences or flags.
+__device__ __forceinline__ void st_word(uint2* p, uint32_t ep, float v) {
+    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(ep), "r"(__float_as_uint(v)) : "memory");
+}
+__device__ __forceinline__ uint2 ld_word(const uint2* p) {
+    uint2 v;
+    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
+    return v;
+}
+
+// The all-reduce tail of the tensor-parallel GEMVs: this CTA's outputs are the
+// tiles [t_begin, t_end) of member 0, NTOK tokens each, and every rank's CTA
+// with this index has written its partials of them into this rank's receive
+// buffer as (EP, value) words.  Waits (bounded) for each word and sums the
+// ranks in rank order.
+template <typename TP>
+__device__ void tp_gather_sum(const TP& tp, const Member& M, int t_begin, int t_end, int ntok, uint32_t ep,
+                              int* err) {
+    const uint2* slots = tp.my_recv + ((int64_t)(ep & 1u) * tp.world * kMaxTpCtas + blockIdx.x) * tp.cap;
+    const int64_t rank_stride = (int64_t)kMaxTpCtas * tp.cap;
+    const int64_t per_tile = (int64_t)ntok * 16;
+    const int64_t n_el = (int64_t)(t_end - t_begin) * per_tile;
+    for (int64_t i = threadIdx.x; i < n_el; i += blockDim.x) {
+        const int tile = t_begin + (int)(i / per_tile);
+        const int idx = (int)(i - (int64_t)(tile - t_begin) * per_tile);
+        const int64_t row = (int64_t)(tile - (int)M.tile_begin) * 16 + (idx & 15);
+        if (row >= M.rows) continue;
+        float sum = 0.f;
+        for (int q = 0; q < tp.world; q++) {  // fixed rank order
+            const uint2* src = slots + q * rank_stride + i;
+            uint2 w = ld_word(src);
+            for (uint32_t it = 0; w.x != ep && it < (1u << 22); it++) {
+                if (*(volatile int*)err) break;
+                if (it > 32) __nanosleep(32);
+                w = ld_word(src);
+            }
+            if (w.x != ep) atomicExch(err, CLQ_ERR_TIMEOUT);
+            sum += __uint_as_float(w.y);
+        }
+        M.out[(int64_t)(idx >> 4) * M.ldo + row] = sum;
+    }
+}
+
+// This rank's partial SUM of output IDX of local tile TL (tile - t_begin), into
+// this CTA's region of every rank's receive buffer.
+template <typename TP>
+__device__ __forceinline__ void tp_put(const TP& tp, uint32_t ep, int64_t tl, int ntok, int idx, float sum) {
+    const int64_t off =
+        (((int64_t)(ep & 1u) * tp.world + tp.rank) * kMaxTpCtas + blockIdx.x) * tp.cap + tl * ntok * 16 + idx;
+    for (int q = 0; q < tp.world; q++) st_word(tp.peer_recv[q] + off, ep, sum);
 }
 
 __device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }

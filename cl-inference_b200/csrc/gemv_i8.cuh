@@ -1,13 +1,15 @@
 // gemv_i8.cuh -- decode GEMV compute on the integer tensor-core MMA for Q4_K and
 // Q6_K at one or two activation rows.
 //
-// Codes become unsigned bytes with one AND (and a shift for high nibbles, an OR
-// for Q6_K's high bits) per four weights -- no conversion to fp16 -- and run
+// Codes become unsigned bytes with one AND per four weights (Q4_K high nibbles
+// stay in place as 16 q; Q6_K adds a shift and an OR for its high bits) -- no
+// conversion to fp16 -- and run
 // through mma.sync m16n8k32 (Q4_K, one 32-element sub-block per MMA) or
 // m16n8k16 (Q6_K, one 16-element sub-scale group per MMA), u8 x s8 -> s32.
 // The activations of a 256-column chunk are scaled by a power of two per
 // (chunk, token) to a 30-bit integer image X = rint(x * 2^e) and split into
-// four balanced base-256 digits, X = D3 2^24 + D2 2^16 + D1 2^8 + D0; MMA column
+// four balanced base-256 digits, X = D3 2^24 + D2 2^16 + D1 2^8 + D0 (one add,
+// one XOR and a byte transpose per four elements); MMA column
 // n carries token n / 4, digit 3 - n % 4, so lane t's two accumulator columns
 // are (D3, D2) for even t and (D1, D0) for odd t of token t / 2.  Every integer
 // product and sum is exact; the sub-block scales are applied as one integer
@@ -49,106 +51,149 @@ template <int D> struct I8Block;
 template <> struct I8Block<kQ4_K> { static constexpr int sf = 32, bytes = 1024 + 32 + 16; };
 template <> struct I8Block<kQ6_K> { static constexpr int sf = 64, bytes = 1024 + 64 + 16; };
 
+// The four balanced base-256 digits of X (|X| < 2^30) as the bytes of one word,
+// least significant first: adding 128 to each of the three low digit positions
+// turns the carries of the balanced form into plain byte arithmetic, and the
+// XOR maps each low byte y to the signed byte y - 128.  The top byte is the
+// signed top digit (|D3| <= 64).
+__device__ __forceinline__ uint32_t digits_of(int X) { return ((uint32_t)X + 0x00808080u) ^ 0x00808080u; }
+
+// 4 x 4 byte transpose: out[d] holds byte d of v0..v3 (in that order), i.e.
+// digit d of four consecutive elements.
+__device__ __forceinline__ void transpose4(uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3, uint32_t (&out)[4]) {
+    const uint32_t t0 = prmt(v0, v1, 0x5140u), t1 = prmt(v0, v1, 0x7362u);
+    const uint32_t t2 = prmt(v2, v3, 0x5140u), t3 = prmt(v2, v3, 0x7362u);
+    out[0] = prmt(t0, t2, 0x5410u);
+    out[1] = prmt(t0, t2, 0x7632u);
+    out[2] = prmt(t1, t3, 0x5410u);
+    out[3] = prmt(t1, t3, 0x7632u);
+}
+
 // Stage chunks [c0, c0 + pc) of activation rows 0..ntok-1; block
 // (cc, u) at STAGE + (cc * ntok + u) * I8Block<D>::bytes holds
-//   [0, 1024)   digit dg (0 = most significant) of each element, as the MMA's
-//               B fragment: Q4_K uint2 at ((s*4 + tt)*4 + dg) = elements
-//               8tt..8tt+7 of sub-block s (k-slots 4tt.. and 16+4tt..); Q6_K
-//               uint32 at ((j*4 + tt)*4 + dg) = elements 16 half + 4tt.. of
-//               group j = (2h + half)*4 + grp (k-slots 4tt..4tt+3);
+//   [0, 1024)   the digit fragments, 16 bytes per (lane, MMA pair / quad):
+//               digit dg (0 = most significant) of 8 elements per 8 bytes;
+//               Q4_K uint4 at ((j*4 + dg)*4 + tt) = sub-blocks 2j and 2j+1,
+//               elements 8tt..8tt+7 of each (k-slots 4tt.. and 16+4tt..);
+//               Q6_K uint4 at ((hh*4 + dg)*4 + tt) = word grp (0..3) for group
+//               hh*4 + grp, elements 16 half + 4tt.. of (h, half) = hh
+//               (k-slots 4tt..4tt+3);
 //   [1024, +sf) hi / lo fp16 halves of the sums S of X over the sub-blocks
 //               (Q4_K: uint32 pair (S_2t, S_2t+1) at (t*2 + part)) or groups
 //               (Q6_K: uint2 at (t*2 + part), pairs (2t, 2t+1) and (8+2t, 9+2t)),
 //               times 2^-21;
 //   [.., +4)    the unscale 2^-e.
-template <int D, typename XT, int WARPS>
+// The lane-to-fragment order makes every 8-lane phase of the consumers'
+// 16-byte reads touch 128 consecutive bytes (no bank conflicts).
+// One (chunk, token) block from this lane's eight activations V (elements
+// 8 lane .. 8 lane + 7 of the chunk) into BASE.
+template <int D>
+__device__ __forceinline__ void stage_block_i8(const float (&v)[8], unsigned char* base) {
+    const int lane = threadIdx.x & 31;
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    int e = 0;
+    if (amax > 0.f) {
+        // amax * 2^e in [2^29, 2^30): four balanced digits always suffice
+        e = 29 - ((int)((__float_as_uint(amax) >> 23) & 255) - 127);
+        e = e < -100 ? -100 : (e > 120 ? 120 : e);
+    }
+    const float sc = __uint_as_float((uint32_t)(127 + e) << 23);  // 2^e, a normal float for e in [-100, 120]
+    uint32_t V[8];
+    float fsum = 0.f;  // this lane's share of the sub-block / group sum, in units of 2^-e
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const float y = v[i] * sc;  // exact scaling
+        fsum += y;
+        V[i] = digits_of(__float2int_rn(y));
+    }
+    uint32_t d03[4], d47[4];  // [digit position 0 = least significant]
+    transpose4(V[0], V[1], V[2], V[3], d03);
+    transpose4(V[4], V[5], V[6], V[7], d47);
+    if constexpr (D == kQ4_K) {
+        const int s = lane >> 2, tt = lane & 3;  // sub-block s, elements 8tt..
+        uint2* xq = reinterpret_cast<uint2*>(base);
+#pragma unroll
+        for (int dg = 0; dg < 4; dg++)
+            xq[(((s >> 1) * 4 + dg) * 4 + tt) * 2 + (s & 1)] = make_uint2(d03[3 - dg], d47[3 - dg]);
+        fsum += __shfl_xor_sync(0xffffffffu, fsum, 1);
+        fsum += __shfl_xor_sync(0xffffffffu, fsum, 2);  // lanes 4s..4s+3: S_s
+        const float S = fsum * 4.76837158203125e-07f;  // 2^-21
+        const float So = __shfl_down_sync(0xffffffffu, S, 4);  // S_{s+1}
+        if ((lane & 7) == 0) {  // s even: the pair for k-slots 2t', 2t'+1, t' = s / 2
+            uint32_t hi, lo;
+            split2(S, So, hi, lo);
+            uint32_t* sf = reinterpret_cast<uint32_t*>(base + 1024);
+            sf[(lane >> 3) * 2] = hi;
+            sf[(lane >> 3) * 2 + 1] = lo;
+        }
+    } else {
+        // lane L: h = L / 16, grp = (L % 16) / 4, half = (L % 4) / 2, elements 8 (L % 2)..
+        const int h = lane >> 4, grp = (lane >> 2) & 3, half = (lane >> 1) & 1, tt = 2 * (lane & 1);
+        const int hh = 2 * h + half, j = hh * 4 + grp;
+        uint32_t* xq = reinterpret_cast<uint32_t*>(base);
+#pragma unroll
+        for (int dg = 0; dg < 4; dg++) {
+            xq[((hh * 4 + dg) * 4 + tt) * 4 + grp] = d03[3 - dg];
+            xq[((hh * 4 + dg) * 4 + tt + 1) * 4 + grp] = d47[3 - dg];
+        }
+        fsum += __shfl_xor_sync(0xffffffffu, fsum, 1);  // lanes L, L^1: S_j
+        const float S = fsum * 4.76837158203125e-07f;
+        const float So = __shfl_down_sync(0xffffffffu, S, 4);  // group j + 1 (grp + 1)
+        if ((lane & 1) == 0 && (grp & 1) == 0) {
+            const int tp = (j & 7) >> 1, reg = j >> 3;  // pair (j, j+1) -> b0 (j < 8) or b1
+            uint32_t hi, lo;
+            split2(S, So, hi, lo);
+            uint32_t* sf = reinterpret_cast<uint32_t*>(base + 1024);
+            sf[(tp * 2) * 2 + reg] = hi;
+            sf[(tp * 2 + 1) * 2 + reg] = lo;
+        }
+    }
+    if (lane == 0) *reinterpret_cast<float*>(base + 1024 + I8Block<D>::sf) = __uint_as_float((uint32_t)(127 - e) << 23);
+}
+
+// AFTER_LOADS() runs once, after the first loads are issued and before any
+// block is converted (a caller's hook to issue more copies behind them).
+struct NoHook {
+    __device__ void operator()() const {}
+};
+template <int D, typename XT, int WARPS, typename Hook = NoHook>
 __device__ void stage_x_i8(const void* xv, int64_t k, int x_aligned, int64_t c0, int pc, int ntok,
-                           unsigned char* stage) {
+                           unsigned char* stage, Hook after_loads = Hook()) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const XT* x = reinterpret_cast<const XT*>(xv);
     constexpr int TB = I8Block<D>::bytes;
-    // warp w stages chunks w, w + WARPS, ...: exactly the chunks it multiplies
-    // later, so no other warp waits for its staging
-    for (int cc = warp; cc < pc; cc += WARPS)
-    for (int u = 0; u < ntok; u++) {
-        const int w = cc * ntok + u;
-        unsigned char* base = stage + (size_t)w * TB;
-        const XT* src = x + (int64_t)u * k + (c0 + cc) * 256 + 8 * lane;
-        float v[8];
-        if (x_aligned) {
-            xload8(src, v);
-        } else {
+    // warp w stages chunks w, w + WARPS, ... (all tokens of each), loading up to
+    // four (chunk, token) blocks before converting any: one memory round trip
+    // per four blocks
+    const int per = warp < pc ? ((pc - warp + WARPS - 1) / WARPS) * ntok : 0;
+    for (int b0 = 0; b0 < per; b0 += 4) {
+        float vb[4][8];
 #pragma unroll
-            for (int i = 0; i < 8; i++) v[i] = xload(src + i);
-        }
-        float amax = 0.f;
+        for (int b = 0; b < 4; b++) {
+            const int i = b0 + b, cc = warp + (i / ntok) * WARPS, u = i - (i / ntok) * ntok;
+            const XT* src = x + (int64_t)u * k + (c0 + cc) * 256 + 8 * lane;
+            if (i >= per) {
 #pragma unroll
-        for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
+                for (int e = 0; e < 8; e++) vb[b][e] = 0.f;
+            } else if (x_aligned) {
+                xload8(src, vb[b]);
+            } else {
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        int e = 0;
-        if (amax > 0.f) {
-            // amax * 2^e in [2^29, 2^30): four balanced digits always suffice
-            e = 29 - ((int)((__float_as_uint(amax) >> 23) & 255) - 127);
-            e = e < -100 ? -100 : (e > 120 ? 120 : e);
-        }
-        const float sc = __uint_as_float((uint32_t)(127 + e) << 23);  // 2^e, a normal float for e in [-100, 120]
-        // balanced base-256 digits: the digit's byte is the low byte of the
-        // remainder, and the next remainder is (r + 128) >> 8
-        uint32_t dg[4][2] = {{0u, 0u}, {0u, 0u}, {0u, 0u}, {0u, 0u}};  // [digit 3..0][elements 0-3, 4-7]
-        long long lsum = 0;  // this lane's share of the sub-block / group sum of X
-#pragma unroll
-        for (int i = 0; i < 8; i++) {
-            const int Xi = __float2int_rn(v[i] * sc);  // exact scaling, one rounding
-            lsum += Xi;
-            int r = Xi;
-#pragma unroll
-            for (int d = 3; d >= 0; d--) {
-                dg[d][i >> 2] |= ((uint32_t)r & 0xFFu) << (8 * (i & 3));
-                r = (r + 128) >> 8;
+                for (int e = 0; e < 8; e++) vb[b][e] = xload(src + e);
             }
         }
-        float* us = reinterpret_cast<float*>(base + 1024 + I8Block<D>::sf);
-        if constexpr (D == kQ4_K) {
-            const int s = lane >> 2, tt = lane & 3;  // sub-block s, elements 8tt..
-            uint2* xq = reinterpret_cast<uint2*>(base);
+        if (b0 == 0) after_loads();
 #pragma unroll
-            for (int d = 0; d < 4; d++) xq[(s * 4 + tt) * 4 + d] = make_uint2(dg[d][0], dg[d][1]);
-            lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);
-            lsum += __shfl_xor_sync(0xffffffffu, lsum, 2);  // lanes 4s..4s+3: S_s
-            const float S = (float)lsum * 4.76837158203125e-07f;  // 2^-21
-            const float So = __shfl_down_sync(0xffffffffu, S, 4);  // S_{s+1}
-            if ((lane & 7) == 0) {  // s even: the pair for k-slots 2t', 2t'+1, t' = s / 2
-                uint32_t hi, lo;
-                split2(S, So, hi, lo);
-                uint32_t* sf = reinterpret_cast<uint32_t*>(base + 1024);
-                sf[(lane >> 3) * 2] = hi;
-                sf[(lane >> 3) * 2 + 1] = lo;
-            }
-        } else {
-            // lane L: h = L / 16, grp = (L % 16) / 4, half = (L % 4) / 2, elements 8 (L % 2)..
-            const int h = lane >> 4, grp = (lane >> 2) & 3, half = (lane >> 1) & 1, tt = 2 * (lane & 1);
-            const int j = (2 * h + half) * 4 + grp;
-            uint32_t* xq = reinterpret_cast<uint32_t*>(base);
-#pragma unroll
-            for (int d = 0; d < 4; d++) {
-                xq[(j * 4 + tt) * 4 + d] = dg[d][0];
-                xq[(j * 4 + tt + 1) * 4 + d] = dg[d][1];
-            }
-            lsum += __shfl_xor_sync(0xffffffffu, lsum, 1);  // lanes L, L^1: S_j
-            const float S = (float)lsum * 4.76837158203125e-07f;
-            const float So = __shfl_down_sync(0xffffffffu, S, 4);  // group j + 1 (grp + 1)
-            if ((lane & 1) == 0 && (grp & 1) == 0) {
-                const int tp = (j & 7) >> 1, reg = j >> 3;  // pair (j, j+1) -> b0 (j < 8) or b1
-                uint32_t hi, lo;
-                split2(S, So, hi, lo);
-                uint32_t* sf = reinterpret_cast<uint32_t*>(base + 1024);
-                sf[(tp * 2) * 2 + reg] = hi;
-                sf[(tp * 2 + 1) * 2 + reg] = lo;
-            }
+        for (int b = 0; b < 4; b++) {
+            const int i = b0 + b, cc = warp + (i / ntok) * WARPS, u = i - (i / ntok) * ntok;
+            if (i < per) stage_block_i8<D>(vb[b], stage + (size_t)(cc * ntok + u) * TB);
         }
-        if (lane == 0) *us = __uint_as_float((uint32_t)(127 - e) << 23);
     }
+    if (per == 0) after_loads();
 }
 
 // Per-lane constants of the i8 product.  Lane (g, t) reads B column g = token
@@ -179,13 +224,9 @@ __device__ __forceinline__ I8Lane i8_lane(int ntok) {
     L.s_sel = b0 | (4u << 4) | (b1 << 8) | (4u << 12);
     const int tb = min(L.g >> 2, ntok - 1), tm = min(L.g >> 1, ntok - 1);
     const int dgt = L.g & 3, part = L.g & 1;
-    if constexpr (D == kQ4_K) {
-        L.xb = tb * TB + (L.t * 4 + dgt) * 8;
-        L.xm = tm * TB + 1024 + (L.t * 2 + part) * 4;
-    } else {
-        L.xb = tb * TB + (L.t * 4 + dgt) * 4;
-        L.xm = tm * TB + 1024 + (L.t * 2 + part) * 8;
-    }
+    L.xb = tb * TB + (dgt * 4 + L.t) * 16;  // + 256 bytes per sub-block pair (Q4_K) / (h, half) (Q6_K)
+    if constexpr (D == kQ4_K) L.xm = tm * TB + 1024 + (L.t * 2 + part) * 4;
+    else L.xm = tm * TB + 1024 + (L.t * 2 + part) * 8;
     L.ua = min(L.t >> 1, ntok - 1) * TB + 1024 + I8Block<D>::sf;
     L.um = min(L.t, ntok - 1) * TB + 1024 + I8Block<D>::sf;
     return L;
@@ -201,37 +242,41 @@ __device__ __forceinline__ int sbyte(uint32_t w, int b) {
 // Q4_K, one chunk: HD[h] = 16-byte header of row g + 8h; CW[h][j] = bytes
 // 8t..8t+7 of code group j; XS = the chunk's first staged block.  Adds to accm
 // (digit-weighted, token t/2) and accn (min term of token t, to be subtracted).
+// Low nibbles (sub-block 2j) enter the MMA as bytes 0..15; high nibbles
+// (sub-block 2j+1) are only masked, entering as 16 q, and their sums go to a
+// second accumulator: sum = 16 al + ah is 16x the scaled code sum (|.| < 2^30),
+// and the factor 16 is taken out with the fp16 scale.
 __device__ __forceinline__ void q4k_i8_chunk(const I8Lane& L, const uint32_t (&HD)[2][4], const uint2 (&CW)[2][4],
                                              const unsigned char* xs, float (&accm)[2], float (&accn)[2]) {
-    const unsigned char* xb = xs + L.xb;
-    uint32_t sc03[2], sc47[2], m03[2], m47[2];
+    const uint4* xb = reinterpret_cast<const uint4*>(xs + L.xb);
+    uint32_t scw[2][2], m03[2], m47[2];
 #pragma unroll
     for (int h = 0; h < 2; h++) {
-        sc03[h] = HD[h][1] & 0x3F3F3F3Fu;
-        sc47[h] = (HD[h][3] & 0x0F0F0F0Fu) | ((HD[h][1] >> 2) & 0x30303030u);
+        scw[h][0] = HD[h][1] & 0x3F3F3F3Fu;                                        // sub-blocks 0..3
+        scw[h][1] = (HD[h][3] & 0x0F0F0F0Fu) | ((HD[h][1] >> 2) & 0x30303030u);    // 4..7
         m03[h] = HD[h][2] & 0x3F3F3F3Fu;
         m47[h] = ((HD[h][3] >> 4) & 0x0F0F0F0Fu) | ((HD[h][2] >> 2) & 0x30303030u);
     }
-    int acc[4] = {0, 0, 0, 0};
+    int al[4] = {0, 0, 0, 0}, ah[4] = {0, 0, 0, 0};
 #pragma unroll
     for (int j = 0; j < 4; j++) {
-#pragma unroll
-        for (int hn = 0; hn < 2; hn++) {  // low nibbles: sub-block 2j; high: 2j + 1
-            const int s = 2 * j + hn;
-            const uint32_t a0 = hn ? (CW[0][j].x >> 4) & 0x0F0F0F0Fu : CW[0][j].x & 0x0F0F0F0Fu;
-            const uint32_t a2 = hn ? (CW[0][j].y >> 4) & 0x0F0F0F0Fu : CW[0][j].y & 0x0F0F0F0Fu;
-            const uint32_t a1 = hn ? (CW[1][j].x >> 4) & 0x0F0F0F0Fu : CW[1][j].x & 0x0F0F0F0Fu;
-            const uint32_t a3 = hn ? (CW[1][j].y >> 4) & 0x0F0F0F0Fu : CW[1][j].y & 0x0F0F0F0Fu;
-            const uint2 b = *reinterpret_cast<const uint2*>(xb + s * 128);
-            int c[4];
-            imma_k32(c, a0, a1, a2, a3, b.x, b.y);
-            const int s0 = ubyte(s < 4 ? sc03[0] : sc47[0], s & 3);
-            const int s1 = ubyte(s < 4 ? sc03[1] : sc47[1], s & 3);
-            acc[0] += s0 * c[0];
-            acc[1] += s0 * c[1];
-            acc[2] += s1 * c[2];
-            acc[3] += s1 * c[3];
-        }
+        const uint4 b = xb[16 * j];  // .xy: sub-block 2j, .zw: sub-block 2j + 1
+        const uint32_t w0 = scw[0][j >> 1], w1 = scw[1][j >> 1];
+        int c[4];
+        imma_k32(c, CW[0][j].x & 0x0F0F0F0Fu, CW[1][j].x & 0x0F0F0F0Fu, CW[0][j].y & 0x0F0F0F0Fu,
+                 CW[1][j].y & 0x0F0F0F0Fu, b.x, b.y);
+        const int l0 = ubyte(w0, 2 * (j & 1)), l1 = ubyte(w1, 2 * (j & 1));
+        al[0] += l0 * c[0];
+        al[1] += l0 * c[1];
+        al[2] += l1 * c[2];
+        al[3] += l1 * c[3];
+        imma_k32(c, CW[0][j].x & 0xF0F0F0F0u, CW[1][j].x & 0xF0F0F0F0u, CW[0][j].y & 0xF0F0F0F0u,
+                 CW[1][j].y & 0xF0F0F0F0u, b.z, b.w);
+        const int h0 = ubyte(w0, 2 * (j & 1) + 1), h1 = ubyte(w1, 2 * (j & 1) + 1);
+        ah[0] += h0 * c[0];
+        ah[1] += h0 * c[1];
+        ah[2] += h1 * c[2];
+        ah[3] += h1 * c[3];
     }
     // min term: A = (m_{2t}, m_{2t+1}) per row, k-slots 8.. are zero
     uint32_t am[2];
@@ -239,12 +284,13 @@ __device__ __forceinline__ void q4k_i8_chunk(const I8Lane& L, const uint32_t (&H
     for (int h = 0; h < 2; h++) am[h] = hsub2(prmt(prmt(m03[h], m47[h], L.m_sel), kMagic, kSelLo), kH1024);
     float cm[4] = {0.f, 0.f, 0.f, 0.f};
     mma16816(cm, am[0], am[1], 0u, 0u, *reinterpret_cast<const uint32_t*>(xs + L.xm), 0u);
-    const float ut = *reinterpret_cast<const float*>(xs + L.ua);
+    const float ut = *reinterpret_cast<const float*>(xs + L.ua) * 0.0625f;  // and the 16 of the code sums
     const float umin = *reinterpret_cast<const float*>(xs + L.um) * 2097152.f;  // times 2^21
 #pragma unroll
     for (int h = 0; h < 2; h++) {
         const float d = lo_half(HD[h][0]), dm = hi_half(HD[h][0]);
-        const float f = fmaf((float)acc[2 * h], L.wa, (float)acc[2 * h + 1] * L.wb);
+        const int fa = al[2 * h] * 16 + ah[2 * h], fb = al[2 * h + 1] * 16 + ah[2 * h + 1];
+        const float f = fmaf((float)fa, L.wa, (float)fb * L.wb);
         accm[h] = fmaf(d * ut, f, accm[h]);
         accn[h] = fmaf(dm * umin, cm[2 * h] + cm[2 * h + 1], accn[h]);
     }
@@ -257,7 +303,7 @@ __device__ __forceinline__ void q4k_i8_chunk(const I8Lane& L, const uint32_t (&H
 __device__ __forceinline__ void q6k_i8_chunk(const I8Lane& L, const uint32_t (&QW)[2][12], const uint4 (&SW)[2],
                                              const uint32_t (&DB)[2], const unsigned char* xs, float (&accm)[2],
                                              float (&accn)[2]) {
-    const unsigned char* xb = xs + L.xb;
+    const uint4* xb = reinterpret_cast<const uint4*>(xs + L.xb);
     const uint32_t sw[2][4] = {{SW[0].x, SW[0].y, SW[0].z, SW[0].w}, {SW[1].x, SW[1].y, SW[1].z, SW[1].w}};
     int acc[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -272,11 +318,12 @@ __device__ __forceinline__ void q6k_i8_chunk(const I8Lane& L, const uint32_t (&Q
             q[r][2] = ((W0 >> 4) & 0x0F0F0F0Fu) | (QH & 0x30303030u);
             q[r][3] = ((W1 >> 4) & 0x0F0F0F0Fu) | ((QH >> 2) & 0x30303030u);
         }
+        const uint4 bq = xb[16 * hh];
+        const uint32_t bw[4] = {bq.x, bq.y, bq.z, bq.w};
 #pragma unroll
         for (int grp = 0; grp < 4; grp++) {
-            const int j = hh * 4 + grp;
             int c[4];
-            imma_k16(c, q[0][grp], q[1][grp], *reinterpret_cast<const uint32_t*>(xb + j * 64));
+            imma_k16(c, q[0][grp], q[1][grp], bw[grp]);
             const int idx = 8 * h6 + 2 * grp + half;  // sub-scale of this group
             const int s0 = sbyte(sw[0][idx >> 2], idx & 3), s1 = sbyte(sw[1][idx >> 2], idx & 3);
             acc[0] += s0 * c[0];

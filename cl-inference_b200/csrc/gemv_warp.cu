@@ -1,0 +1,450 @@
+// gemv_warp.cu -- decode GEMV (one or two activation rows) for Q4_K and Q6_K
+// with an independent weight stream per warp.
+//
+// One persistent CTA of 16 warps per SM owns a contiguous range of 16-row
+// tiles.  Its (tile, chunk) units -- 16 rows x 256 columns, tile-major -- are
+// cut into contiguous runs of equal length, one per warp.  Each warp streams
+// its own run: one lane copies each unit as one box of a 2-D tensor map over
+// the weight's q plane (16 rows x one chunk's bytes) into a ring of DEPTH
+// slots in shared memory, with completion counted on one mbarrier per slot
+// (rows past the weight's end read as zeros); the warp waits for a slot,
+// reads its words, refills the
+// slot with the unit DEPTH ahead and multiplies with the integer-MMA product
+// of gemv_i8.cuh.  No warp waits for another except once, after the
+// activations are staged, so a slow warp never stalls the others' streams.
+//
+// A tile's K range can be split between consecutive warps.  Each warp leaves
+// one partial sum per tile it touches (a "piece") in shared memory and counts
+// it on the tile's counter; the warp that completes the count adds the tile's
+// pieces in warp order -- a fixed order, so results do not depend on timing --
+// and writes the outputs or, under tensor parallelism, sends them to every
+// rank.
+//
+// The copies do not depend on the previous kernel (the weights are constant):
+// under programmatic dependent launch each warp starts its ring before
+// griddepcontrol.wait and fills it once its activation loads are out; only
+// the activation staging waits for the previous kernel.  The weight stream is
+// read with an L2 evict-first policy.  Every wait is bounded (pipeline.cuh); after an expired wait the
+// warp stops, drains the copies it issued, and the status word reports it.
+#include <atomic>
+#include <cstdlib>
+#include <mutex>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "../../include/clq.h"
+#include "clq_internal.h"
+#include "gemv_common.cuh"
+#include "gemv_i8.cuh"
+#include "pipeline.cuh"
+
+namespace clq {
+namespace {
+
+using namespace pipe;
+
+constexpr int kWW = 16;  // warps per CTA
+constexpr int kWThreads = kWW * 32;
+constexpr int kWMaxDepth = 4;
+constexpr int kWHeader = kWW * kWMaxDepth * 8 + 16;  // slot barriers, this call's epoch
+constexpr int kWMaxDevices = 64;
+constexpr size_t kWSmemLimit = 227 * 1024;
+// Units each warp copies before waiting for the previous kernel; the rest of
+// its ring is filled after its activation loads are issued, so that those
+// loads do not queue behind a full ring's worth of weight traffic.
+constexpr int kWPreWait = 2;
+
+// Bytes of one row of one unit in the q plane (the whole unit's data for Q4_K;
+// Q6_K's sub-scales and scale, 9% of its bytes, are read with plain loads).
+template <int D> struct WGeo;
+template <> struct WGeo<kQ4_K> { static constexpr int q = 144; };
+template <> struct WGeo<kQ6_K> { static constexpr int q = 192; };
+
+struct WarpParams {
+    CUtensorMap maps[kGroup];  // q plane of each member: [rows][K / 256 * Q] bytes, box 16 x Q
+    Member mem[kGroup];
+    int nmem;
+    int tiles;
+    int nchunks;  // K / 256
+    int m;        // 1 or 2
+    int64_t k;
+    const void* x;
+    int x_aligned;
+    int depth;    // ring slots per warp
+    uint32_t cnt_off, x_off, piece_off, ring_off;
+    int* err;
+    int tp_on;
+    TpLink tp;
+};
+
+// The warp whose run holds unit u: runs are [w U / W, (w+1) U / W) for the
+// W = min(16, U) warps in use, all non-empty.
+__device__ __forceinline__ int warp_of(int u, int U, int W) { return (W * (u + 1) + U - 1) / U - 1; }
+
+template <int D, typename XT>
+__global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_constant__ WarpParams P) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr int Q = WGeo<D>::q;
+    constexpr uint32_t kSlot = 16u * Q;
+    constexpr int TB = I8Block<D>::bytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
+    uint32_t* ep_sh = reinterpret_cast<uint32_t*>(bars + kWW * kWMaxDepth);
+    int* cnt = reinterpret_cast<int*>(smem + P.cnt_off);
+    unsigned char* xstage = smem + P.x_off;
+    float* piece = reinterpret_cast<float*>(smem + P.piece_off);
+
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    const int nch = P.nchunks, ntok = P.m, depth = P.depth;
+    const int t_begin = (int)((int64_t)blockIdx.x * P.tiles / gridDim.x);
+    const int t_end = (int)(((int64_t)blockIdx.x + 1) * P.tiles / gridDim.x);
+    const int U = (t_end - t_begin) * nch;
+    const int W = U < kWW ? U : kWW;
+    const int u0 = warp < W ? warp * U / W : 0, u1 = warp < W ? (warp + 1) * U / W : 0;
+    uint64_t* bar = bars + warp * kWMaxDepth;
+    unsigned char* ring = smem + P.ring_off + (size_t)warp * depth * kSlot;
+    int* err = P.err;
+
+    if (lane == 0) {
+        for (int s = 0; s < depth; s++) mbar_init(&bar[s], 1);
+        mbar_init_fence();
+    }
+    __syncwarp();
+    allow_dependents();
+
+    // ---- this warp's copies: unit (itile, ic) into slot islot ----
+    const uint64_t policy = evict_first_policy();
+    int issued = u0, itile = t_begin + (u0 / (nch > 0 ? nch : 1)), ic = u0 - (itile - t_begin) * nch, islot = 0;
+    auto issue = [&]() {
+        if (lane == 0) {
+            const int mi = member_of(P, (int64_t)itile);
+            mbar_arrive_tx(&bar[islot], kSlot);
+            tensor_copy_2d_hint(ring + islot * kSlot, &P.maps[mi], ic * Q,
+                                (itile - (int)P.mem[mi].tile_begin) * 16, &bar[islot], policy);
+        }
+        ++issued;
+        if (++islot == depth) islot = 0;
+        if (++ic == nch) {
+            ic = 0;
+            ++itile;
+        }
+    };
+    while (issued < u1 && issued < u0 + kWPreWait) issue();
+
+    grid_dependency_wait();  // the activations may come from the previous kernel
+    if (threadIdx.x == 0 && P.tp_on) ep_sh[0] = P.tp.epochs[blockIdx.x] + 1u;
+    for (int i = threadIdx.x; i < t_end - t_begin; i += kWThreads) cnt[i] = 0;
+    stage_x_i8<D, XT, kWW>(P.x, P.k, P.x_aligned, 0, nch, ntok, xstage, [&]() {
+        while (issued < u1 && issued < u0 + depth) issue();
+    });
+    __syncthreads();
+
+    const I8Lane L8 = i8_lane<D>(ntok);
+    float accm[2] = {0.f, 0.f}, accn[2] = {0.f, 0.f};
+    bool ok = true;
+    int done = u0;
+
+    // Q6_K sub-scales and scale of rows g, g + 8 for a unit, one unit ahead
+    uint4 s_cur[2] = {}, s_nxt[2] = {};
+    uint32_t d_cur[2] = {0u, 0u}, d_nxt[2] = {0u, 0u};
+    auto side = [&](int tile, int c) {
+        const Member& M = P.mem[member_of(P, (int64_t)tile)];
+        int64_t r0 = (int64_t)(tile - (int)M.tile_begin) * 16 + g, r1 = r0 + 8;
+        if (r0 >= M.rows) r0 = M.rows - 1;
+        if (r1 >= M.rows) r1 = M.rows - 1;
+        s_nxt[0] = __ldg(reinterpret_cast<const uint4*>(M.p.s + (r0 * nch + c) * 16));
+        s_nxt[1] = __ldg(reinterpret_cast<const uint4*>(M.p.s + (r1 * nch + c) * 16));
+        d_nxt[0] = __ldg(reinterpret_cast<const unsigned short*>(M.p.d + (r0 * nch + c) * 2));
+        d_nxt[1] = __ldg(reinterpret_cast<const unsigned short*>(M.p.d + (r1 * nch + c) * 2));
+    };
+
+    int tl = u0 / (nch > 0 ? nch : 1), c = u0 - tl * nch, slot = 0;
+    uint32_t phase = 0;
+    if constexpr (D == kQ6_K) {
+        if (u0 < u1) side(t_begin + tl, c);
+    }
+    for (int u = u0; u < u1; u++) {
+        if constexpr (D == kQ6_K) {
+            s_cur[0] = s_nxt[0]; s_cur[1] = s_nxt[1];
+            d_cur[0] = d_nxt[0]; d_cur[1] = d_nxt[1];
+            if (u + 1 < u1) {
+                const bool wrap = c + 1 == nch;
+                side(t_begin + tl + (wrap ? 1 : 0), wrap ? 0 : c + 1);
+            }
+        }
+        if (!mbar_wait(&bar[slot], phase, err)) {
+            ok = false;
+            break;
+        }
+        const unsigned char* st = ring + slot * kSlot;
+        const unsigned char* xs = xstage + (size_t)c * ntok * TB;
+        if constexpr (D == kQ4_K) {
+            uint32_t HD[2][4];
+            uint2 CW[2][4];
+            // MMA rows g and g + 8 are the tile's rows 2g and 2g + 1: lanes g
+            // then read 288 bytes apart, and one 16-lane phase (g = 0..3) of
+            // the 8-byte reads covers all 32 banks once
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const unsigned char* q = st + (2 * g + h) * Q;
+                const uint4 hd = *reinterpret_cast<const uint4*>(q);
+                HD[h][0] = hd.x; HD[h][1] = hd.y; HD[h][2] = hd.z; HD[h][3] = hd.w;
+#pragma unroll
+                for (int j = 0; j < 4; j++) CW[h][j] = *reinterpret_cast<const uint2*>(q + 16 + 32 * j + 8 * t);
+            }
+            __syncwarp();
+            if (issued < u1) issue();  // the slot's words are in registers: refill it
+            q4k_i8_chunk(L8, HD, CW, xs, accm, accn);
+        } else {
+            uint32_t QW[2][12];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const unsigned char* q = st + (g + 8 * h) * Q + 48 * t;
+#pragma unroll
+                for (int i = 0; i < 3; i++) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(q + 16 * i);
+                    QW[h][4 * i] = v.x; QW[h][4 * i + 1] = v.y; QW[h][4 * i + 2] = v.z; QW[h][4 * i + 3] = v.w;
+                }
+            }
+            __syncwarp();
+            if (issued < u1) issue();
+            q6k_i8_chunk(L8, QW, s_cur, d_cur, xs, accm, accn);
+        }
+        done = u + 1;
+        if (++slot == depth) {
+            slot = 0;
+            phase ^= 1u;
+        }
+        const bool tile_end = ++c == nch;
+        if (tile_end || u + 1 == u1) {
+            // ---- this warp's piece of tile tl: to shared memory, then count it ----
+            float v[2];
+#pragma unroll
+            for (int h = 0; h < 2; h++) v[h] = i8_finish(L8, accm[h], accn[h]);
+            const int tok = t >> 1;
+            if ((t & 1) == 0 && tok < ntok) {
+#pragma unroll
+                for (int h = 0; h < 2; h++)
+                    piece[((warp + tl) * ntok + tok) * 16 + (D == kQ4_K ? 2 * g + h : g + 8 * h)] = v[h];
+            }
+            accm[0] = accm[1] = accn[0] = accn[1] = 0.f;
+            __syncwarp();
+            int old = 0;
+            if (lane == 0) {
+                __threadfence_block();
+                old = atomicAdd(&cnt[tl], 1);
+            }
+            old = __shfl_sync(0xffffffffu, old, 0);
+            const int wf = warp_of(tl * nch, U, W), wl = warp_of(tl * nch + nch - 1, U, W);
+            if (old == wl - wf) {  // the tile's last piece: add them in warp order
+                __threadfence_block();
+                const int tile = t_begin + tl;
+                const Member& M = P.mem[member_of(P, (int64_t)tile)];
+                for (int idx = lane; idx < ntok * 16; idx += 32) {
+                    float sum = 0.f;
+                    for (int w = wf; w <= wl; w++) sum += piece[((w + tl) * ntok) * 16 + idx];
+                    const int64_t row = (int64_t)(tile - (int)M.tile_begin) * 16 + (idx & 15);
+                    if (row >= M.rows) continue;
+                    if (P.tp_on) tp_put(P.tp, ep_sh[0], tl, ntok, idx, sum);
+                    else M.out[(int64_t)(idx >> 4) * M.ldo + row] = sum;
+                }
+            }
+            if (tile_end) {
+                c = 0;
+                ++tl;
+            }
+        }
+    }
+
+    // copies issued but not consumed (only after an expired wait) land before the CTA exits
+    if (!ok && lane == 0) {
+        for (int v = done; v < issued; v++) {
+            const int k = v - u0;
+            mbar_drain(&bar[k % depth], (uint32_t)(k / depth) & 1u);
+        }
+    }
+    if (P.tp_on) {
+        // every rank partitions the tiles the same way, so this CTA's
+        // counterparts produce the same outputs: wait for their words, sum
+        __syncthreads();
+        const uint32_t ep = ep_sh[0];
+        tp_gather_sum(P.tp, P.mem[0], t_begin, t_end, ntok, ep, err);
+        if (threadIdx.x == 0) P.tp.epochs[blockIdx.x] = ep;
+    }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// ROWS rows of ROW_BYTES bytes at BASE, read as boxes of 16 rows x BOX bytes.
+bool encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box) {
+    PFN_cuTensorMapEncodeTiled_v12000 fn = encode_tiled();
+    if (!fn || (uintptr_t)base % 16 || row_bytes % 16 || box % 16) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t boxd[2] = {(cuuint32_t)box, 16u};
+    const cuuint32_t estr[2] = {1u, 1u};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, boxd, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+bool warp_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("CLQ_GEMV_WARP");  // tuning knob: 0 sends decode to the shared-ring bulk kernel
+        const char* i = getenv("CLQ_GEMV_I8");
+        on = ((e && e[0] == '0') || (i && i[0] == '0')) ? 0 : 1;
+    }
+    return on == 1;
+}
+
+size_t al128(size_t v) { return (v + 127) & ~(size_t)127; }
+
+// CTAs for TILES tiles: one per SM, or -- with CLQ_GEMV_WARP_GRID=balanced, a
+// tuning knob -- the count in [3/4 of the SMs, all of them] that leaves the
+// fewest idle tile slots (the busiest CTA sets the kernel's time).
+int64_t warp_grid(int64_t tiles) {
+    static int mode = -1;
+    if (mode < 0) {
+        const char* e = getenv("CLQ_GEMV_WARP_GRID");
+        mode = (e && e[0] == 'b') ? 1 : 0;
+    }
+    const int64_t sms = sm_count();
+    if (tiles <= sms) return tiles;
+    if (!mode) return sms;
+    int64_t best = sms, best_pad = (tiles + sms - 1) / sms * sms - tiles;
+    for (int64_t g = sms - 1; g >= sms * 3 / 4; g--) {
+        const int64_t pad = (tiles + g - 1) / g * g - tiles;
+        if (pad < best_pad) {
+            best = g;
+            best_pad = pad;
+        }
+    }
+    return best;
+}
+
+// Shared memory: header, tile counters, all of K's staged activations, the
+// pieces, then 16 rings of DEPTH slots (4, else 3).  False when three slots
+// per warp do not fit.
+template <int D>
+bool wplan(WarpParams& P, int64_t grid, size_t* smem) {
+    const int64_t tiles_cta = (P.tiles + grid - 1) / grid;
+    P.cnt_off = kWHeader;
+    P.x_off = (uint32_t)al128(P.cnt_off + (size_t)tiles_cta * 4);
+    P.piece_off = (uint32_t)al128(P.x_off + (size_t)P.nchunks * P.m * I8Block<D>::bytes);
+    P.ring_off = (uint32_t)al128(P.piece_off + (size_t)(kWW + tiles_cta) * P.m * 16 * 4);
+    for (int depth = kWMaxDepth; depth >= 3; depth--) {
+        const size_t total = P.ring_off + (size_t)kWW * depth * 16 * WGeo<D>::q;
+        if (total <= kWSmemLimit) {
+            P.depth = depth;
+            *smem = total;
+            return true;
+        }
+    }
+    return false;
+}
+
+template <int D, typename XT>
+cudaError_t launch_warp(WarpParams P, cudaStream_t stream) {
+    const int64_t grid = warp_grid(P.tiles);
+    if (P.tp_on && (grid > kMaxTpCtas || (P.tiles + grid - 1) / grid * 16 * P.m > P.tp.cap))
+        return cudaErrorNotSupported;
+    size_t smem = 0;
+    if (!wplan<D>(P, grid, &smem)) return cudaErrorNotSupported;
+    auto kern = gemv_warp_kernel<D, XT>;
+    static std::atomic<int> set_for[kWMaxDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= kWMaxDevices) return cudaErrorInvalidDevice;
+    if ((int)smem > set_for[dev].load(std::memory_order_relaxed)) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        int seen = set_for[dev].load(std::memory_order_relaxed);
+        while ((int)smem > seen && !set_for[dev].compare_exchange_weak(seen, (int)smem)) {
+        }
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid);
+    cfg.blockDim = dim3(kWThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = gemv_pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, P);
+}
+
+template <typename XT>
+cudaError_t launch_warp_dtype(const WarpParams& P, int dtype, cudaStream_t s) {
+    switch (dtype) {
+    case kQ4_K: return launch_warp<kQ4_K, XT>(P, s);
+    case kQ6_K: return launch_warp<kQ6_K, XT>(P, s);
+    default: return cudaErrorNotSupported;
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, int count, const void* x, int xtype,
+                             int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
+                             cudaStream_t stream) {
+    if (!warp_enabled() || m < 1 || m > 2 || count < 1 || count > kGroup) return cudaErrorNotSupported;
+    const int dtype = w[0]->dtype;
+    if ((dtype != kQ4_K && dtype != kQ6_K) || w[0]->k < 256) return cudaErrorNotSupported;
+    int* err = device_status_word();
+    if (!err) return cudaErrorNotSupported;
+    WarpParams P = {};
+    P.nmem = count;
+    int64_t tiles = 0;
+    for (int i = 0; i < count; i++) {
+        if (w[i]->dtype != dtype || w[i]->k != w[0]->k || w[i]->k % 256 || rows[i] < 1) return cudaErrorNotSupported;
+        P.mem[i].p = Planes{w[i]->q, w[i]->s, w[i]->d, w[i]->nb};
+        P.mem[i].rows = rows[i];
+        P.mem[i].out = out[i];
+        P.mem[i].ldo = ldo[i];
+        P.mem[i].tile_begin = tiles;
+        tiles += (rows[i] + 15) / 16;
+    }
+    // unit counts per CTA stay far below 2^31 / 16
+    if (tiles > (1 << 24) || w[0]->k / 256 > (1 << 16)) return cudaErrorNotSupported;
+    P.tiles = (int)tiles;
+    P.k = w[0]->k;
+    P.nchunks = (int)(w[0]->k / 256);
+    P.m = (int)m;
+    P.x = x;
+    P.err = err;
+    const int qb = dtype == kQ4_K ? WGeo<kQ4_K>::q : WGeo<kQ6_K>::q;
+    for (int i = 0; i < count; i++)
+        if (!encode_rows(&P.maps[i], w[i]->q, rows[i], (int64_t)P.nchunks * qb, qb)) return cudaErrorNotSupported;
+    if (tp) {
+        P.tp_on = 1;
+        P.tp = *tp;
+    }
+    const int esize = xtype == CLQ_X_F32 ? 4 : 2;
+    P.x_aligned = ((uintptr_t)x % 16 == 0) && ((P.k * esize) % 16 == 0);
+    switch (xtype) {
+    case CLQ_X_F32: return launch_warp_dtype<float>(P, dtype, stream);
+    case CLQ_X_BF16: return launch_warp_dtype<__nv_bfloat16>(P, dtype, stream);
+    case CLQ_X_F16: return launch_warp_dtype<__half>(P, dtype, stream);
+    default: return cudaErrorNotSupported;
+    }
+}
+
+}  // namespace clq

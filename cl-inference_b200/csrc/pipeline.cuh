@@ -1,7 +1,7 @@
 // pipeline.cuh -- shared-memory pipelines fed by the bulk-copy (TMA) engine:
-// mbarrier set-up, arrival, bounded waits, and 1-D cp.async.bulk copies from
-// global to shared memory.  No tensor maps; every copy has one destination,
-// this CTA's shared memory, and reads this GPU's own memory.
+// mbarrier set-up, arrival, bounded waits, 1-D cp.async.bulk copies and 2-D
+// tensor-map box copies from global to shared memory.  Every copy has one
+// destination, this CTA's shared memory, and reads this GPU's own memory.
 //
 // Every wait is bounded.  When a wait gives up it sets the sticky error word
 // (the library's device status, read by clq_device_status) and returns false;
@@ -68,6 +68,33 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, uint32_t b
         "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
             smem_u32(dst)),
         "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+// The box of the 2-D tensor map MAP (a kernel parameter) at (X, Y) -- X the
+// innermost coordinate, in elements, with X times the element size a multiple
+// of 16 bytes -- to shared DST (128-byte aligned); completion is counted on
+// BAR's transaction count (the full box, out-of-range elements zero-filled).
+__device__ __forceinline__ void tensor_copy_2d(void* dst, const void* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+// An L2 policy that marks lines read once (a weight stream) first for
+// eviction, so that they do not push out small, reused data.
+__device__ __forceinline__ uint64_t evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+// tensor_copy_2d with the L2 cache POLICY.
+__device__ __forceinline__ void tensor_copy_2d_hint(void* dst, const void* map, int x, int y, uint64_t* bar,
+                                                    uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+        "%3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
 // Named barrier over the first THREADS threads of the CTA (ID 0 is __syncthreads).
