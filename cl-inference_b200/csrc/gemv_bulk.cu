@@ -245,7 +245,8 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
             const int nks = (pcn + kCW - 1) / kCW;
             if (pass == 0) {
                 grid_dependency_wait();  // activations may come from the previous kernel
-                if (P.tp_on && threadIdx.x == 0) tp_sh[0] = P.tp.epochs[blockIdx.x] + 1u;
+                // read through L2: an SM's L1 may hold a line of epochs from an earlier call
+                if (P.tp_on && threadIdx.x == 0) tp_sh[0] = __ldcg(&P.tp.epochs[blockIdx.x]) + 1u;
             }
             if constexpr (I8) {
                 // each warp restages only its own chunks (after its own units of
@@ -384,7 +385,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
                     const int64_t row = (int64_t)(tile - (int)M.tile_begin) * 16 + (idx & 15);
                     if (!ok || row >= M.rows) continue;
                     if (P.tp_on) {  // this rank's partial, into this CTA's region of every rank
-                        tp_put(P.tp, tp_sh[0], tile - t_begin, ntok, idx, sum);
+                        tp_put(P.tp, tp_sh[0], (int)blockIdx.x, tile - t_begin, ntok, idx, sum);
                     } else {
                         M.out[(int64_t)(idx >> 4) * M.ldo + row] = sum;
                     }
@@ -402,6 +403,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) gemv_bulk_kernel(const __grid
         __syncthreads();
         const uint32_t ep = tp_sh[0];
         tp_gather_sum(P.tp, P.mem[0], t_begin, t_end, ntok, ep, err);
+        __syncthreads();  // every thread has its words before the epoch moves on
         if (threadIdx.x == 0) P.tp.epochs[blockIdx.x] = ep;
     }
 

@@ -488,12 +488,13 @@ __device__ void tp_gather_sum(const TP& tp, const Member& M, int t_begin, int t_
     }
 }
 
-// This rank's partial SUM of output IDX of local tile TL (tile - t_begin), into
-// this CTA's region of every rank's receive buffer.
+// This rank's partial SUM of output IDX of tile TL of CTA index CTA's region
+// (its tiles counted from its first), into that region of every rank's receive
+// buffer, tagged EP (the region owner's epoch).
 template <typename TP>
-__device__ __forceinline__ void tp_put(const TP& tp, uint32_t ep, int64_t tl, int ntok, int idx, float sum) {
+__device__ __forceinline__ void tp_put(const TP& tp, uint32_t ep, int cta, int64_t tl, int ntok, int idx, float sum) {
     const int64_t off =
-        (((int64_t)(ep & 1u) * tp.world + tp.rank) * kMaxTpCtas + blockIdx.x) * tp.cap + tl * ntok * 16 + idx;
+        (((int64_t)(ep & 1u) * tp.world + tp.rank) * kMaxTpCtas + cta) * tp.cap + tl * ntok * 16 + idx;
     for (int q = 0; q < tp.world; q++) st_word(tp.peer_recv[q] + off, ep, sum);
 }
 

@@ -90,15 +90,16 @@ __device__ __forceinline__ void transpose4(uint32_t v0, uint32_t v1, uint32_t v2
 template <int D>
 __device__ __forceinline__ void stage_block_i8(const float (&v)[8], unsigned char* base) {
     const int lane = threadIdx.x & 31;
-    float amax = 0.f;
+    float lmax = 0.f;
 #pragma unroll
-    for (int i = 0; i < 8; i++) amax = fmaxf(amax, fabsf(v[i]));
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    for (int i = 0; i < 8; i++) lmax = fmaxf(lmax, fabsf(v[i]));
+    // the bit patterns of non-negative floats order like the floats: one
+    // warp-wide integer max gives the chunk's largest magnitude
+    const uint32_t amax_bits = __reduce_max_sync(0xffffffffu, __float_as_uint(lmax));
     int e = 0;
-    if (amax > 0.f) {
+    if (amax_bits != 0u) {
         // amax * 2^e in [2^29, 2^30): four balanced digits always suffice
-        e = 29 - ((int)((__float_as_uint(amax) >> 23) & 255) - 127);
+        e = 29 - ((int)((amax_bits >> 23) & 255) - 127);
         e = e < -100 ? -100 : (e > 120 ? 120 : e);
     }
     const float sc = __uint_as_float((uint32_t)(127 + e) << 23);  // 2^e, a normal float for e in [-100, 120]

@@ -136,7 +136,8 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
     while (issued < u1 && issued < u0 + kWPreWait) issue();
 
     grid_dependency_wait();  // the activations may come from the previous kernel
-    if (threadIdx.x == 0 && P.tp_on) ep_sh[0] = P.tp.epochs[blockIdx.x] + 1u;
+    // read through L2: an SM's L1 may hold a line of epochs from an earlier call
+    if (threadIdx.x == 0 && P.tp_on) ep_sh[0] = __ldcg(&P.tp.epochs[blockIdx.x]) + 1u;
     for (int i = threadIdx.x; i < t_end - t_begin; i += kWThreads) cnt[i] = 0;
     stage_x_i8<D, XT, kWW>(P.x, P.k, P.x_aligned, 0, nch, ntok, xstage, [&]() {
         while (issued < u1 && issued < u0 + depth) issue();
@@ -249,7 +250,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
                     for (int w = wf; w <= wl; w++) sum += piece[((w + tl) * ntok) * 16 + idx];
                     const int64_t row = (int64_t)(tile - (int)M.tile_begin) * 16 + (idx & 15);
                     if (row >= M.rows) continue;
-                    if (P.tp_on) tp_put(P.tp, ep_sh[0], tl, ntok, idx, sum);
+                    if (P.tp_on) tp_put(P.tp, ep_sh[0], (int)blockIdx.x, tl, ntok, idx, sum);
                     else M.out[(int64_t)(idx >> 4) * M.ldo + row] = sum;
                 }
             }
@@ -273,6 +274,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
         __syncthreads();
         const uint32_t ep = ep_sh[0];
         tp_gather_sum(P.tp, P.mem[0], t_begin, t_end, ntok, ep, err);
+        __syncthreads();  // every thread has its words before the epoch moves on
         if (threadIdx.x == 0) P.tp.epochs[blockIdx.x] = ep;
     }
 }
