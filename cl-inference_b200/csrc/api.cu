@@ -186,17 +186,27 @@ struct DeviceBuffer {
 
 // Page-locked host staging: pageable copies make the driver stage through its
 // own buffer on every call, which dominates small decode-sized products.
+// Page-locked host memory, mapped into the device's address space: kernels
+// can store into it directly (dptr), with no copy back.
 struct PinnedBuffer {
     void* ptr = nullptr;
+    void* dptr = nullptr;
     size_t cap = 0;
     cudaError_t ensure(size_t bytes) {
         if (bytes <= cap) return cudaSuccess;
         if (ptr) cudaFreeHost(ptr);
-        ptr = nullptr; cap = 0;
+        ptr = dptr = nullptr; cap = 0;
         size_t want = bytes < 65536 ? 65536 : bytes + bytes / 4;
-        cudaError_t e = cudaMallocHost(&ptr, want);
-        if (e == cudaSuccess) cap = want;
-        return e;
+        cudaError_t e = cudaHostAlloc(&ptr, want, cudaHostAllocMapped);
+        if (e != cudaSuccess) return e;
+        e = cudaHostGetDevicePointer(&dptr, ptr, 0);
+        if (e != cudaSuccess) {
+            cudaFreeHost(ptr);
+            ptr = dptr = nullptr;
+            return e;
+        }
+        cap = want;
+        return cudaSuccess;
     }
 };
 
@@ -495,22 +505,24 @@ int clq_matmul(int dtype, float* out, const float* x, const uint8_t* bytes, int6
     cudaError_t e;
     if ((e = ctx->x.ensure(xbytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(x)");
     if ((e = ctx->out.ensure(obytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(out)");
-    // small products (decode) go through page-locked staging; large ones copy
-    // straight from and to the caller's memory
+    // small products (decode): x goes through page-locked staging and the
+    // kernel stores its outputs straight into mapped page-locked memory (no
+    // copy back); large ones copy from and to the caller's memory
     const bool staged = xbytes + obytes <= ((size_t)8 << 20);
     if (staged) {
-        if ((e = ctx->hx.ensure(xbytes)) != cudaSuccess) return cuda_fail(e, "cudaMallocHost(x)");
-        if ((e = ctx->hout.ensure(obytes)) != cudaSuccess) return cuda_fail(e, "cudaMallocHost(out)");
+        if ((e = ctx->hx.ensure(xbytes)) != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(x)");
+        if ((e = ctx->hout.ensure(obytes)) != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(out)");
         std::memcpy(ctx->hx.ptr, x, xbytes);
     }
     if ((e = cudaMemcpyAsync(ctx->x.ptr, staged ? ctx->hx.ptr : x, xbytes, cudaMemcpyHostToDevice, ctx->stream)) !=
         cudaSuccess)
         return cuda_fail(e, "copy x to device");
-    if ((e = clq::launch_linear(view_of(store.get(), row_begin), n, ctx->x.ptr, CLQ_X_F32, m,
-                                (float*)ctx->out.ptr, n, flags & CLQ_MATH_FAST, ctx->stream)) != cudaSuccess)
+    float* dout = staged ? (float*)ctx->hout.dptr : (float*)ctx->out.ptr;
+    if ((e = clq::launch_linear(view_of(store.get(), row_begin), n, ctx->x.ptr, CLQ_X_F32, m, dout, n,
+                                flags & CLQ_MATH_FAST, ctx->stream)) != cudaSuccess)
         return cuda_fail(e, "linear kernel launch");
-    if ((e = cudaMemcpyAsync(staged ? ctx->hout.ptr : out, ctx->out.ptr, obytes, cudaMemcpyDeviceToHost,
-                             ctx->stream)) != cudaSuccess)
+    if (!staged && (e = cudaMemcpyAsync(out, ctx->out.ptr, obytes, cudaMemcpyDeviceToHost, ctx->stream)) !=
+                       cudaSuccess)
         return cuda_fail(e, "copy out to host");
     if ((e = cudaStreamSynchronize(ctx->stream)) != cudaSuccess) return cuda_fail(e, "linear");
     if (staged) std::memcpy(out, ctx->hout.ptr, obytes);

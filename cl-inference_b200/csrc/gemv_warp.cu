@@ -29,6 +29,7 @@
 #include <atomic>
 #include <cstdlib>
 #include <mutex>
+#include <unordered_map>
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -305,6 +306,37 @@ bool encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t row_b
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Encoded maps, per thread, by (base, rows, row bytes, box): a map is a pure
+// function of these, so an entry never goes stale.  Decode calls one weight at
+// a time, so the per-call encode is the common case to avoid.
+struct MapKey {
+    const void* base;
+    int64_t rows, row_bytes;
+    int box;
+    bool operator==(const MapKey& o) const {
+        return base == o.base && rows == o.rows && row_bytes == o.row_bytes && box == o.box;
+    }
+};
+struct MapKeyHash {
+    size_t operator()(const MapKey& k) const {
+        return std::hash<const void*>()(k.base) ^ (std::hash<int64_t>()(k.rows) * 31) ^
+               (std::hash<int64_t>()(k.row_bytes) * 131) ^ (size_t)k.box;
+    }
+};
+bool cached_encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box) {
+    thread_local std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
+    const MapKey key{base, rows, row_bytes, box};
+    auto it = cache.find(key);
+    if (it != cache.end()) {
+        *map = it->second;
+        return true;
+    }
+    if (!encode_rows(map, base, rows, row_bytes, box)) return false;
+    if (cache.size() >= 4096) cache.clear();
+    cache.emplace(key, *map);
+    return true;
+}
+
 bool warp_enabled() {
     static int on = -1;
     if (on < 0) {
@@ -434,7 +466,8 @@ cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, in
     P.err = err;
     const int qb = dtype == kQ4_K ? WGeo<kQ4_K>::q : WGeo<kQ6_K>::q;
     for (int i = 0; i < count; i++)
-        if (!encode_rows(&P.maps[i], w[i]->q, rows[i], (int64_t)P.nchunks * qb, qb)) return cudaErrorNotSupported;
+        if (!cached_encode_rows(&P.maps[i], w[i]->q, rows[i], (int64_t)P.nchunks * qb, qb))
+            return cudaErrorNotSupported;
     if (tp) {
         P.tp_on = 1;
         P.tp = *tp;
