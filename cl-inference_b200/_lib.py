@@ -18,6 +18,7 @@ STATUS_NAMES = {
     0: "CLQ_OK", 1: "CLQ_ERR_ARGUMENT", 2: "CLQ_ERR_SHAPE", 3: "CLQ_ERR_BLOCKS",
     4: "CLQ_ERR_NONFINITE_SCALE", 5: "CLQ_ERR_CUDA", 6: "CLQ_ERR_NCCL", 7: "CLQ_ERR_TIMEOUT",
     8: "CLQ_ERR_NO_DEVICE", 9: "CLQ_ERR_UNSUPPORTED", 10: "CLQ_ERR_OUT_OF_MEMORY",
+    11: "CLQ_ERR_FORMAT", 12: "CLQ_ERR_IO",
 }
 
 _i64 = ctypes.c_int64
@@ -53,6 +54,20 @@ SIGNATURES = {
     "clq_ipc_handle": (_int, [_ptr, _ptr]),
     "clq_ipc_open": (_int, [_ptr, ctypes.POINTER(_ptr)]),
     "clq_ipc_close": (_int, [_ptr]),
+    "clq_gguf_open": (_int, [ctypes.c_char_p, _ptr]),
+    "clq_gguf_close": (_int, [_ptr]),
+    "clq_gguf_tensor_count": (_int, [_ptr, ctypes.POINTER(_i64)]),
+    "clq_gguf_tensor_info": (_int, [_ptr, _i64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_int),
+                                    ctypes.POINTER(_int), ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_uint64),
+                                    ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_ptr)]),
+    "clq_gguf_find_tensor": (_int, [_ptr, ctypes.c_char_p, ctypes.POINTER(_i64)]),
+    "clq_gguf_metadata_count": (_int, [_ptr, ctypes.POINTER(_i64)]),
+    "clq_gguf_metadata_key": (_int, [_ptr, _i64, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(_int)]),
+    "clq_gguf_metadata_value": (_int, [_ptr, ctypes.c_char_p, ctypes.POINTER(_int), ctypes.POINTER(ctypes.c_uint64),
+                                       ctypes.POINTER(_i64), ctypes.POINTER(ctypes.c_double),
+                                       ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_uint64),
+                                       ctypes.POINTER(_int), ctypes.POINTER(ctypes.c_uint64)]),
+    "clq_gguf_store": (_int, [_ptr, _i64, _ptr]),
     "clq_tp_create": (_int, [_int, _int, _i64, _ptr, _ptr, ctypes.POINTER(_ptr)]),
     "clq_tp_free": (_int, [_ptr]),
     "clq_linear_allreduce_device": (_int, [_ptr, _i64, _i64, _ptr, _int, _i64, _ptr, _i64, _ptr, _ptr]),

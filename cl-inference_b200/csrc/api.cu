@@ -293,6 +293,16 @@ int cached_store(int dtype, int64_t n, int64_t k, const uint8_t* bytes, int devi
 
 }  // namespace
 
+int clq::set_error(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    t_last_error = buf;
+    return code;
+}
+
 // Sticky per-device status word: a kernel whose bounded wait expires records a
 // CLQ_ERR_* code here and every later wait on the device falls through at once;
 // clq_device_status reads and clears it.

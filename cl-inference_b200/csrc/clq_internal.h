@@ -21,6 +21,9 @@ struct WeightView {
 
 bool geometry(int dtype, int* elems, int* block_bytes);
 
+// Records the formatted message as this thread's clq_last_error and returns CODE.
+int set_error(int code, const char* fmt, ...);
+
 // Re-tile NBLOCKS native GGUF blocks (N rows of NB blocks) into the planes at
 // DST (layout.cuh); the planes' tail must be zeroed by the caller.
 cudaError_t launch_retile(const uint8_t* native, int dtype, int64_t n, int64_t nb, uint8_t* dst,

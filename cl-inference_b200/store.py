@@ -47,6 +47,15 @@ class Store:
             raise TypeError("store data must be a uint8 numpy array or a uint8 CUDA tensor")
         self._handle = handle
 
+    @classmethod
+    def from_handle(cls, dtype, n, k, handle):
+        """Wrap a clq_store made elsewhere (clq_gguf_store); the Store owns it."""
+        self = cls.__new__(cls)
+        self.dtype = find_dtype(dtype)
+        self.n, self.k = int(n), int(k)
+        self._handle = handle
+        return self
+
     @property
     def handle(self):
         if self._handle is None:

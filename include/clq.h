@@ -44,7 +44,9 @@ enum clq_status {
     CLQ_ERR_TIMEOUT = 7,        /* a bounded wait ran out                            */
     CLQ_ERR_NO_DEVICE = 8,      /* no usable sm_100 device                           */
     CLQ_ERR_UNSUPPORTED = 9,    /* valid request this build does not implement       */
-    CLQ_ERR_OUT_OF_MEMORY = 10
+    CLQ_ERR_OUT_OF_MEMORY = 10,
+    CLQ_ERR_FORMAT = 11,        /* malformed GGUF file (gguf/reader.lisp's gguf-error) */
+    CLQ_ERR_IO = 12             /* a file could not be opened or mapped              */
 };
 
 /* Store creation flags. */
@@ -209,6 +211,48 @@ int clq_gather_device(const clq_store *w, const int32_t *ids, int64_t count, flo
 int clq_dequantize(int dtype, const uint8_t *bytes, size_t nbytes, float *out);
 int clq_take(int dtype, const uint8_t *bytes, int64_t n, int64_t k, const int32_t *ids,
              int64_t count, float *out);
+
+/* ---- GGUF files -> device stores ------------------------------------------
+ * clq_gguf_open maps a little-endian GGUF v3 file read-only and parses its
+ * header with the checks of gguf/reader.lisp (parse-gguf, :167-196; replaces
+ * open-gguf of gguf/weights.lisp:18-30 for the packed weights): magic and
+ * version, u64 counts bounded by the bytes left, UTF-8 strings, metadata types
+ * 0..12 nested at most 32 deep, booleans 0 or 1, no duplicate keys or tensors,
+ * ranks 1..4 of positive dimensions, known ggml types, rows of whole blocks, a
+ * power-of-two general.alignment of at most 4096 (default 32), and aligned,
+ * non-overlapping tensors inside the file.  Malformed files fail with
+ * CLQ_ERR_FORMAT, unreadable ones with CLQ_ERR_IO.  Names, strings and tensor
+ * bytes handed out point into FILE and stay valid until clq_gguf_close.
+ */
+typedef struct clq_gguf clq_gguf;
+int clq_gguf_open(const char *path, clq_gguf **out);
+int clq_gguf_close(clq_gguf *file);
+int clq_gguf_tensor_count(const clq_gguf *file, int64_t *count);
+/* Tensor INDEX in file order: name, ggml type id, rank, dimensions in the
+ * file's order (dims[0] = row length; unused ones are 1), offset in the data
+ * section, byte count, and its bytes in the mapping (the :u8 view of
+ * weights-make-bytes, gguf/weights.lisp:71-74).  Any output may be NULL. */
+int clq_gguf_tensor_info(const clq_gguf *file, int64_t index, const char **name, int *ggml_type,
+                         int *rank, int64_t dims[4], uint64_t *offset, uint64_t *nbytes,
+                         const uint8_t **bytes);
+int clq_gguf_find_tensor(const clq_gguf *file, const char *name, int64_t *index);
+/* Metadata keys in file order, with their value types (0..12). */
+int clq_gguf_metadata_count(const clq_gguf *file, int64_t *count);
+int clq_gguf_metadata_key(const clq_gguf *file, int64_t index, const char **key, int *type);
+/* The value of KEY: unsigned integers and booleans in *uvalue, signed integers
+ * in *ivalue, floats in *fvalue, strings as (*svalue, *slen); for an array
+ * (type 9) its element type and length (elements are not kept).  Any output
+ * may be NULL. */
+int clq_gguf_metadata_value(const clq_gguf *file, const char *key, int *type, uint64_t *uvalue,
+                            int64_t *ivalue, double *fvalue, const char **svalue, uint64_t *slen,
+                            int *elem_type, uint64_t *count);
+/* Tensor INDEX (Q4_0, Q8_0, Q4_K or Q6_K; N = dims[1] * dims[2] * dims[3]
+ * rows of K = dims[0]) as a store on the current device: the bytes are read
+ * from the file into two page-locked staging buffers in turn, one filled while
+ * the other's asynchronous copy runs, and are then checked and re-tiled as
+ * clq_store_create does (CLQ_ERR_NONFINITE_SCALE for an fp16 scale with
+ * exponent 31).  Other types: CLQ_ERR_UNSUPPORTED. */
+int clq_gguf_store(clq_gguf *file, int64_t index, clq_store **out);
 
 #ifdef __cplusplus
 }
