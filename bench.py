@@ -74,6 +74,10 @@ def parse():
     ap.add_argument("--allreduce", choices=["fused", "nccl"], default="fused",
                     help="tensor parallel: row-parallel linears all-reduce inside the GEMV over NVLink "
                          "(fused) or through NCCL after it")
+    ap.add_argument("--fusions", choices=["off", "fused", "unfused"], default="off",
+                    help="run each layer with the reference's data flow around the linears (RMSNorm -> q/k/v, "
+                         "o + residual, RMSNorm -> gate/up, SwiGLU -> down + residual; no attention): fused into "
+                         "the GEMVs (clq_linear_fused_device), or as torch element-wise ops between plain linears")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -276,7 +280,51 @@ def run_clq(args):
             return got
         comm = tpcomm.TpComm(rank, world, exchange, cap=max(4096, 16 * m * (cfg["hidden"] // 16 // 100 + 1)))
 
-    def step():
+    fuse_mode = args.fusions if (args.workload == "step" and world == 1) else "off"
+    if fuse_mode != "off":
+        if xdtype != torch.float32:
+            raise SystemExit("--fusions runs the fp32 decode data flow")
+        # the residual stream (each layer's input, updated in place), the RMSNorm
+        # weights, and the layer data flow of local/blocks.lisp:115-116, 151-154,
+        # 387-392; every step restarts from the same stream
+        hidden = cfg["hidden"]
+        resid0 = torch.randn(m, hidden, device="cuda", generator=gen)
+        resid = resid0.clone()
+        norm_w = torch.rand(hidden, device="cuda", generator=gen) + 0.5
+        per_layer = len(tp.layer_linears(cfg))
+
+        def rms(v):
+            return v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + 1e-5) * norm_w
+
+        def step():
+            resid.copy_(resid0)
+            for layer in range(cfg["layers"]):
+                b = layer * per_layer
+                q, kk, v, o, gt, up, dn = (stores[b + j][0] for j in range(7))
+                if fuse_mode == "fused":
+                    clq.linear_group_fused([q, kk, v], resid, norm_weight=norm_w, eps=1e-5,
+                                           outs=[outs[b], outs[b + 1], outs[b + 2]])
+                    clq.linear_fused(o, inputs["attn"], out=resid, residual=resid)
+                    clq.linear_group_fused([gt, up], resid, norm_weight=norm_w, eps=1e-5,
+                                           outs=[outs[b + 4], outs[b + 5]])
+                    clq.linear_fused(dn, outs[b + 5], gate=outs[b + 4], out=resid, residual=resid)
+                else:
+                    clq.linear_group([q, kk, v], rms(resid), outs=[outs[b], outs[b + 1], outs[b + 2]])
+                    o.linear(inputs["attn"], out=outs[b + 3])
+                    resid.add_(outs[b + 3])
+                    clq.linear_group([gt, up], rms(resid), outs=[outs[b + 4], outs[b + 5]])
+                    dn.linear(torch.nn.functional.silu(outs[b + 4]) * outs[b + 5], out=outs[b + 6])
+                    resid.add_(outs[b + 6])
+            head = stores[-1][0]
+            if fuse_mode == "fused":
+                clq.linear_fused(head, resid, norm_weight=norm_w, eps=1e-5, out=outs[-1])
+            else:
+                head.linear(rms(resid), out=outs[-1])
+    else:
+        def step():
+            step_linears()
+
+    def step_linears():
         for idx in groups:
             if comm is not None and stores[idx[0]][3] == "cols":
                 store = stores[idx[0]][0]
@@ -398,6 +446,9 @@ def run_clq(args):
                              + f"; M={m}, {xtype} activations; {len(stores) // len(SWEEPS[args.workload])} weight copies"),
                 "m": m, "xtype": xtype, "layers": cfg["layers"], "parallelism": f"tp{world}",
                 "allreduce": (args.allreduce if world > 1 else None),
+                "fusions": (None if fuse_mode == "off" else
+                            fuse_mode + ": RMSNorm->q/k/v, o+residual, RMSNorm->gate/up, SwiGLU->down+residual, "
+                                        "RMSNorm->head"),
                 "weights_gb": round(job_bytes / 1e9, 3),
                 "l2": "weights per step far above the 126 MB L2; no flush",
             },

@@ -11,7 +11,7 @@ from .quant import (DTYPES, PackedDtype, PackedError, PackedStorage, PackedTenso
                     make_packed_storage, make_q4_0_storage, make_q4_k_storage, make_q6_k_storage,
                     make_q8_0_storage, make_tensor_view, matmul, slice_rows, take, take_dequantized,
                     transpose)
-from .store import Store, linear_group
+from .store import Store, linear_fused, linear_group, linear_group_fused
 
 __all__ = [
     "ClqError", "DTYPES", "PackedDtype", "PackedError", "PackedStorage", "PackedTensor", "Store",

@@ -54,6 +54,10 @@ SIGNATURES = {
     "clq_ipc_handle": (_int, [_ptr, _ptr]),
     "clq_ipc_open": (_int, [_ptr, ctypes.POINTER(_ptr)]),
     "clq_ipc_close": (_int, [_ptr]),
+    "clq_linear_fused_device": (_int, [_ptr, _i64, _i64, _ptr, _int, _i64, _ptr, _ptr, _i64, ctypes.c_uint, _ptr]),
+    "clq_linear_group_fused_device": (_int, [ctypes.POINTER(_ptr), ctypes.POINTER(_i64), ctypes.POINTER(_i64), _int,
+                                             _ptr, _int, _i64, _ptr, ctypes.POINTER(_ptr), ctypes.POINTER(_i64),
+                                             ctypes.c_uint, _ptr]),
     "clq_gguf_open": (_int, [ctypes.c_char_p, _ptr]),
     "clq_gguf_close": (_int, [_ptr]),
     "clq_gguf_tensor_count": (_int, [_ptr, ctypes.POINTER(_i64)]),

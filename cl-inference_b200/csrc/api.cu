@@ -1,6 +1,7 @@
 // api.cu -- the C ABI of libclq (include/clq.h): status codes, the device
 // store, the host-range weight cache behind the drop-in kernels, and the
 // per-thread stream and staging buffers for host-pointer calls.
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -464,6 +465,97 @@ int clq_linear_group_device(const clq_store* const* w, const int64_t* row_begin,
     cudaError_t e = clq::launch_gemv_mma_group(vp, rows, count, x, xtype, m, out, ldo, (cudaStream_t)stream);
     if (e != cudaSuccess) return cuda_fail(e, "grouped linear kernel launch");
     return CLQ_OK;
+}
+
+int clq_linear_group_fused_device(const clq_store* const* w, const int64_t* row_begin, const int64_t* rows,
+                                  int count, const void* x, int xtype, int64_t m, const clq_fusion* fusion,
+                                  float* const* out, const int64_t* ldo, unsigned flags, void* stream) {
+    if (!fusion || (!fusion->norm_weight && !fusion->gate && !fusion->residual)) {
+        if (count == 1 && w && row_begin && rows && out && ldo)
+            return clq_linear_device(w[0], row_begin[0], rows[0], x, xtype, m, out[0], ldo[0], flags, stream);
+        return clq_linear_group_device(w, row_begin, rows, count, x, xtype, m, out, ldo, flags, stream);
+    }
+    if (count < 1 || count > 4) return fail(CLQ_ERR_ARGUMENT, "group of %d weights (1..4 allowed)", count);
+    if (!w || !row_begin || !rows || !out || !ldo) return fail(CLQ_ERR_ARGUMENT, "null group array");
+    if (xtype != CLQ_X_F32 && xtype != CLQ_X_BF16 && xtype != CLQ_X_F16)
+        return fail(CLQ_ERR_ARGUMENT, "unknown activation type %d", xtype);
+    if (flags & ~(CLQ_MATH_FAST)) return fail(CLQ_ERR_ARGUMENT, "unknown product flags 0x%x", flags);
+    if (fusion->residual && count != 1) return fail(CLQ_ERR_ARGUMENT, "a residual needs a single weight");
+    if (!(fusion->norm_epsilon >= 0.f) || fusion->norm_epsilon == INFINITY)
+        return fail(CLQ_ERR_ARGUMENT, "RMSNorm epsilon must be finite and non-negative");
+    for (int i = 0; i < count; i++) {
+        if (!w[i]) return fail(CLQ_ERR_ARGUMENT, "null store %d in group", i);
+        if (w[i]->dtype != w[0]->dtype || w[i]->k != w[0]->k)
+            return fail(CLQ_ERR_SHAPE, "group members need one dtype and row length");
+        if (row_begin[i] < 0 || rows[i] < 0 || row_begin[i] + rows[i] > w[i]->n || ldo[i] < rows[i])
+            return fail(CLQ_ERR_SHAPE, "member %d: rows [%lld, %lld), output stride %lld for a (%lld %lld) weight", i,
+                        (long long)row_begin[i], (long long)(row_begin[i] + rows[i]), (long long)ldo[i],
+                        (long long)w[i]->n, (long long)w[i]->k);
+    }
+    if (fusion->residual && fusion->ldr < rows[0])
+        return fail(CLQ_ERR_SHAPE, "residual stride %lld < rows %lld", (long long)fusion->ldr, (long long)rows[0]);
+    if (m < 0) return fail(CLQ_ERR_SHAPE, "negative activation rows %lld", (long long)m);
+    if (m == 0) return CLQ_OK;
+    if (!x) return fail(CLQ_ERR_ARGUMENT, "null activations");
+    for (int i = 0; i < count; i++)
+        if (rows[i] && !out[i]) return fail(CLQ_ERR_ARGUMENT, "null output %d", i);
+    int device, rc;
+    if ((rc = current_device(&device))) return rc;
+    clq::WeightView views[4];
+    const clq::WeightView* vp[4];
+    for (int i = 0; i < count; i++) {
+        if (w[i]->device != device)
+            return fail(CLQ_ERR_ARGUMENT, "store lives on device %d, current device is %d", w[i]->device, device);
+        views[i] = view_of(w[i], row_begin[i]);
+        vp[i] = &views[i];
+    }
+    const int64_t k = w[0]->k;
+    clq::Fusion f;
+    f.norm_w = fusion->norm_weight;
+    f.norm_eps = fusion->norm_epsilon;
+    f.gate = fusion->gate;
+    f.res = fusion->residual;
+    f.ldr = fusion->ldr;
+    cudaStream_t s = (cudaStream_t)stream;
+    bool nonempty = true;
+    for (int i = 0; i < count; i++) nonempty = nonempty && rows[i] > 0;
+    // the decode kernel applies the fusion itself
+    if (nonempty && k > 0 && k % 256 == 0 && !clq::uses_gemm_tc(views[0], xtype, m, flags)) {
+        cudaError_t e = clq::launch_gemv_warp(vp, rows, count, x, xtype, m, out, ldo, nullptr, s, &f);
+        if (e == cudaSuccess) return CLQ_OK;
+        if (e != cudaErrorNotSupported) return cuda_fail(e, "fused linear kernel launch");
+    }
+    // every other path: the fused input (fp32) into scratch, the plain product,
+    // the residual; a request that takes the tensor-core GEMM keeps it (its
+    // fp32 input then goes through the GEMM's own fp16 staging)
+    float* h = nullptr;
+    float* part = nullptr;
+    cudaError_t e = cudaSuccess;
+    if ((f.norm_w || f.gate) && k > 0) e = cudaMallocAsync((void**)&h, (size_t)(m * k) * sizeof(float), s);
+    if (e == cudaSuccess && f.res) e = cudaMallocAsync((void**)&part, (size_t)(m * rows[0]) * sizeof(float), s);
+    if (e != cudaSuccess) {
+        if (h) cudaFreeAsync(h, s);
+        return cuda_fail(e, "fusion scratch");
+    }
+    if (h && (e = clq::launch_fuse_input(x, xtype, m, k, f, h, s)) != cudaSuccess) rc = cuda_fail(e, "fused input");
+    const void* xin = h ? (const void*)h : x;
+    const int xt = h ? CLQ_X_F32 : xtype;
+    const unsigned pf = (h && clq::uses_gemm_tc(views[0], xtype, m, flags)) ? (flags | CLQ_MATH_FAST) : flags;
+    if (!rc) {
+        if (f.res) rc = clq_linear_device(w[0], row_begin[0], rows[0], xin, xt, m, part, rows[0], pf, stream);
+        else rc = clq_linear_group_device(w, row_begin, rows, count, xin, xt, m, out, ldo, pf, stream);
+    }
+    if (!rc && f.res &&
+        (e = clq::launch_add_residual(out[0], ldo[0], part, rows[0], f.res, f.ldr, m, rows[0], s)) != cudaSuccess)
+        rc = cuda_fail(e, "residual add");
+    if (h) cudaFreeAsync(h, s);
+    if (part) cudaFreeAsync(part, s);
+    return rc;
+}
+
+int clq_linear_fused_device(const clq_store* w, int64_t row_begin, int64_t rows, const void* x, int xtype, int64_t m,
+                            const clq_fusion* fusion, float* out, int64_t ldo, unsigned flags, void* stream) {
+    return clq_linear_group_fused_device(&w, &row_begin, &rows, 1, x, xtype, m, fusion, &out, &ldo, flags, stream);
 }
 
 int clq_dequantize_device(const clq_store* w, int64_t row_begin, int64_t rows, float* out,

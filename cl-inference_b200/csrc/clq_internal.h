@@ -74,12 +74,32 @@ struct TpLink {
 cudaError_t launch_gemv_bulk_allreduce(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
                                        float* out, int64_t ldo, const TpLink& tp, cudaStream_t stream);
 
+// Work fused around a linear (local/blocks.lisp:115-116, 151-154, 387-392):
+// the product's input is h = (gate ? silu(gate) * x : x), then, with norm_w,
+// h * norm_w / sqrt(mean(h^2) + norm_eps) per activation row; with res,
+// out = res + h W^T (res row stride ldr; single-weight calls only).
+struct Fusion {
+    const float* norm_w = nullptr;
+    float norm_eps = 0.f;
+    const void* gate = nullptr;
+    const float* res = nullptr;
+    int64_t ldr = 0;
+    bool any() const { return norm_w || gate || res; }
+};
+
 // The decode GEMV with one weight stream per warp (Q4_K / Q6_K, m <= 2), with
-// the all-reduce over TP's ranks fused in when TP is non-null;
+// the all-reduce over TP's ranks fused in when TP is non-null and the
+// prologue / epilogue of FUSE when that is non-null;
 // cudaErrorNotSupported for shapes it does not take, before anything is launched.
 cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, int count, const void* x, int xtype,
                              int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
-                             cudaStream_t stream);
+                             cudaStream_t stream, const Fusion* fuse = nullptr);
+// The unfused forms, for every other kernel: H (fp32 [m, k]) = the fused input
+// of X; OUT[t, j] = RES[t, j] + PART[t, j] for j < rows (OUT may be RES).
+cudaError_t launch_fuse_input(const void* x, int xtype, int64_t m, int64_t k, const Fusion& f, float* h,
+                              cudaStream_t stream);
+cudaError_t launch_add_residual(float* out, int64_t ldo, const float* part, int64_t ldp, const float* res,
+                                int64_t ldr, int64_t m, int64_t rows, cudaStream_t stream);
 // Streaming multiprocessors of the current device (cached).
 int sm_count();
 

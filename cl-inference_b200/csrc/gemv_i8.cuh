@@ -158,12 +158,17 @@ __device__ __forceinline__ void stage_block_i8(const float (&v)[8], unsigned cha
 
 // AFTER_LOADS() runs once, after the first loads are issued and before any
 // block is converted (a caller's hook to issue more copies behind them).
+// XFORM(u, col, v) may rewrite a lane's eight loaded activations of row U,
+// columns COL.. (a fused prologue), before they are converted.
 struct NoHook {
     __device__ void operator()() const {}
 };
-template <int D, typename XT, int WARPS, typename Hook = NoHook>
+struct NoXform {
+    __device__ void operator()(int, int64_t, float (&)[8]) const {}
+};
+template <int D, typename XT, int WARPS, typename Hook = NoHook, typename Xform = NoXform>
 __device__ void stage_x_i8(const void* xv, int64_t k, int x_aligned, int64_t c0, int pc, int ntok,
-                           unsigned char* stage, Hook after_loads = Hook()) {
+                           unsigned char* stage, Hook after_loads = Hook(), Xform xform = Xform()) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const XT* x = reinterpret_cast<const XT*>(xv);
     constexpr int TB = I8Block<D>::bytes;
@@ -191,7 +196,10 @@ __device__ void stage_x_i8(const void* xv, int64_t k, int x_aligned, int64_t c0,
 #pragma unroll
         for (int b = 0; b < 4; b++) {
             const int i = b0 + b, cc = warp + (i / ntok) * WARPS, u = i - (i / ntok) * ntok;
-            if (i < per) stage_block_i8<D>(vb[b], stage + (size_t)(cc * ntok + u) * TB);
+            if (i < per) {
+                xform(u, (c0 + cc) * 256 + 8 * lane, vb[b]);
+                stage_block_i8<D>(vb[b], stage + (size_t)(cc * ntok + u) * TB);
+            }
         }
     }
     if (per == 0) after_loads();

@@ -51,7 +51,10 @@ using namespace pipe;
 constexpr int kWW = 16;  // warps per CTA
 constexpr int kWThreads = kWW * 32;
 constexpr int kWMaxDepth = 4;
-constexpr int kWHeader = kWW * kWMaxDepth * 8 + 16;  // slot barriers, this call's epoch
+// header: slot barriers, this call's epoch, the fused RMSNorm's per-row scales
+// and its reduction partials
+constexpr int kWEpochOff = kWW * kWMaxDepth * 8, kWNormOff = kWEpochOff + 16, kWRedOff = kWNormOff + 16;
+constexpr int kWHeader = kWRedOff + kWW * 2 * 4;
 constexpr int kWMaxDevices = 64;
 constexpr size_t kWSmemLimit = 227 * 1024;
 // Units each warp copies before waiting for the previous kernel; the rest of
@@ -80,20 +83,31 @@ struct WarpParams {
     int* err;
     int tp_on;
     TpLink tp;
+    // fused prologue / epilogue (the FUSE variant): see Fusion in clq_internal.h
+    const float* norm_w;
+    float norm_eps;
+    const void* gate;
+    int gate_aligned, norm_aligned;
+    const float* res;
+    int64_t ldr;
 };
 
 // The warp whose run holds unit u: runs are [w U / W, (w+1) U / W) for the
 // W = min(16, U) warps in use, all non-empty.
 __device__ __forceinline__ int warp_of(int u, int U, int W) { return (W * (u + 1) + U - 1) / U - 1; }
 
-template <int D, typename XT>
+// The product's input element from activation X and gate G: silu(g) * x with a
+// gate, else x.
+__device__ __forceinline__ float swiglu_in(float x, float g) { return g / (1.f + expf(-g)) * x; }
+
+template <int D, typename XT, bool FUSE>
 __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_constant__ WarpParams P) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int Q = WGeo<D>::q;
     constexpr uint32_t kSlot = 16u * Q;
     constexpr int TB = I8Block<D>::bytes;
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem);
-    uint32_t* ep_sh = reinterpret_cast<uint32_t*>(bars + kWW * kWMaxDepth);
+    uint32_t* ep_sh = reinterpret_cast<uint32_t*>(smem + kWEpochOff);
     int* cnt = reinterpret_cast<int*>(smem + P.cnt_off);
     unsigned char* xstage = smem + P.x_off;
     float* piece = reinterpret_cast<float*>(smem + P.piece_off);
@@ -140,9 +154,66 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
     // read through L2: an SM's L1 may hold a line of epochs from an earlier call
     if (threadIdx.x == 0 && P.tp_on) ep_sh[0] = __ldcg(&P.tp.epochs[blockIdx.x]) + 1u;
     for (int i = threadIdx.x; i < t_end - t_begin; i += kWThreads) cnt[i] = 0;
-    stage_x_i8<D, XT, kWW>(P.x, P.k, P.x_aligned, 0, nch, ntok, xstage, [&]() {
+    auto top_up = [&]() {
         while (issued < u1 && issued < u0 + depth) issue();
-    });
+    };
+    if constexpr (FUSE) {
+        // RMSNorm: 1 / sqrt(mean(h^2) + eps) per activation row, from every
+        // thread's strided share of the row (fixed order: deterministic)
+        float* rn = reinterpret_cast<float*>(smem + kWNormOff);
+        float* red = reinterpret_cast<float*>(smem + kWRedOff);
+        const XT* xg = reinterpret_cast<const XT*>(P.x);
+        const XT* gg = reinterpret_cast<const XT*>(P.gate);
+        if (P.norm_w) {
+            for (int u = 0; u < ntok; u++) {
+                float ss = 0.f;
+                for (int64_t e = threadIdx.x; e < P.k; e += kWThreads) {
+                    float h = xload(xg + (int64_t)u * P.k + e);
+                    if (gg) h = swiglu_in(h, xload(gg + (int64_t)u * P.k + e));
+                    ss = fmaf(h, h, ss);
+                }
+#pragma unroll
+                for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+                if (lane == 0) red[warp * 2 + u] = ss;
+            }
+            __syncthreads();
+            if (threadIdx.x < ntok) {
+                float tot = 0.f;
+                for (int w = 0; w < kWW; w++) tot += red[w * 2 + threadIdx.x];
+                rn[threadIdx.x] = 1.f / sqrtf(tot / (float)P.k + P.norm_eps);
+            }
+            __syncthreads();
+        }
+        auto xform = [&](int u, int64_t col, float (&v)[8]) {
+            if (gg) {
+                float gv[8];
+                const XT* gp = gg + (int64_t)u * P.k + col;
+                if (P.gate_aligned) {
+                    xload8(gp, gv);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) gv[i] = xload(gp + i);
+                }
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[i] = swiglu_in(v[i], gv[i]);
+            }
+            if (P.norm_w) {
+                const float r = rn[u];
+                float wv[8];
+                if (P.norm_aligned) {
+                    xload8(P.norm_w + col, wv);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 8; i++) wv[i] = P.norm_w[col + i];
+                }
+#pragma unroll
+                for (int i = 0; i < 8; i++) v[i] = v[i] * r * wv[i];
+            }
+        };
+        stage_x_i8<D, XT, kWW>(P.x, P.k, P.x_aligned, 0, nch, ntok, xstage, top_up, xform);
+    } else {
+        stage_x_i8<D, XT, kWW>(P.x, P.k, P.x_aligned, 0, nch, ntok, xstage, top_up);
+    }
     __syncthreads();
 
     const I8Lane L8 = i8_lane<D>(ntok);
@@ -251,8 +322,15 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
                     for (int w = wf; w <= wl; w++) sum += piece[((w + tl) * ntok) * 16 + idx];
                     const int64_t row = (int64_t)(tile - (int)M.tile_begin) * 16 + (idx & 15);
                     if (row >= M.rows) continue;
-                    if (P.tp_on) tp_put(P.tp, ep_sh[0], (int)blockIdx.x, tl, ntok, idx, sum);
-                    else M.out[(int64_t)(idx >> 4) * M.ldo + row] = sum;
+                    if (P.tp_on) {
+                        tp_put(P.tp, ep_sh[0], (int)blockIdx.x, tl, ntok, idx, sum);
+                    } else {
+                        float o = sum;
+                        if constexpr (FUSE) {
+                            if (P.res) o += P.res[(int64_t)(idx >> 4) * P.ldr + row];  // single weight only
+                        }
+                        M.out[(int64_t)(idx >> 4) * M.ldo + row] = o;
+                    }
                 }
             }
             if (tile_end) {
@@ -393,14 +471,14 @@ bool wplan(WarpParams& P, int64_t grid, size_t* smem) {
     return false;
 }
 
-template <int D, typename XT>
+template <int D, typename XT, bool FUSE>
 cudaError_t launch_warp(WarpParams P, cudaStream_t stream) {
     const int64_t grid = warp_grid(P.tiles);
     if (P.tp_on && (grid > kMaxTpCtas || (P.tiles + grid - 1) / grid * 16 * P.m > P.tp.cap))
         return cudaErrorNotSupported;
     size_t smem = 0;
     if (!wplan<D>(P, grid, &smem)) return cudaErrorNotSupported;
-    auto kern = gemv_warp_kernel<D, XT>;
+    auto kern = gemv_warp_kernel<D, XT, FUSE>;
     static std::atomic<int> set_for[kWMaxDevices];
     int dev = 0;
     cudaGetDevice(&dev);
@@ -426,10 +504,10 @@ cudaError_t launch_warp(WarpParams P, cudaStream_t stream) {
 }
 
 template <typename XT>
-cudaError_t launch_warp_dtype(const WarpParams& P, int dtype, cudaStream_t s) {
+cudaError_t launch_warp_dtype(const WarpParams& P, int dtype, bool fuse, cudaStream_t s) {
     switch (dtype) {
-    case kQ4_K: return launch_warp<kQ4_K, XT>(P, s);
-    case kQ6_K: return launch_warp<kQ6_K, XT>(P, s);
+    case kQ4_K: return fuse ? launch_warp<kQ4_K, XT, true>(P, s) : launch_warp<kQ4_K, XT, false>(P, s);
+    case kQ6_K: return fuse ? launch_warp<kQ6_K, XT, true>(P, s) : launch_warp<kQ6_K, XT, false>(P, s);
     default: return cudaErrorNotSupported;
     }
 }
@@ -438,8 +516,10 @@ cudaError_t launch_warp_dtype(const WarpParams& P, int dtype, cudaStream_t s) {
 
 cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, int count, const void* x, int xtype,
                              int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
-                             cudaStream_t stream) {
+                             cudaStream_t stream, const Fusion* fuse) {
     if (!warp_enabled() || m < 1 || m > 2 || count < 1 || count > kGroup) return cudaErrorNotSupported;
+    const bool fused = fuse && fuse->any();
+    if (fused && (tp || (fuse->res && count != 1))) return cudaErrorNotSupported;
     const int dtype = w[0]->dtype;
     if ((dtype != kQ4_K && dtype != kQ6_K) || w[0]->k < 256) return cudaErrorNotSupported;
     int* err = device_status_word();
@@ -474,10 +554,19 @@ cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, in
     }
     const int esize = xtype == CLQ_X_F32 ? 4 : 2;
     P.x_aligned = ((uintptr_t)x % 16 == 0) && ((P.k * esize) % 16 == 0);
+    if (fused) {
+        P.norm_w = fuse->norm_w;
+        P.norm_eps = fuse->norm_eps;
+        P.gate = fuse->gate;
+        P.gate_aligned = ((uintptr_t)fuse->gate % 16 == 0) && ((P.k * esize) % 16 == 0);
+        P.norm_aligned = (uintptr_t)fuse->norm_w % 16 == 0;
+        P.res = fuse->res;
+        P.ldr = fuse->ldr;
+    }
     switch (xtype) {
-    case CLQ_X_F32: return launch_warp_dtype<float>(P, dtype, stream);
-    case CLQ_X_BF16: return launch_warp_dtype<__nv_bfloat16>(P, dtype, stream);
-    case CLQ_X_F16: return launch_warp_dtype<__half>(P, dtype, stream);
+    case CLQ_X_F32: return launch_warp_dtype<float>(P, dtype, fused, stream);
+    case CLQ_X_BF16: return launch_warp_dtype<__nv_bfloat16>(P, dtype, fused, stream);
+    case CLQ_X_F16: return launch_warp_dtype<__half>(P, dtype, fused, stream);
     default: return cudaErrorNotSupported;
     }
 }

@@ -224,6 +224,93 @@ cudaError_t launch_gather(const WeightView& w, const int32_t* ids, int64_t count
     return cudaGetLastError();
 }
 
+namespace {
+
+__device__ __forceinline__ float act(const float* p) { return *p; }
+__device__ __forceinline__ float act(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+__device__ __forceinline__ float act(const __half* p) { return __half2float(*p); }
+
+// One CTA per activation row: h = silu(gate) * x (with a gate), then times
+// norm_w / sqrt(mean(h^2) + eps) (with norm_w): the per-element arithmetic of
+// the decode GEMV's fused prologue (its sum of squares runs in another order).
+template <typename XT>
+__global__ void fuse_input_kernel(const XT* x, const XT* gate, const float* norm_w, float eps, int64_t k,
+                                  float* h) {
+    constexpr int T = 256;
+    __shared__ float red[T / 32];
+    const int64_t row = blockIdx.x;
+    const XT* xr = x + row * k;
+    const XT* gr = gate ? gate + row * k : nullptr;
+    float* hr = h + row * k;
+    auto in = [&](int64_t e) {
+        float v = act(xr + e);
+        if (gr) {
+            const float g = act(gr + e);
+            v = g / (1.f + expf(-g)) * v;
+        }
+        return v;
+    };
+    if (!norm_w) {
+        for (int64_t e = threadIdx.x; e < k; e += T) hr[e] = in(e);
+        return;
+    }
+    float ss = 0.f;
+    for (int64_t e = threadIdx.x; e < k; e += T) {
+        const float v = in(e);
+        ss = fmaf(v, v, ss);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+    for (int w = 0; w < T / 32; w++) tot += red[w];
+    const float r = 1.f / sqrtf(tot / (float)k + eps);
+    for (int64_t e = threadIdx.x; e < k; e += T) hr[e] = in(e) * r * norm_w[e];
+}
+
+// out = res + part, element by element (OUT may be RES: each element is read
+// before it is written, by the same thread).
+__global__ void add_residual_kernel(float* out, int64_t ldo, const float* part, int64_t ldp, const float* res,
+                                    int64_t ldr, int64_t m, int64_t rows) {
+    const int64_t n = m * rows;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / rows, j = i - t * rows;
+        out[t * ldo + j] = res[t * ldr + j] + part[t * ldp + j];
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_fuse_input(const void* x, int xtype, int64_t m, int64_t k, const Fusion& f, float* h,
+                              cudaStream_t s) {
+    if (m <= 0 || k <= 0) return cudaSuccess;
+    switch (xtype) {
+    case CLQ_X_F32:
+        fuse_input_kernel<float><<<(unsigned)m, 256, 0, s>>>((const float*)x, (const float*)f.gate, f.norm_w,
+                                                             f.norm_eps, k, h);
+        break;
+    case CLQ_X_BF16:
+        fuse_input_kernel<__nv_bfloat16><<<(unsigned)m, 256, 0, s>>>((const __nv_bfloat16*)x,
+                                                                     (const __nv_bfloat16*)f.gate, f.norm_w,
+                                                                     f.norm_eps, k, h);
+        break;
+    case CLQ_X_F16:
+        fuse_input_kernel<__half><<<(unsigned)m, 256, 0, s>>>((const __half*)x, (const __half*)f.gate, f.norm_w,
+                                                              f.norm_eps, k, h);
+        break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_add_residual(float* out, int64_t ldo, const float* part, int64_t ldp, const float* res,
+                                int64_t ldr, int64_t m, int64_t rows, cudaStream_t s) {
+    if (m <= 0 || rows <= 0) return cudaSuccess;
+    add_residual_kernel<<<grid_for(m * rows, kThreads), kThreads, 0, s>>>(out, ldo, part, ldp, res, ldr, m, rows);
+    return cudaGetLastError();
+}
+
 cudaError_t launch_linear_generic(const WeightView& w, int64_t rows, const void* x, int xtype,
                                   int64_t m, float* out, int64_t ldo, cudaStream_t s) {
     if (rows <= 0 || m <= 0) return cudaSuccess;

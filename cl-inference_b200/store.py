@@ -118,6 +118,79 @@ class Store:
         return out
 
 
+class _Fusion(ctypes.Structure):
+    _fields_ = [("norm_weight", ctypes.c_void_p), ("norm_epsilon", ctypes.c_float), ("gate", ctypes.c_void_p),
+                ("residual", ctypes.c_void_p), ("ldr", ctypes.c_int64)]
+
+
+def _fusion(x, norm_weight, eps, gate, residual):
+    """The clq_fusion of the optional fp32 [K] NORM_WEIGHT, GATE (x's type and
+    shape) and fp32 RESIDUAL; the tensors are returned to keep them alive."""
+    torch = _torch()
+    keep = []
+    f = _Fusion(None, float(eps), None, None, 0)
+    if norm_weight is not None:
+        norm_weight = norm_weight.to(device=x.device, dtype=torch.float32).contiguous()
+        if norm_weight.numel() != x.shape[1]:
+            raise ValueError(f"norm weight has {norm_weight.numel()} elements for rows of {x.shape[1]}")
+        f.norm_weight = norm_weight.data_ptr()
+        keep.append(norm_weight)
+    if gate is not None:
+        if gate.shape != x.shape or gate.dtype != x.dtype or not gate.is_cuda:
+            raise ValueError("gate must match x's shape, type and device")
+        gate = gate.contiguous()
+        f.gate = gate.data_ptr()
+        keep.append(gate)
+    if residual is not None:
+        if residual.dtype != torch.float32 or residual.dim() != 2 or residual.stride(1) != 1:
+            raise ValueError("residual must be an fp32 [m, n] matrix with unit column stride")
+        f.residual = residual.data_ptr()
+        f.ldr = residual.stride(0)
+        keep.append(residual)
+    return f, keep
+
+
+def linear_fused(store, x, out=None, norm_weight=None, eps=1e-5, gate=None, residual=None, row_begin=0, rows=None,
+                 flags=0, stream=None):
+    """out = h(x) . W^T (+ residual) with the RMSNorm / SwiGLU prologue and the
+    residual epilogue of clq_linear_fused_device."""
+    torch = _torch()
+    rows = store.n - row_begin if rows is None else rows
+    x = x.contiguous()
+    m = x.shape[0]
+    if out is None:
+        out = torch.empty((m, rows), dtype=torch.float32, device=x.device)
+    f, keep = _fusion(x, norm_weight, eps, gate, residual)
+    xtype = _XTYPE.get(str(x.dtype).replace("torch.", ""))
+    _lib.check(_lib.lib.clq_linear_fused_device(store.handle, row_begin, rows, x.data_ptr(), xtype, m,
+                                                ctypes.byref(f), out.data_ptr(), out.stride(0), flags,
+                                                stream if stream is not None else current_stream_handle()))
+    del keep
+    return out
+
+
+def linear_group_fused(stores, x, norm_weight=None, eps=1e-5, gate=None, outs=None, flags=0, stream=None):
+    """linear_group over the fused input h(x) (clq_linear_group_fused_device)."""
+    torch = _torch()
+    n = len(stores)
+    x = x.contiguous()
+    m = x.shape[0]
+    if outs is None:
+        outs = [torch.empty((m, s.n), dtype=torch.float32, device=x.device) for s in stores]
+    f, keep = _fusion(x, norm_weight, eps, gate, None)
+    handles = (ctypes.c_void_p * n)(*[s.handle.value for s in stores])
+    begins = (ctypes.c_int64 * n)(*([0] * n))
+    rows = (ctypes.c_int64 * n)(*[o.shape[1] for o in outs])
+    optrs = (ctypes.c_void_p * n)(*[o.data_ptr() for o in outs])
+    ldos = (ctypes.c_int64 * n)(*[o.stride(0) for o in outs])
+    xtype = _XTYPE.get(str(x.dtype).replace("torch.", ""))
+    _lib.check(_lib.lib.clq_linear_group_fused_device(handles, begins, rows, n, x.data_ptr(), xtype, m,
+                                                      ctypes.byref(f), optrs, ldos, flags,
+                                                      stream if stream is not None else current_stream_handle()))
+    del keep
+    return outs
+
+
 def linear_group(stores, x, outs=None, flags=0, stream=None):
     """One launch for up to 4 stores of one dtype and K that read the same x
     (clq_linear_group_device); returns the list of [m, rows] outputs."""

@@ -193,6 +193,36 @@ int clq_tp_free(clq_tp *tp);
 int clq_linear_allreduce_device(const clq_store *w, int64_t row_begin, int64_t rows, const void *x, int xtype,
                                 int64_t m, float *out, int64_t ldo, clq_tp *tp, void *stream);
 
+/* ---- work fused around the linear -----------------------------------------
+ * The product's input is h, derived from X per activation row; OUT = h W^T,
+ * plus a residual (local/blocks.lisp: the RMSNorm of apply-rmsnorm :115-116,
+ * run ahead of q/k/v, gate/up and the head; the SwiGLU product silu(gate) * up
+ * fed to the down projection, :151-154; the residual add of layer-forward,
+ * :387-392):
+ *   gate        (optional, X's type and shape)  h = silu(gate) * x, silu(g) = g / (1 + e^-g);
+ *   norm_weight (optional, fp32 [K])            h = h * norm_weight / sqrt(mean(h^2) + norm_epsilon);
+ *   residual    (optional, fp32 [m, ldr])       OUT = residual + h W^T (single weight only; OUT may
+ *                                               be the residual itself).
+ * The decode GEMV (Q4_K / Q6_K, up to two activation rows) applies these in
+ * its activation staging and tile epilogue, with no extra launch or round
+ * trip; other shapes run the same arithmetic as separate kernels on the
+ * stream (scratch from the stream-ordered pool).  Asynchronous on STREAM.
+ */
+typedef struct clq_fusion {
+    const float *norm_weight;
+    float norm_epsilon;
+    const void *gate;
+    const float *residual;
+    int64_t ldr;
+} clq_fusion;
+int clq_linear_fused_device(const clq_store *w, int64_t row_begin, int64_t rows, const void *x, int xtype,
+                            int64_t m, const clq_fusion *fusion, float *out, int64_t ldo, unsigned flags,
+                            void *stream);
+/* clq_linear_group_device with a fusion (no residual): q/k/v or gate/up from one normalized input. */
+int clq_linear_group_fused_device(const clq_store *const *w, const int64_t *row_begin, const int64_t *rows,
+                                  int count, const void *x, int xtype, int64_t m, const clq_fusion *fusion,
+                                  float *const *out, const int64_t *ldo, unsigned flags, void *stream);
+
 /* ---- dequantize and gather ------------------------------------------------
  * Bit-exact fp32 values of packed-element (quant/packed.lisp:85-108) and the
  * Q8_0 dequantize-executor (quant/q8-0.lisp:98-123).
