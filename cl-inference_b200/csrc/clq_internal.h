@@ -87,9 +87,9 @@ struct Fusion {
     bool any() const { return norm_w || gate || res; }
 };
 
-// The decode GEMV with one weight stream per warp (Q4_K / Q6_K, m <= 2), with
+// The decode GEMV with one weight stream per warp (Q4_K / Q6_K, m <= 8), with
 // the all-reduce over TP's ranks fused in when TP is non-null and the
-// prologue / epilogue of FUSE when that is non-null;
+// prologue / epilogue of FUSE (m <= 2) when that is non-null;
 // cudaErrorNotSupported for shapes it does not take, before anything is launched.
 cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, int count, const void* x, int xtype,
                              int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,

@@ -588,7 +588,7 @@ cudaError_t launch_gemv_bulk_impl(const WeightView* const* w, const int64_t* row
                                   int xtype, int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
                                   cudaStream_t stream) {
     if (!bulk_enabled() || m < 1 || m > 8 || count < 1 || count > kGroup) return cudaErrorNotSupported;
-    // one and two activation rows of Q4_K / Q6_K: the per-warp streams when their plan fits
+    // up to eight activation rows of Q4_K / Q6_K: the per-warp streams when their plan fits
     const cudaError_t ew = launch_gemv_warp(w, rows, count, x, xtype, m, out, ldo, tp, stream);
     if (ew != cudaErrorNotSupported) return ew;
     int* err = device_status_word();

@@ -1,5 +1,5 @@
 // gemv_i8.cuh -- decode GEMV compute on the integer tensor-core MMA for Q4_K and
-// Q6_K at one or two activation rows.
+// Q6_K at one or two activation rows, and at up to four pairs of rows.
 //
 // Codes become unsigned bytes with one AND per four weights (Q4_K high nibbles
 // stay in place as 16 q; Q6_K adds a shift and an OR for its high bits) -- no
@@ -158,51 +158,70 @@ __device__ __forceinline__ void stage_block_i8(const float (&v)[8], unsigned cha
 
 // AFTER_LOADS() runs once, after the first loads are issued and before any
 // block is converted (a caller's hook to issue more copies behind them).
-// XFORM(u, col, v) may rewrite a lane's eight loaded activations of row U,
-// columns COL.. (a fused prologue), before they are converted.
+// XFORM may rewrite a lane's eight loaded activations of row U, columns COL..
+// (a fused prologue) before they are converted: XFORM.load(u, col, aux) runs
+// beside the activation loads (its own loads then share their round trip)
+// and XFORM.apply(u, col, v, aux) after them; Xform::kBatch blocks are loaded
+// per round trip.
 struct NoHook {
     __device__ void operator()() const {}
 };
 struct NoXform {
-    __device__ void operator()(int, int64_t, float (&)[8]) const {}
+    static constexpr int kBatch = 4;
+    struct Aux {};
+    __device__ void load(int, int64_t, Aux&) const {}
+    __device__ void apply(int, int64_t, float (&)[8], const Aux&) const {}
 };
-template <int D, typename XT, int WARPS, typename Hook = NoHook, typename Xform = NoXform>
-__device__ void stage_x_i8(const void* xv, int64_t k, int x_aligned, int64_t c0, int pc, int ntok,
-                           unsigned char* stage, Hook after_loads = Hook(), Xform xform = Xform()) {
+template <int D, typename XT, int WARPS, typename Hook, typename Xform>
+__device__ __forceinline__ void stage_x_i8_with(const void* xv, int64_t k, int x_aligned, int64_t c0, int pc,
+                                                int ntok, unsigned char* stage, Hook after_loads, Xform& xform) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const XT* x = reinterpret_cast<const XT*>(xv);
     constexpr int TB = I8Block<D>::bytes;
+    constexpr int B = Xform::kBatch;
     // warp w stages chunks w, w + WARPS, ... (all tokens of each), loading up to
-    // four (chunk, token) blocks before converting any: one memory round trip
-    // per four blocks
+    // B (chunk, token) blocks before converting any: one memory round trip per
+    // B blocks
     const int per = warp < pc ? ((pc - warp + WARPS - 1) / WARPS) * ntok : 0;
-    for (int b0 = 0; b0 < per; b0 += 4) {
-        float vb[4][8];
+    for (int b0 = 0; b0 < per; b0 += B) {
+        float vb[B][8];
+        typename Xform::Aux aux[B];
 #pragma unroll
-        for (int b = 0; b < 4; b++) {
+        for (int b = 0; b < B; b++) {
             const int i = b0 + b, cc = warp + (i / ntok) * WARPS, u = i - (i / ntok) * ntok;
-            const XT* src = x + (int64_t)u * k + (c0 + cc) * 256 + 8 * lane;
+            const int64_t col = (c0 + cc) * 256 + 8 * lane;
+            const XT* src = x + (int64_t)u * k + col;
             if (i >= per) {
 #pragma unroll
                 for (int e = 0; e < 8; e++) vb[b][e] = 0.f;
-            } else if (x_aligned) {
-                xload8(src, vb[b]);
             } else {
+                if (x_aligned) {
+                    xload8(src, vb[b]);
+                } else {
 #pragma unroll
-                for (int e = 0; e < 8; e++) vb[b][e] = xload(src + e);
+                    for (int e = 0; e < 8; e++) vb[b][e] = xload(src + e);
+                }
+                xform.load(u, col, aux[b]);
             }
         }
         if (b0 == 0) after_loads();
 #pragma unroll
-        for (int b = 0; b < 4; b++) {
+        for (int b = 0; b < B; b++) {
             const int i = b0 + b, cc = warp + (i / ntok) * WARPS, u = i - (i / ntok) * ntok;
             if (i < per) {
-                xform(u, (c0 + cc) * 256 + 8 * lane, vb[b]);
+                xform.apply(u, (c0 + cc) * 256 + 8 * lane, vb[b], aux[b]);
                 stage_block_i8<D>(vb[b], stage + (size_t)(cc * ntok + u) * TB);
             }
         }
     }
     if (per == 0) after_loads();
+}
+
+template <int D, typename XT, int WARPS, typename Hook = NoHook>
+__device__ __forceinline__ void stage_x_i8(const void* xv, int64_t k, int x_aligned, int64_t c0, int pc, int ntok,
+                                           unsigned char* stage, Hook after_loads = Hook()) {
+    NoXform none;
+    stage_x_i8_with<D, XT, WARPS>(xv, k, x_aligned, c0, pc, ntok, stage, after_loads, none);
 }
 
 // Per-lane constants of the i8 product.  Lane (g, t) reads B column g = token
@@ -371,6 +390,205 @@ __device__ __forceinline__ float i8_finish(const I8Lane& L, float accm, float ac
     const float m = accm + __shfl_xor_sync(0xffffffffu, accm, 1);
     const int lane = threadIdx.x & 31;
     const float n = __shfl_sync(0xffffffffu, accn, (lane & ~3) | (L.t >> 1));
+    return m - n;
+}
+
+
+// ---- several pairs of activation rows --------------------------------------
+// The same product for NP pairs of activation rows (up to eight rows): the
+// weight fragments of a unit are unpacked once and meet each pair's digit
+// columns in its own MMA; the correction MMAs take four rows each.  Pair p's
+// rows are 2p and 2p + 1 (lane (g, t): B column row 2p + g / 4; accumulator
+// row 2p + t / 2), correction group q's rows 4q .. 4q + 3 (B column row
+// 4q + g / 2, accumulator row 4q + t).  Rows past the staged ones read the
+// last staged row, and their results are dropped.  At NP = 1 this is the
+// single-pair product above.
+template <int D, int NP>
+struct I8LaneN {
+    static constexpr int NQ = (NP + 1) / 2;
+    int t, g;
+    float wa, wb;
+    uint32_t m_sel, s_sel;
+    int xb[NP], ua[NP];  // B column block and unscale of pair p
+    int xm[NQ], um[NQ];  // correction column block and unscale of group q
+};
+
+template <int D, int NP>
+__device__ __forceinline__ I8LaneN<D, NP> i8_lane_n(int ntok) {
+    I8LaneN<D, NP> L;
+    const int lane = threadIdx.x & 31;
+    constexpr int TB = I8Block<D>::bytes;
+    L.t = lane & 3;
+    L.g = lane >> 2;
+    L.wa = (L.t & 1) ? 256.f : 16777216.f;
+    L.wb = (L.t & 1) ? 1.f : 65536.f;
+    L.m_sel = (uint32_t)(2 * L.t) | ((uint32_t)(2 * L.t + 1) << 4);
+    const uint32_t b0 = (uint32_t)(L.t >> 1), b1 = b0 + 2;
+    L.s_sel = b0 | (4u << 4) | (b1 << 8) | (4u << 12);
+    const int dgt = L.g & 3, part = L.g & 1;
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+        L.xb[p] = min(2 * p + (L.g >> 2), ntok - 1) * TB + (dgt * 4 + L.t) * 16;
+        L.ua[p] = min(2 * p + (L.t >> 1), ntok - 1) * TB + 1024 + I8Block<D>::sf;
+    }
+#pragma unroll
+    for (int q = 0; q < I8LaneN<D, NP>::NQ; q++) {
+        const int tm = min(4 * q + (L.g >> 1), ntok - 1);
+        L.xm[q] = tm * TB + 1024 + (L.t * 2 + part) * (D == kQ4_K ? 4 : 8);
+        L.um[q] = min(4 * q + L.t, ntok - 1) * TB + 1024 + I8Block<D>::sf;
+    }
+    return L;
+}
+
+// Q4_K over NP pairs.  The low-nibble MMA's sums enter the accumulator times
+// 16 (the sub-block scale is shifted instead), the high-nibble MMA's as they
+// are: the accumulator is 16 al + ah of the single-pair form, |.| < 2^30 at
+// the end (partial sums wrap harmlessly in two's complement).
+template <int NP>
+__device__ __forceinline__ void q4k_i8_chunk_n(const I8LaneN<kQ4_K, NP>& L, const uint32_t (&HD)[2][4],
+                                               const uint2 (&CW)[2][4], const unsigned char* xs,
+                                               float (&accm)[NP][2], float (&accn)[(NP + 1) / 2][2]) {
+    constexpr int NQ = (NP + 1) / 2;
+    uint32_t scw[2][2], m03[2], m47[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        scw[h][0] = HD[h][1] & 0x3F3F3F3Fu;
+        scw[h][1] = (HD[h][3] & 0x0F0F0F0Fu) | ((HD[h][1] >> 2) & 0x30303030u);
+        m03[h] = HD[h][2] & 0x3F3F3F3Fu;
+        m47[h] = ((HD[h][3] >> 4) & 0x0F0F0F0Fu) | ((HD[h][2] >> 2) & 0x30303030u);
+    }
+    int acc[NP][4];
+#pragma unroll
+    for (int p = 0; p < NP; p++) acc[p][0] = acc[p][1] = acc[p][2] = acc[p][3] = 0;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint32_t w0 = scw[0][j >> 1], w1 = scw[1][j >> 1];
+        const int l0 = ubyte(w0, 2 * (j & 1)) << 4, l1 = ubyte(w1, 2 * (j & 1)) << 4;
+        const int h0 = ubyte(w0, 2 * (j & 1) + 1), h1 = ubyte(w1, 2 * (j & 1) + 1);
+        const uint32_t lo0 = CW[0][j].x & 0x0F0F0F0Fu, lo1 = CW[1][j].x & 0x0F0F0F0Fu;
+        const uint32_t lo2 = CW[0][j].y & 0x0F0F0F0Fu, lo3 = CW[1][j].y & 0x0F0F0F0Fu;
+        const uint32_t hi0 = CW[0][j].x & 0xF0F0F0F0u, hi1 = CW[1][j].x & 0xF0F0F0F0u;
+        const uint32_t hi2 = CW[0][j].y & 0xF0F0F0F0u, hi3 = CW[1][j].y & 0xF0F0F0F0u;
+#pragma unroll
+        for (int p = 0; p < NP; p++) {
+            const uint4 b = reinterpret_cast<const uint4*>(xs + L.xb[p])[16 * j];
+            int c[4];
+            imma_k32(c, lo0, lo1, lo2, lo3, b.x, b.y);
+            acc[p][0] += l0 * c[0];
+            acc[p][1] += l0 * c[1];
+            acc[p][2] += l1 * c[2];
+            acc[p][3] += l1 * c[3];
+            imma_k32(c, hi0, hi1, hi2, hi3, b.z, b.w);
+            acc[p][0] += h0 * c[0];
+            acc[p][1] += h0 * c[1];
+            acc[p][2] += h1 * c[2];
+            acc[p][3] += h1 * c[3];
+        }
+    }
+    uint32_t am[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) am[h] = hsub2(prmt(prmt(m03[h], m47[h], L.m_sel), kMagic, kSelLo), kH1024);
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+        const float ut = *reinterpret_cast<const float*>(xs + L.ua[p]) * 0.0625f;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const float d = lo_half(HD[h][0]);
+            const float f = fmaf((float)acc[p][2 * h], L.wa, (float)acc[p][2 * h + 1] * L.wb);
+            accm[p][h] = fmaf(d * ut, f, accm[p][h]);
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < NQ; q++) {
+        float cm[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(cm, am[0], am[1], 0u, 0u, *reinterpret_cast<const uint32_t*>(xs + L.xm[q]), 0u);
+        const float umin = *reinterpret_cast<const float*>(xs + L.um[q]) * 2097152.f;
+#pragma unroll
+        for (int h = 0; h < 2; h++) accn[q][h] = fmaf(hi_half(HD[h][0]) * umin, cm[2 * h] + cm[2 * h + 1], accn[q][h]);
+    }
+}
+
+// Q6_K over NP pairs.
+template <int NP>
+__device__ __forceinline__ void q6k_i8_chunk_n(const I8LaneN<kQ6_K, NP>& L, const uint32_t (&QW)[2][12],
+                                               const uint4 (&SW)[2], const uint32_t (&DB)[2],
+                                               const unsigned char* xs, float (&accm)[NP][2],
+                                               float (&accn)[(NP + 1) / 2][2]) {
+    constexpr int NQ = (NP + 1) / 2;
+    const uint32_t sw[2][4] = {{SW[0].x, SW[0].y, SW[0].z, SW[0].w}, {SW[1].x, SW[1].y, SW[1].z, SW[1].w}};
+    int acc[NP][4];
+#pragma unroll
+    for (int p = 0; p < NP; p++) acc[p][0] = acc[p][1] = acc[p][2] = acc[p][3] = 0;
+#pragma unroll
+    for (int hh = 0; hh < 4; hh++) {
+        const int h6 = hh >> 1, half = hh & 1;
+        uint32_t q[2][4];
+#pragma unroll
+        for (int r = 0; r < 2; r++) {
+            const uint32_t W0 = QW[r][3 * hh], W1 = QW[r][3 * hh + 1], QH = QW[r][3 * hh + 2];
+            q[r][0] = (W0 & 0x0F0F0F0Fu) | ((QH << 4) & 0x30303030u);
+            q[r][1] = (W1 & 0x0F0F0F0Fu) | ((QH << 2) & 0x30303030u);
+            q[r][2] = ((W0 >> 4) & 0x0F0F0F0Fu) | (QH & 0x30303030u);
+            q[r][3] = ((W1 >> 4) & 0x0F0F0F0Fu) | ((QH >> 2) & 0x30303030u);
+        }
+        uint32_t bw[NP][4];
+#pragma unroll
+        for (int p = 0; p < NP; p++) {
+            const uint4 bq = reinterpret_cast<const uint4*>(xs + L.xb[p])[16 * hh];
+            bw[p][0] = bq.x; bw[p][1] = bq.y; bw[p][2] = bq.z; bw[p][3] = bq.w;
+        }
+#pragma unroll
+        for (int grp = 0; grp < 4; grp++) {
+            const int idx = 8 * h6 + 2 * grp + half;
+            const int s0 = sbyte(sw[0][idx >> 2], idx & 3), s1 = sbyte(sw[1][idx >> 2], idx & 3);
+#pragma unroll
+            for (int p = 0; p < NP; p++) {
+                int c[4];
+                imma_k16(c, q[0][grp], q[1][grp], bw[p][grp]);
+                acc[p][0] += s0 * c[0];
+                acc[p][1] += s0 * c[1];
+                acc[p][2] += s1 * c[2];
+                acc[p][3] += s1 * c[3];
+            }
+        }
+    }
+    uint32_t a[2][2];
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        const bool odd = (L.t & 1) != 0;
+        a[r][0] = hsub2(prmt((odd ? sw[r][1] : sw[r][0]) ^ 0x80808080u, kMagic, L.s_sel), kH1152);
+        a[r][1] = hsub2(prmt((odd ? sw[r][3] : sw[r][2]) ^ 0x80808080u, kMagic, L.s_sel), kH1152);
+    }
+    float d[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) d[h] = __half2float(__ushort_as_half((unsigned short)DB[h]));
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+        const float ut = *reinterpret_cast<const float*>(xs + L.ua[p]);
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            const float f = fmaf((float)acc[p][2 * h], L.wa, (float)acc[p][2 * h + 1] * L.wb);
+            accm[p][h] = fmaf(d[h] * ut, f, accm[p][h]);
+        }
+    }
+#pragma unroll
+    for (int q = 0; q < NQ; q++) {
+        const uint2 bs = *reinterpret_cast<const uint2*>(xs + L.xm[q]);
+        float co[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(co, a[0][0], a[1][0], a[0][1], a[1][1], bs.x, bs.y);
+        const float uo = *reinterpret_cast<const float*>(xs + L.um[q]) * 67108864.f;
+#pragma unroll
+        for (int h = 0; h < 2; h++) accn[q][h] = fmaf(d[h] * uo, co[2 * h] + co[2 * h + 1], accn[q][h]);
+    }
+}
+
+// End of a tile for pair P: ACCM = accm[P][h], ACCN = accn[P / 2][h].  Lanes
+// with even t return row g + 8h of activation row 2P + t / 2.
+template <int D, int NP>
+__device__ __forceinline__ float i8_finish_n(const I8LaneN<D, NP>& L, int p, float accm, float accn) {
+    const float m = accm + __shfl_xor_sync(0xffffffffu, accm, 1);
+    const int lane = threadIdx.x & 31;
+    const float n = __shfl_sync(0xffffffffu, accn, (lane & ~3) | (2 * (p & 1) + (L.t >> 1)));
     return m - n;
 }
 

@@ -1,4 +1,4 @@
-// gemv_warp.cu -- decode GEMV (one or two activation rows) for Q4_K and Q6_K
+// gemv_warp.cu -- decode GEMV (one to eight activation rows) for Q4_K and Q6_K
 // with an independent weight stream per warp.
 //
 // One persistent CTA of 16 warps per SM owns a contiguous range of 16-row
@@ -13,12 +13,22 @@
 // of gemv_i8.cuh.  No warp waits for another except once, after the
 // activations are staged, so a slow warp never stalls the others' streams.
 //
-// A tile's K range can be split between consecutive warps.  Each warp leaves
-// one partial sum per tile it touches (a "piece") in shared memory and counts
-// it on the tile's counter; the warp that completes the count adds the tile's
-// pieces in warp order -- a fixed order, so results do not depend on timing --
-// and writes the outputs or, under tensor parallelism, sends them to every
-// rank.
+// A tile's K range can be split between consecutive warps.  A tile inside one
+// warp's run is finished by that warp from its registers.  For a tile shared
+// by several warps, each leaves its partial sum (a "piece") in shared memory
+// -- one slot per warp for the first tile of its run, one for the last -- and
+// counts it on the tile's counter; the warp that completes the count adds the
+// tile's pieces in warp order -- a fixed order, so results do not depend on
+// timing.  Finished tiles are written out or, under tensor parallelism, sent
+// to every rank.
+//
+// A CTA stages the activations of every chunk it reads (4 bytes per element
+// and row).  When those of all of K do not fit beside the rings -- several
+// activation rows, or long rows -- K is split between the KS CTAs of a tile
+// group: each stages and reads only its split, leaves its tile sums in a
+// global scratch and counts them on the tile's counter, and the split that
+// completes the count adds the KS partials in split order (again a fixed
+// order) and writes the outputs.
 //
 // The copies do not depend on the previous kernel (the weights are constant):
 // under programmatic dependent launch each warp starts its ring before
@@ -30,6 +40,7 @@
 #include <cstdlib>
 #include <mutex>
 #include <unordered_map>
+#include <vector>
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -51,9 +62,9 @@ using namespace pipe;
 constexpr int kWW = 16;  // warps per CTA
 constexpr int kWThreads = kWW * 32;
 constexpr int kWMaxDepth = 4;
-// header: slot barriers, this call's epoch, the fused RMSNorm's per-row scales
-// and its reduction partials
-constexpr int kWEpochOff = kWW * kWMaxDepth * 8, kWNormOff = kWEpochOff + 16, kWRedOff = kWNormOff + 16;
+// header: slot barriers, this call's epoch, the fused RMSNorm's row scales
+// and per-warp sums of squares
+constexpr int kWEpochOff = kWW * kWMaxDepth * 8, kWNormOff = kWEpochOff + 16, kWRedOff = kWEpochOff + 32;
 constexpr int kWHeader = kWRedOff + kWW * 2 * 4;
 constexpr int kWMaxDevices = 64;
 constexpr size_t kWSmemLimit = 227 * 1024;
@@ -74,12 +85,13 @@ struct WarpParams {
     int nmem;
     int tiles;
     int nchunks;  // K / 256
-    int m;        // 1 or 2
+    int m;        // activation rows, 1 .. 8
+    int ksplit;   // K splits: CTAs per tile group, one cluster (1: each CTA takes all of K)
     int64_t k;
     const void* x;
     int x_aligned;
     int depth;    // ring slots per warp
-    uint32_t cnt_off, x_off, piece_off, ring_off;
+    uint32_t cnt_off, x_off, piece_off, tsum_off, ring_off;
     int* err;
     int tp_on;
     TpLink tp;
@@ -92,6 +104,22 @@ struct WarpParams {
     int64_t ldr;
 };
 
+// Every thread of the cluster's CTAs arrives (its earlier shared-memory
+// stores released) and waits for all of them.
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// The float at LOCAL's offset in the shared memory of the cluster's CTA RANK.
+__device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t rank) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(local);
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    float v;
+    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(r) : "memory");
+    return v;
+}
+
 // The warp whose run holds unit u: runs are [w U / W, (w+1) U / W) for the
 // W = min(16, U) warps in use, all non-empty.
 __device__ __forceinline__ int warp_of(int u, int U, int W) { return (W * (u + 1) + U - 1) / U - 1; }
@@ -100,7 +128,59 @@ __device__ __forceinline__ int warp_of(int u, int U, int W) { return (W * (u + 1
 // gate, else x.
 __device__ __forceinline__ float swiglu_in(float x, float g) { return g / (1.f + expf(-g)) * x; }
 
-template <int D, typename XT, bool FUSE>
+// The fused prologue as a staging transform: the gate and norm-weight words
+// are loaded beside the activations (one round trip for all three), then
+// h = silu(gate) * x (when gated) is staged as h * norm_w, its squares summed
+// per row for the RMSNorm scale the finisher applies.
+template <typename XT>
+struct FusedInput {
+    static constexpr int kBatch = 2;
+    struct Aux {
+        float g[8], w[8];
+    };
+    const XT* gate = nullptr;
+    const float* norm_w = nullptr;
+    int64_t k = 0;
+    int gate_aligned = 0, norm_aligned = 0;
+    float ss0 = 0.f, ss1 = 0.f;
+    __device__ __forceinline__ void load(int u, int64_t col, Aux& a) const {
+        if (gate) {
+            const XT* gp = gate + (int64_t)u * k + col;
+            if (gate_aligned) {
+                xload8(gp, a.g);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) a.g[i] = xload(gp + i);
+            }
+        }
+        if (norm_w) {
+            if (norm_aligned) {
+                xload8(norm_w + col, a.w);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; i++) a.w[i] = norm_w[col + i];
+            }
+        }
+    }
+    __device__ __forceinline__ void apply(int u, int64_t, float (&v)[8], const Aux& a) {
+        if (gate) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = swiglu_in(v[i], a.g[i]);
+        }
+        if (norm_w) {
+            float sq = 0.f;
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                sq = fmaf(v[i], v[i], sq);
+                v[i] *= a.w[i];
+            }
+            if (u == 0) ss0 += sq;
+            else ss1 += sq;
+        }
+    }
+};
+
+template <int D, typename XT, bool FUSE, int NP, bool SPLIT>
 __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_constant__ WarpParams P) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr int Q = WGeo<D>::q;
@@ -110,13 +190,18 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
     uint32_t* ep_sh = reinterpret_cast<uint32_t*>(smem + kWEpochOff);
     int* cnt = reinterpret_cast<int*>(smem + P.cnt_off);
     unsigned char* xstage = smem + P.x_off;
-    float* piece = reinterpret_cast<float*>(smem + P.piece_off);
+    float* piece = reinterpret_cast<float*>(smem + P.piece_off);  // [2 per warp][m][16]
+    float* tsum = reinterpret_cast<float*>(smem + P.tsum_off);    // K split: [tiles][m][16]
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t = lane & 3;
-    const int nch = P.nchunks, ntok = P.m, depth = P.depth;
-    const int t_begin = (int)((int64_t)blockIdx.x * P.tiles / gridDim.x);
-    const int t_end = (int)(((int64_t)blockIdx.x + 1) * P.tiles / gridDim.x);
+    // CTA b takes K split b % KS of tile group b / KS (KS = 1: all of K)
+    const int KS = SPLIT ? P.ksplit : 1, groups = (int)gridDim.x / KS;
+    const int grp = (int)blockIdx.x / KS, ks = (int)blockIdx.x - grp * KS;
+    const int kc0 = (int)((int64_t)ks * P.nchunks / KS);
+    const int nch = (int)((int64_t)(ks + 1) * P.nchunks / KS) - kc0, ntok = P.m, depth = P.depth;
+    const int t_begin = (int)((int64_t)grp * P.tiles / groups);
+    const int t_end = (int)(((int64_t)grp + 1) * P.tiles / groups);
     const int U = (t_end - t_begin) * nch;
     const int W = U < kWW ? U : kWW;
     const int u0 = warp < W ? warp * U / W : 0, u1 = warp < W ? (warp + 1) * U / W : 0;
@@ -138,7 +223,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
         if (lane == 0) {
             const int mi = member_of(P, (int64_t)itile);
             mbar_arrive_tx(&bar[islot], kSlot);
-            tensor_copy_2d_hint(ring + islot * kSlot, &P.maps[mi], ic * Q,
+            tensor_copy_2d_hint(ring + islot * kSlot, &P.maps[mi], (kc0 + ic) * Q,
                                 (itile - (int)P.mem[mi].tile_begin) * 16, &bar[islot], policy);
         }
         ++issued;
@@ -157,67 +242,56 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
     auto top_up = [&]() {
         while (issued < u1 && issued < u0 + depth) issue();
     };
+    float* red = reinterpret_cast<float*>(smem + kWRedOff);
     if constexpr (FUSE) {
-        // RMSNorm: 1 / sqrt(mean(h^2) + eps) per activation row, from every
-        // thread's strided share of the row (fixed order: deterministic)
-        float* rn = reinterpret_cast<float*>(smem + kWNormOff);
-        float* red = reinterpret_cast<float*>(smem + kWRedOff);
-        const XT* xg = reinterpret_cast<const XT*>(P.x);
-        const XT* gg = reinterpret_cast<const XT*>(P.gate);
+        // h = silu(gate) * x (when gated), staged as h * norm_w; the RMSNorm
+        // scale 1 / sqrt(mean(h^2) + eps) is a per-row factor of the product,
+        // applied by the tile finisher.  Its sum of squares comes from the
+        // staging pass itself (every CTA stages the whole row, in the same
+        // partition: the same fixed order in every CTA, no second read of x)
+        FusedInput<XT> fi;
+        fi.gate = reinterpret_cast<const XT*>(P.gate);
+        fi.norm_w = P.norm_w;
+        fi.k = P.k;
+        fi.gate_aligned = P.gate_aligned;
+        fi.norm_aligned = P.norm_aligned;
+        stage_x_i8_with<D, XT, kWW>(P.x, P.k, P.x_aligned, kc0, nch, ntok, xstage, top_up, fi);
         if (P.norm_w) {
-            for (int u = 0; u < ntok; u++) {
-                float ss = 0.f;
-                for (int64_t e = threadIdx.x; e < P.k; e += kWThreads) {
-                    float h = xload(xg + (int64_t)u * P.k + e);
-                    if (gg) h = swiglu_in(h, xload(gg + (int64_t)u * P.k + e));
-                    ss = fmaf(h, h, ss);
-                }
+            float ss0 = fi.ss0, ss1 = fi.ss1;
 #pragma unroll
-                for (int off = 16; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-                if (lane == 0) red[warp * 2 + u] = ss;
+            for (int off = 16; off > 0; off >>= 1) {
+                ss0 += __shfl_xor_sync(0xffffffffu, ss0, off);
+                ss1 += __shfl_xor_sync(0xffffffffu, ss1, off);
             }
-            __syncthreads();
-            if (threadIdx.x < ntok) {
+            if (lane == 0) {
+                red[warp * 2] = ss0;
+                red[warp * 2 + 1] = ss1;
+            }
+        }
+    } else {
+        stage_x_i8<D, XT, kWW>(P.x, P.k, P.x_aligned, kc0, nch, ntok, xstage, top_up);
+    }
+    __syncthreads();
+    float* rn = reinterpret_cast<float*>(smem + kWNormOff);  // the fused RMSNorm's scale of rows 0 and 1
+    if constexpr (FUSE) {
+        if (P.norm_w) {
+            if (threadIdx.x < 2) {
                 float tot = 0.f;
+#pragma unroll
                 for (int w = 0; w < kWW; w++) tot += red[w * 2 + threadIdx.x];
                 rn[threadIdx.x] = 1.f / sqrtf(tot / (float)P.k + P.norm_eps);
             }
             __syncthreads();
         }
-        auto xform = [&](int u, int64_t col, float (&v)[8]) {
-            if (gg) {
-                float gv[8];
-                const XT* gp = gg + (int64_t)u * P.k + col;
-                if (P.gate_aligned) {
-                    xload8(gp, gv);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 8; i++) gv[i] = xload(gp + i);
-                }
-#pragma unroll
-                for (int i = 0; i < 8; i++) v[i] = swiglu_in(v[i], gv[i]);
-            }
-            if (P.norm_w) {
-                const float r = rn[u];
-                float wv[8];
-                if (P.norm_aligned) {
-                    xload8(P.norm_w + col, wv);
-                } else {
-#pragma unroll
-                    for (int i = 0; i < 8; i++) wv[i] = P.norm_w[col + i];
-                }
-#pragma unroll
-                for (int i = 0; i < 8; i++) v[i] = v[i] * r * wv[i];
-            }
-        };
-        stage_x_i8<D, XT, kWW>(P.x, P.k, P.x_aligned, 0, nch, ntok, xstage, top_up, xform);
-    } else {
-        stage_x_i8<D, XT, kWW>(P.x, P.k, P.x_aligned, 0, nch, ntok, xstage, top_up);
     }
-    __syncthreads();
 
-    const I8Lane L8 = i8_lane<D>(ntok);
-    float accm[2] = {0.f, 0.f}, accn[2] = {0.f, 0.f};
+    constexpr int NQ = (NP + 1) / 2;
+    const I8LaneN<D, NP> L8 = i8_lane_n<D, NP>(ntok);
+    float accm[NP][2], accn[NQ][2];
+#pragma unroll
+    for (int p = 0; p < NP; p++) accm[p][0] = accm[p][1] = 0.f;
+#pragma unroll
+    for (int q = 0; q < NQ; q++) accn[q][0] = accn[q][1] = 0.f;
     bool ok = true;
     int done = u0;
 
@@ -229,13 +303,15 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
         int64_t r0 = (int64_t)(tile - (int)M.tile_begin) * 16 + g, r1 = r0 + 8;
         if (r0 >= M.rows) r0 = M.rows - 1;
         if (r1 >= M.rows) r1 = M.rows - 1;
-        s_nxt[0] = __ldg(reinterpret_cast<const uint4*>(M.p.s + (r0 * nch + c) * 16));
-        s_nxt[1] = __ldg(reinterpret_cast<const uint4*>(M.p.s + (r1 * nch + c) * 16));
-        d_nxt[0] = __ldg(reinterpret_cast<const unsigned short*>(M.p.d + (r0 * nch + c) * 2));
-        d_nxt[1] = __ldg(reinterpret_cast<const unsigned short*>(M.p.d + (r1 * nch + c) * 2));
+        const int64_t cg = kc0 + c, nc = P.nchunks;
+        s_nxt[0] = __ldg(reinterpret_cast<const uint4*>(M.p.s + (r0 * nc + cg) * 16));
+        s_nxt[1] = __ldg(reinterpret_cast<const uint4*>(M.p.s + (r1 * nc + cg) * 16));
+        d_nxt[0] = __ldg(reinterpret_cast<const unsigned short*>(M.p.d + (r0 * nc + cg) * 2));
+        d_nxt[1] = __ldg(reinterpret_cast<const unsigned short*>(M.p.d + (r1 * nc + cg) * 2));
     };
 
     int tl = u0 / (nch > 0 ? nch : 1), c = u0 - tl * nch, slot = 0;
+    const int tl_first = tl;  // the first tile of this warp's run
     uint32_t phase = 0;
     if constexpr (D == kQ6_K) {
         if (u0 < u1) side(t_begin + tl, c);
@@ -271,7 +347,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
             }
             __syncwarp();
             if (issued < u1) issue();  // the slot's words are in registers: refill it
-            q4k_i8_chunk(L8, HD, CW, xs, accm, accn);
+            q4k_i8_chunk_n<NP>(L8, HD, CW, xs, accm, accn);
         } else {
             uint32_t QW[2][12];
 #pragma unroll
@@ -285,7 +361,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
             }
             __syncwarp();
             if (issued < u1) issue();
-            q6k_i8_chunk(L8, QW, s_cur, d_cur, xs, accm, accn);
+            q6k_i8_chunk_n<NP>(L8, QW, s_cur, d_cur, xs, accm, accn);
         }
         done = u + 1;
         if (++slot == depth) {
@@ -294,17 +370,28 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
         }
         const bool tile_end = ++c == nch;
         if (tile_end || u + 1 == u1) {
-            // ---- this warp's piece of tile tl: to shared memory, then count it ----
-            float v[2];
+            const int wf = warp_of(tl * nch, U, W), wl = warp_of(tl * nch + nch - 1, U, W);
+            // this warp's piece of the tile goes to its slot for the run's
+            // first tile or the one for any later tile (a later tile not
+            // shared with other warps is finished by this warp at once)
+            const int slot = 2 * warp + (tl == tl_first ? 0 : 1);
 #pragma unroll
-            for (int h = 0; h < 2; h++) v[h] = i8_finish(L8, accm[h], accn[h]);
-            const int tok = t >> 1;
-            if ((t & 1) == 0 && tok < ntok) {
+            for (int p = 0; p < NP; p++) {
+                float v[2];
 #pragma unroll
-                for (int h = 0; h < 2; h++)
-                    piece[((warp + tl) * ntok + tok) * 16 + (D == kQ4_K ? 2 * g + h : g + 8 * h)] = v[h];
+                for (int h = 0; h < 2; h++) v[h] = i8_finish_n(L8, p, accm[p][h], accn[p >> 1][h]);
+                const int tok = 2 * p + (t >> 1);
+                if ((t & 1) == 0 && tok < ntok) {
+#pragma unroll
+                    for (int h = 0; h < 2; h++) {
+                        piece[(slot * ntok + tok) * 16 + (D == kQ4_K ? 2 * g + h : g + 8 * h)] = v[h];
+                    }
+                }
             }
-            accm[0] = accm[1] = accn[0] = accn[1] = 0.f;
+#pragma unroll
+            for (int p = 0; p < NP; p++) accm[p][0] = accm[p][1] = 0.f;
+#pragma unroll
+            for (int q = 0; q < NQ; q++) accn[q][0] = accn[q][1] = 0.f;
             __syncwarp();
             int old = 0;
             if (lane == 0) {
@@ -312,25 +399,38 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
                 old = atomicAdd(&cnt[tl], 1);
             }
             old = __shfl_sync(0xffffffffu, old, 0);
-            const int wf = warp_of(tl * nch, U, W), wl = warp_of(tl * nch + nch - 1, U, W);
             if (old == wl - wf) {  // the tile's last piece: add them in warp order
                 __threadfence_block();
                 const int tile = t_begin + tl;
                 const Member& M = P.mem[member_of(P, (int64_t)tile)];
-                for (int idx = lane; idx < ntok * 16; idx += 32) {
-                    float sum = 0.f;
-                    for (int w = wf; w <= wl; w++) sum += piece[((w + tl) * ntok) * 16 + idx];
+                // one output of the tile: into the cluster's sums (K split), to
+                // every rank (tensor parallel) or, after the fused epilogue, out
+                auto emit = [&](int idx, float sum) {
+                    if constexpr (SPLIT) {
+                        tsum[tl * ntok * 16 + idx] = sum;
+                        return;
+                    }
                     const int64_t row = (int64_t)(tile - (int)M.tile_begin) * 16 + (idx & 15);
-                    if (row >= M.rows) continue;
+                    if (row >= M.rows) return;
                     if (P.tp_on) {
                         tp_put(P.tp, ep_sh[0], (int)blockIdx.x, tl, ntok, idx, sum);
-                    } else {
-                        float o = sum;
-                        if constexpr (FUSE) {
-                            if (P.res) o += P.res[(int64_t)(idx >> 4) * P.ldr + row];  // single weight only
-                        }
-                        M.out[(int64_t)(idx >> 4) * M.ldo + row] = o;
+                        return;
                     }
+                    float o = sum;
+                    if constexpr (FUSE) {
+                        if (P.norm_w) o *= rn[idx >> 4];
+                        if (P.res) o += P.res[(int64_t)(idx >> 4) * P.ldr + row];  // single weight only
+                    }
+                    M.out[(int64_t)(idx >> 4) * M.ldo + row] = o;
+                };
+                // the tile is the first of every later warp's run, and of
+                // warp wf's when that run starts with the tile
+                const int s_first = 2 * wf + (wf * U / W == tl * nch ? 0 : 1);
+                for (int idx = lane; idx < ntok * 16; idx += 32) {
+                    float sum = 0.f;
+                    sum += piece[s_first * ntok * 16 + idx];
+                    for (int w = wf + 1; w <= wl; w++) sum += piece[2 * w * ntok * 16 + idx];
+                    emit(idx, sum);
                 }
             }
             if (tile_end) {
@@ -346,6 +446,27 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
             const int k = v - u0;
             mbar_drain(&bar[k % depth], (uint32_t)(k / depth) & 1u);
         }
+    }
+    if constexpr (SPLIT) {
+        // the cluster's KS CTAs hold the same tiles' sums over their K
+        // splits: each adds a share of the outputs over the splits, in split
+        // order, reading the others' shared memory; the second barrier keeps
+        // every CTA's sums alive until all reads are done
+        __syncwarp();
+        cluster_barrier();
+        const float* ts = reinterpret_cast<const float*>(smem + P.tsum_off);
+        const int per_tile = ntok * 16, total = (t_end - t_begin) * per_tile;
+        const int e0 = (int)((int64_t)ks * total / KS), e1 = (int)((int64_t)(ks + 1) * total / KS);
+        for (int e = e0 + (int)threadIdx.x; e < e1; e += kWThreads) {
+            float sum = 0.f;
+            for (int k2 = 0; k2 < KS; k2++) sum += ld_cluster_f32(ts + e, (uint32_t)k2);
+            const int tile = t_begin + e / per_tile, idx = e - (e / per_tile) * per_tile;
+            const Member& M = P.mem[member_of(P, (int64_t)tile)];
+            const int64_t row = (int64_t)(tile - (int)M.tile_begin) * 16 + (idx & 15);
+            if (row < M.rows) M.out[(int64_t)(idx >> 4) * M.ldo + row] = sum;
+        }
+        __syncwarp();
+        cluster_barrier();
     }
     if (P.tp_on) {
         // every rank partitions the tiles the same way, so this CTA's
@@ -450,17 +571,20 @@ int64_t warp_grid(int64_t tiles) {
     return best;
 }
 
-// Shared memory: header, tile counters, all of K's staged activations, the
-// pieces, then 16 rings of DEPTH slots (4, else 3).  False when three slots
-// per warp do not fit.
+// Shared memory: header, tile counters, the staged activations of the CTA's
+// K split (all of K at KS = 1), the pieces, the tile sums a cluster reduces
+// (KS > 1), then 16 rings of DEPTH slots (4, else 3; 2 when K is split).
+// False when the fewest slots do not fit.
 template <int D>
-bool wplan(WarpParams& P, int64_t grid, size_t* smem) {
-    const int64_t tiles_cta = (P.tiles + grid - 1) / grid;
+bool wplan(WarpParams& P, int64_t groups, int ks, size_t* smem) {
+    const int64_t tiles_cta = (P.tiles + groups - 1) / groups;
+    const int64_t pc = (P.nchunks + ks - 1) / ks;
     P.cnt_off = kWHeader;
     P.x_off = (uint32_t)al128(P.cnt_off + (size_t)tiles_cta * 4);
-    P.piece_off = (uint32_t)al128(P.x_off + (size_t)P.nchunks * P.m * I8Block<D>::bytes);
-    P.ring_off = (uint32_t)al128(P.piece_off + (size_t)(kWW + tiles_cta) * P.m * 16 * 4);
-    for (int depth = kWMaxDepth; depth >= 3; depth--) {
+    P.piece_off = (uint32_t)al128(P.x_off + (size_t)pc * P.m * I8Block<D>::bytes);
+    P.tsum_off = (uint32_t)al128(P.piece_off + (size_t)2 * kWW * P.m * 16 * 4);
+    P.ring_off = (uint32_t)al128(P.tsum_off + (ks > 1 ? (size_t)tiles_cta * P.m * 16 * 4 : 0));
+    for (int depth = kWMaxDepth; depth >= (ks > 1 ? 2 : 3); depth--) {
         const size_t total = P.ring_off + (size_t)kWW * depth * 16 * WGeo<D>::q;
         if (total <= kWSmemLimit) {
             P.depth = depth;
@@ -471,15 +595,12 @@ bool wplan(WarpParams& P, int64_t grid, size_t* smem) {
     return false;
 }
 
-template <int D, typename XT, bool FUSE>
-cudaError_t launch_warp(WarpParams P, cudaStream_t stream) {
-    const int64_t grid = warp_grid(P.tiles);
-    if (P.tp_on && (grid > kMaxTpCtas || (P.tiles + grid - 1) / grid * 16 * P.m > P.tp.cap))
-        return cudaErrorNotSupported;
-    size_t smem = 0;
-    if (!wplan<D>(P, grid, &smem)) return cudaErrorNotSupported;
-    auto kern = gemv_warp_kernel<D, XT, FUSE>;
-    static std::atomic<int> set_for[kWMaxDevices];
+constexpr int kWMaxSplit = 8;
+
+// Raises the kernel's dynamic shared-memory limit on the current device to
+// SMEM once (per instance and device).
+template <typename Kern>
+cudaError_t ensure_smem(Kern kern, std::atomic<int> (&set_for)[kWMaxDevices], size_t smem) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= kWMaxDevices) return cudaErrorInvalidDevice;
@@ -490,24 +611,124 @@ cudaError_t launch_warp(WarpParams P, cudaStream_t stream) {
         while ((int)smem > seen && !set_for[dev].compare_exchange_weak(seen, (int)smem)) {
         }
     }
+    return cudaSuccess;
+}
+
+// Clusters of KS CTAs of SMEM bytes each that the current device holds at
+// once (a cluster's CTAs wait for one another, so the launch must be one
+// wave), cached per (device, KS, SMEM); 0 when the query fails.
+template <typename Kern>
+int64_t max_clusters(Kern kern, std::atomic<int> (&set_for)[kWMaxDevices], int ks, size_t smem) {
+    static std::mutex mu;
+    static std::unordered_map<uint64_t, int> seen;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    const uint64_t key = ((uint64_t)dev << 40) | ((uint64_t)ks << 32) | (uint64_t)smem;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        auto it = seen.find(key);
+        if (it != seen.end()) return it->second;
+    }
+    if (ensure_smem(kern, set_for, smem) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)grid);
+    cfg.gridDim = dim3((unsigned)(sm_count() / ks * ks));
+    cfg.blockDim = dim3(kWThreads);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = (unsigned)ks;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    seen[key] = n;
+    return n;
+}
+
+template <int D, typename XT, bool FUSE, int NP>
+cudaError_t launch_warp(WarpParams P, cudaStream_t stream) {
+    auto kern = gemv_warp_kernel<D, XT, FUSE, NP, false>;
+    auto kern_split = gemv_warp_kernel<D, XT, false, NP, true>;
+    static std::atomic<int> set_for[kWMaxDevices], set_for_split[kWMaxDevices];
+    int64_t groups = warp_grid(P.tiles);
+    if (P.tp_on && (groups > kMaxTpCtas || (P.tiles + groups - 1) / groups * 16 * P.m > P.tp.cap))
+        return cudaErrorNotSupported;
+    size_t smem = 0;
+    int ks = 1;
+    if (!wplan<D>(P, groups, 1, &smem)) {
+        // the activations of all of K do not fit beside the rings: split K
+        // between the CTAs of a cluster (not under tensor parallelism or a
+        // fused prologue, which need whole rows in one CTA)
+        if (P.tp_on || FUSE) return cudaErrorNotSupported;
+        ks = 0;
+        const int64_t sms = sm_count();
+        for (int k2 = 2; k2 <= kWMaxSplit && k2 <= P.nchunks; k2 *= 2) {
+            groups = sms / k2 < P.tiles ? sms / k2 : P.tiles;
+            if (!wplan<D>(P, groups, k2, &smem)) continue;
+            const int64_t clusters = max_clusters(kern_split, set_for_split, k2, smem);
+            if (clusters < 1) continue;
+            if (clusters < groups) {  // fewer clusters fit than SMs / KS: more tiles each
+                groups = clusters;
+                if (!wplan<D>(P, groups, k2, &smem)) continue;
+            }
+            ks = k2;
+            break;
+        }
+        if (!ks) return cudaErrorNotSupported;
+    }
+    P.ksplit = ks;
+    cudaError_t e = ks > 1 ? ensure_smem(kern_split, set_for_split, smem) : ensure_smem(kern, set_for, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(groups * ks));
     cfg.blockDim = dim3(kWThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (gemv_pdl_enabled()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na++].val.programmaticStreamSerializationAllowed = 1;
+    }
+    if (ks > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = (unsigned)ks;
+        attr[na].val.clusterDim.y = 1;
+        attr[na++].val.clusterDim.z = 1;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = gemv_pdl_enabled() ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, kern, P);
+    cfg.numAttrs = na;
+    return ks > 1 ? cudaLaunchKernelEx(&cfg, kern_split, P) : cudaLaunchKernelEx(&cfg, kern, P);
+}
+
+// One instance per pair count of activation rows; the fused prologue at one
+// pair only.
+template <int D, typename XT>
+cudaError_t launch_warp_rows(const WarpParams& P, bool fuse, cudaStream_t s) {
+    if (fuse) return launch_warp<D, XT, true, 1>(P, s);
+    switch ((P.m + 1) / 2) {
+    case 1: return launch_warp<D, XT, false, 1>(P, s);
+    case 2: return launch_warp<D, XT, false, 2>(P, s);
+    case 3: return launch_warp<D, XT, false, 3>(P, s);
+    case 4: return launch_warp<D, XT, false, 4>(P, s);
+    default: return cudaErrorNotSupported;
+    }
 }
 
 template <typename XT>
 cudaError_t launch_warp_dtype(const WarpParams& P, int dtype, bool fuse, cudaStream_t s) {
     switch (dtype) {
-    case kQ4_K: return fuse ? launch_warp<kQ4_K, XT, true>(P, s) : launch_warp<kQ4_K, XT, false>(P, s);
-    case kQ6_K: return fuse ? launch_warp<kQ6_K, XT, true>(P, s) : launch_warp<kQ6_K, XT, false>(P, s);
+    case kQ4_K: return launch_warp_rows<kQ4_K, XT>(P, fuse, s);
+    case kQ6_K: return launch_warp_rows<kQ6_K, XT>(P, fuse, s);
     default: return cudaErrorNotSupported;
     }
 }
@@ -517,9 +738,9 @@ cudaError_t launch_warp_dtype(const WarpParams& P, int dtype, bool fuse, cudaStr
 cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, int count, const void* x, int xtype,
                              int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
                              cudaStream_t stream, const Fusion* fuse) {
-    if (!warp_enabled() || m < 1 || m > 2 || count < 1 || count > kGroup) return cudaErrorNotSupported;
+    if (!warp_enabled() || m < 1 || m > 8 || count < 1 || count > kGroup) return cudaErrorNotSupported;
     const bool fused = fuse && fuse->any();
-    if (fused && (tp || (fuse->res && count != 1))) return cudaErrorNotSupported;
+    if (fused && (m > 2 || tp || (fuse->res && count != 1))) return cudaErrorNotSupported;
     const int dtype = w[0]->dtype;
     if ((dtype != kQ4_K && dtype != kQ6_K) || w[0]->k < 256) return cudaErrorNotSupported;
     int* err = device_status_word();

@@ -1,8 +1,12 @@
-"""Decode products of one and two activation rows on Q4_K and Q6_K (needs a B200).
+"""Decode products of one to eight activation rows on Q4_K and Q6_K (needs a B200).
 
 These shapes run the per-warp streaming GEMV: every warp copies its own
 (16-row, 256-column) units with a tensor-map box and the tile partials meet
-through a per-tile count in shared memory.  Cases cover ragged row counts
+through a per-tile count in shared memory.  Where the activations of all of K
+do not fit in a CTA's shared memory (several rows, long rows) K is split
+between CTAs whose partials meet through a global per-tile count, added in
+split order: results are still the same bits on every call, also when calls
+of other shapes run in between.  Cases cover ragged row counts
 (boxes that run past the last row read zeros), row views written into a wider
 output, K from one superblock to a 14336-wide down projection, the three
 activation types, an activation pointer off the 16-byte grid, and activations
@@ -24,7 +28,7 @@ def check(got, ref, mag):
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
-@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("m", [1, 2, 3, 5, 8])
 @pytest.mark.parametrize("n,k", [(300, 2048), (77, 14336), (4100, 256), (2000, 4096)])
 def test_decode_rows_against_oracle(cuda, clq, synth, oracle, dtype, m, n, k):
     torch = cuda
@@ -42,7 +46,7 @@ def test_decode_rows_against_oracle(cuda, clq, synth, oracle, dtype, m, n, k):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("xtype", ["float32", "bfloat16", "float16"])
-@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("m", [1, 2, 4, 7])
 def test_decode_views_types_and_unaligned_activations(cuda, clq, synth, oracle, dtype, xtype, m):
     torch = cuda
     n, k = 333, 1024
@@ -69,10 +73,10 @@ def test_decode_extreme_activation_scales(cuda, clq, synth, oracle, dtype):
     data = synth.packed_blocks(dtype, n, k, seed=9)
     rng = np.random.default_rng(3)
     store = clq.Store(dtype, n, k, data)
-    for scale_a, scale_b in ((1e-30, 1e30), (0.0, 1e4)):
-        x = rng.standard_normal((2, k)).astype(np.float32)
-        x[0] *= np.float32(scale_a)
-        x[1] *= np.float32(scale_b)
+    for scales in ((1e-30, 1e30), (0.0, 1e4), (1e4, 1e-30, 0.0, 1e30, 1.0, 1e-3)):
+        x = rng.standard_normal((len(scales), k)).astype(np.float32)
+        for i, sc in enumerate(scales):
+            x[i] *= np.float32(sc)
         x[1, ::5] = 0.0
         ref, mag = oracle.matmul_f64(dtype, x, data, n)
         got = store.linear(torch.from_numpy(x).cuda()).cpu().numpy().astype(np.float64)
@@ -89,11 +93,34 @@ def test_decode_group_of_projections(cuda, clq, synth, oracle, dtype):
     shapes = [4096, 1024, 1000]
     datas = [synth.packed_blocks(dtype, n, k, seed=90 + i) for i, n in enumerate(shapes)]
     stores = [clq.Store(dtype, n, k, d) for n, d in zip(shapes, datas)]
-    for m in (1, 2):
+    for m in (1, 2, 4, 8):
         x = synth.activations(m, k, seed=95 + m)
         outs = clq.linear_group(stores, torch.from_numpy(x).cuda())
         for o, d, n in zip(outs, datas, shapes):
             ref, mag = oracle.matmul_f64(dtype, x, d, n)
             check(o.cpu().numpy(), ref, mag)
     for s in stores:
+        s.close()
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_split_k_calls_of_other_shapes_in_between(cuda, clq, synth, oracle, dtype):
+    """K-split launches of different tile counts and split counts, in turn:
+    each tile's count must be back at zero after every call."""
+    torch = cuda
+    cases = [(2000, 4096, 8), (77, 14336, 5), (4100, 1024, 6), (515, 14336, 3)]
+    runs = []
+    for i, (n, k, m) in enumerate(cases):
+        data = synth.packed_blocks(dtype, n, k, seed=300 + i)
+        x = torch.from_numpy(synth.activations(m, k, seed=310 + i)).cuda()
+        runs.append((clq.Store(dtype, n, k, data), x, data, n))
+    first = [s.linear(x).cpu().numpy() for s, x, _, _ in runs]
+    for (s, x, data, n), got in zip(runs, first):
+        ref, mag = oracle.matmul_f64(dtype, x.cpu().numpy(), data, n)
+        check(got, ref, mag)
+    for _ in range(2):
+        for (s, x, _, _), want in zip(reversed(runs), reversed(first)):
+            again = s.linear(x).cpu().numpy()
+            assert np.array_equal(again.view(np.uint32), want.view(np.uint32))
+    for s, *_ in runs:
         s.close()
