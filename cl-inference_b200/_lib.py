@@ -18,7 +18,7 @@ STATUS_NAMES = {
     0: "CLQ_OK", 1: "CLQ_ERR_ARGUMENT", 2: "CLQ_ERR_SHAPE", 3: "CLQ_ERR_BLOCKS",
     4: "CLQ_ERR_NONFINITE_SCALE", 5: "CLQ_ERR_CUDA", 6: "CLQ_ERR_NCCL", 7: "CLQ_ERR_TIMEOUT",
     8: "CLQ_ERR_NO_DEVICE", 9: "CLQ_ERR_UNSUPPORTED", 10: "CLQ_ERR_OUT_OF_MEMORY",
-    11: "CLQ_ERR_FORMAT", 12: "CLQ_ERR_IO",
+    11: "CLQ_ERR_FORMAT", 12: "CLQ_ERR_IO", 13: "CLQ_ERR_NONFINITE_VALUE", 14: "CLQ_ERR_CONTEXT",
 }
 
 _i64 = ctypes.c_int64
@@ -79,6 +79,15 @@ SIGNATURES = {
     "clq_gather_device": (_int, [_ptr, _ptr, _i64, _ptr, _ptr]),
     "clq_dequantize": (_int, [_int, _ptr, _size, _ptr]),
     "clq_take": (_int, [_int, _ptr, _i64, _i64, _ptr, _i64, _ptr]),
+    "clq_kv_cache_create": (_int, [_i64, _int, _int, _int, _int, ctypes.POINTER(_ptr)]),
+    "clq_kv_cache_destroy": (_int, [_ptr]),
+    "clq_kv_cache_info": (_int, [_ptr, ctypes.POINTER(_i64), ctypes.POINTER(_int), ctypes.POINTER(_int),
+                                 ctypes.POINTER(_int), ctypes.POINTER(_int)]),
+    "clq_kv_cache_update": (_int, [_ptr, _int, _ptr, _ptr, _i64, _i64, _i64, _i64, _ptr]),
+    "clq_kv_cache_status": (_int, [_ptr, ctypes.POINTER(_int)]),
+    "clq_kv_cache_read": (_int, [_ptr, _int, _i64, _ptr, _ptr, _ptr]),
+    "clq_rope_device": (_int, [_ptr, _i64, _int, _int, _i64, _i64, _int, _i64, ctypes.c_double, _ptr, _int, _ptr]),
+    "clq_attend_device": (_int, [_ptr, _i64, _int, _i64, _ptr, _int, _i64, _i64, _ptr, _i64, _ptr]),
 }
 
 

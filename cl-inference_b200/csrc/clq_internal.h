@@ -23,6 +23,8 @@ bool geometry(int dtype, int* elems, int* block_bytes);
 
 // Records the formatted message as this thread's clq_last_error and returns CODE.
 int set_error(int code, const char* fmt, ...);
+// Makes the current device's stream-ordered pool keep released memory (once per device).
+cudaError_t keep_pool_memory();
 
 // Re-tile NBLOCKS native GGUF blocks (N rows of NB blocks) into the planes at
 // DST (layout.cuh); the planes' tail must be zeroed by the caller.

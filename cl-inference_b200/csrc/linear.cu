@@ -23,10 +23,13 @@ int64_t gemm_min_m() {
     return v;
 }
 
-// Scratch for one GEMM call comes from the device's stream-ordered pool: it is
-// allocated and released on the call's stream (graph memory nodes when the
-// stream is being captured), so concurrent streams never share it.  The pool
-// keeps released memory for reuse instead of returning it at each sync.
+}  // namespace
+
+// Scratch for one GEMM (or attention) call comes from the device's
+// stream-ordered pool: it is allocated and released on the call's stream
+// (graph memory nodes when the stream is being captured), so concurrent
+// streams never share it.  The pool keeps released memory for reuse instead
+// of returning it at each sync.
 cudaError_t keep_pool_memory() {
     static std::mutex mu;
     static std::map<int, bool> done;
@@ -42,8 +45,6 @@ cudaError_t keep_pool_memory() {
     done[dev] = true;
     return cudaSuccess;
 }
-
-}  // namespace
 
 bool uses_gemm_tc(const WeightView& w, int xtype, int64_t m, unsigned flags) {
     const bool sixteen_bit = xtype != CLQ_X_F32 || (flags & CLQ_MATH_FAST);

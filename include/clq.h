@@ -46,7 +46,11 @@ enum clq_status {
     CLQ_ERR_UNSUPPORTED = 9,    /* valid request this build does not implement       */
     CLQ_ERR_OUT_OF_MEMORY = 10,
     CLQ_ERR_FORMAT = 11,        /* malformed GGUF file (gguf/reader.lisp's gguf-error) */
-    CLQ_ERR_IO = 12             /* a file could not be opened or mapped              */
+    CLQ_ERR_IO = 12,            /* a file could not be opened or mapped              */
+    CLQ_ERR_NONFINITE_VALUE = 13, /* a non-finite key or value into a Q8 cache
+                                     (local/kv-cache.lisp:49, "Non-finite key or value") */
+    CLQ_ERR_CONTEXT = 14        /* positions past the cache's context
+                                   (local/kv-cache.lisp:94-96, context-overflow)      */
 };
 
 /* Store creation flags. */
@@ -283,6 +287,50 @@ int clq_gguf_metadata_value(const clq_gguf *file, const char *key, int *type, ui
  * clq_store_create does (CLQ_ERR_NONFINITE_SCALE for an fp16 scale with
  * exponent 31).  Other types: CLQ_ERR_UNSUPPORTED. */
 int clq_gguf_store(clq_gguf *file, int64_t index, clq_store **out);
+
+/* ---- KV cache, RoPE and attention around the linears --------------------
+ * The decode layer's work between the projections (local/blocks.lisp:327-353)
+ * on device memory.  A cache holds every layer's keys and values, each
+ * [n_ctx][kv_heads][head_dim]: f32, or the reference's Q8 codec -- int8
+ * codes and one f32 scale per 32-element group, scale = max(FLT_MIN, peak /
+ * 127) (1 for an all-zero group), code = clamp(round-half-even(value /
+ * scale), -127, 127) (local/kv-cache.lisp:20-78).  Rows are f32 with element
+ * stride 1 and the given position and head strides (in elements). */
+enum clq_kv_type { CLQ_KV_F32 = 0, CLQ_KV_Q8 = 1 };
+enum clq_rope_pairing { CLQ_ROPE_ADJACENT = 0, CLQ_ROPE_NEOX = 1 };
+typedef struct clq_kv_cache clq_kv_cache;
+/* make-kv-cache (local/kv-cache.lisp:17-19) for LAYERS layers on the current device. */
+int clq_kv_cache_create(int64_t n_ctx, int layers, int kv_heads, int head_dim, int cache_type, clq_kv_cache **out);
+int clq_kv_cache_destroy(clq_kv_cache *cache);
+int clq_kv_cache_info(const clq_kv_cache *cache, int64_t *n_ctx, int *layers, int *kv_heads, int *head_dim,
+                      int *cache_type);
+/* The store half of kv-cache-update (local/kv-cache.lisp:92-110): COUNT rows of
+ * K and V into LAYER at positions [START, START + COUNT); CLQ_ERR_CONTEXT past
+ * n_ctx.  Asynchronous on STREAM: a non-finite value into a Q8 cache is
+ * reported by clq_kv_cache_status (the rows are stored all the same). */
+int clq_kv_cache_update(clq_kv_cache *cache, int layer, const float *k, const float *v, int64_t count,
+                        int64_t pos_stride, int64_t head_stride, int64_t start, void *stream);
+/* No counterpart in the reference (its stores fail on the calling thread).
+ * Waits for the device and returns in *STATUS CLQ_ERR_NONFINITE_VALUE when a
+ * Q8 store met a non-finite value since the last call (else CLQ_OK), and clears it. */
+int clq_kv_cache_status(clq_kv_cache *cache, int *status);
+/* The prefix half of kv-cache-update: LAYER's first END positions decoded to f32
+ * [end][kv_heads][head_dim] (the f32 slice, or q8-prefix, local/kv-cache.lisp:62-78);
+ * either output may be null. */
+int clq_kv_cache_read(const clq_kv_cache *cache, int layer, int64_t end, float *keys, float *values, void *stream);
+/* apply-rope with rope-tables (local/blocks.lisp:172-214), in place on COUNT rows
+ * of HEADS heads at positions START..: frequency theta^(-2i/rope_dims) / factors[i]
+ * (FACTORS null: 1; the Llama-3 factors of llama3-rope-factors, :230-252, are the
+ * caller's), cos and sin in double rounded to f32; PAIRING adjacent (2i, 2i+1)
+ * or neox (i, i + rope_dims/2). */
+int clq_rope_device(float *x, int64_t count, int heads, int head_dim, int64_t pos_stride, int64_t head_stride,
+                    int rope_dims, int64_t start, double theta, const float *factors, int pairing, void *stream);
+/* attend with causal-mask (local/blocks.lisp:282-325) over LAYER's cached prefix
+ * [0, END): query row t at position QUERY_START + t sees keys at positions <= it;
+ * head h reads KV head h / (n_heads / kv_heads); scores scaled by 1/sqrt(head_dim);
+ * OUT[t][h * head_dim + d] (row stride LDO) the softmax-weighted values. */
+int clq_attend_device(const float *q, int64_t count, int n_heads, int64_t q_pos_stride, const clq_kv_cache *cache,
+                      int layer, int64_t end, int64_t query_start, float *out, int64_t ldo, void *stream);
 
 #ifdef __cplusplus
 }
