@@ -76,8 +76,13 @@ def parse():
                          "(fused) or through NCCL after it")
     ap.add_argument("--fusions", choices=["off", "fused", "unfused"], default="off",
                     help="run each layer with the reference's data flow around the linears (RMSNorm -> q/k/v, "
-                         "o + residual, RMSNorm -> gate/up, SwiGLU -> down + residual; no attention): fused into "
+                         "o + residual, RMSNorm -> gate/up, SwiGLU -> down + residual; attention with --attention): "
+                         "fused into "
                          "the GEMVs (clq_linear_fused_device), or as torch element-wise ops between plain linears")
+    ap.add_argument("--attention", choices=["off", "f32", "q8"], default="off",
+                    help="with --fusions: each layer also runs RoPE on q and k, stores k and v in a KV cache of "
+                         "that type and attends over --context cached positions (local/blocks.lisp:327-353)")
+    ap.add_argument("--context", type=int, default=1024, help="cached positions attended over (with --attention)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
@@ -296,6 +301,38 @@ def run_clq(args):
         def rms(v):
             return v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + 1e-5) * norm_w
 
+        attn = args.attention if args.attention != "off" else None
+        heads, kvh, hd = cfg["heads"], cfg["kv_heads"], cfg["head_dim"]
+        kv_dim = kvh * hd
+        if attn:
+            att = importlib.import_module("cl-inference_b200.attention")
+            ctx = args.context
+            if ctx < m:
+                raise SystemExit("--context must hold the step's rows")
+            pos0 = ctx - m  # the step's rows take the last positions; each step rewrites them
+            cache = att.KVCache(ctx, cfg["layers"], kvh, hd, attn)
+            for layer in range(cfg["layers"]):  # the prompt's keys and values, once
+                if pos0:
+                    kv = torch.randn(2, pos0, kvh, hd, device="cuda", generator=gen)
+                    cache.update(layer, kv[0], kv[1], 0, check=True)
+            qkv = torch.empty(m, q_dim + 2 * kv_dim, device="cuda")
+            attn_out = torch.empty(m, q_dim, device="cuda")
+            for layer in range(cfg["layers"]):
+                b = layer * per_layer
+                outs[b], outs[b + 1], outs[b + 2] = (qkv[:, :q_dim], qkv[:, q_dim:q_dim + kv_dim],
+                                                     qkv[:, q_dim + kv_dim:])
+
+        def attention(layer, b):
+            """RoPE on q and k (one call over their adjacent heads), the cache
+            update, attention over the context; the o projection's input."""
+            if not attn:
+                return inputs["attn"]
+            att.rope(qkv[:, :q_dim + kv_dim].view(m, heads + kvh, hd), pos0, 500000.0)
+            cache.update(layer, qkv[:, q_dim:q_dim + kv_dim].view(m, kvh, hd),
+                         qkv[:, q_dim + kv_dim:].view(m, kvh, hd), pos0)
+            att.attend(qkv[:, :q_dim].view(m, heads, hd), cache, layer, ctx, pos0, out=attn_out)
+            return attn_out
+
         def step():
             resid.copy_(resid0)
             for layer in range(cfg["layers"]):
@@ -304,13 +341,13 @@ def run_clq(args):
                 if fuse_mode == "fused":
                     clq.linear_group_fused([q, kk, v], resid, norm_weight=norm_w, eps=1e-5,
                                            outs=[outs[b], outs[b + 1], outs[b + 2]])
-                    clq.linear_fused(o, inputs["attn"], out=resid, residual=resid)
+                    clq.linear_fused(o, attention(layer, b), out=resid, residual=resid)
                     clq.linear_group_fused([gt, up], resid, norm_weight=norm_w, eps=1e-5,
                                            outs=[outs[b + 4], outs[b + 5]])
                     clq.linear_fused(dn, outs[b + 5], gate=outs[b + 4], out=resid, residual=resid)
                 else:
                     clq.linear_group([q, kk, v], rms(resid), outs=[outs[b], outs[b + 1], outs[b + 2]])
-                    o.linear(inputs["attn"], out=outs[b + 3])
+                    o.linear(attention(layer, b), out=outs[b + 3])
                     resid.add_(outs[b + 3])
                     clq.linear_group([gt, up], rms(resid), outs=[outs[b + 4], outs[b + 5]])
                     dn.linear(torch.nn.functional.silu(outs[b + 4]) * outs[b + 5], out=outs[b + 6])
@@ -340,6 +377,10 @@ def run_clq(args):
     def lin_bytes(st, dtype):
         return tp.weight_bytes(dtype, st.n, st.k) + x_bytes * m * st.k + 4 * m * st.n
     step_bytes = float(sum(lin_bytes(st, dt) for (_, st, dt, *_r) in stores))
+    if fuse_mode != "off" and args.attention != "off":
+        # each layer reads the cached keys and values of the whole context
+        per_row = cfg["head_dim"] * 4 if args.attention == "f32" else cfg["head_dim"] + 4 * -(-cfg["head_dim"] // 32)
+        step_bytes += float(cfg["layers"] * 2 * args.context * cfg["kv_heads"] * per_row)
     if dist is not None:
         t = torch.tensor([step_bytes], dtype=torch.float64, device="cuda")
         dist.all_reduce(t)
@@ -449,6 +490,9 @@ def run_clq(args):
                 "fusions": (None if fuse_mode == "off" else
                             fuse_mode + ": RMSNorm->q/k/v, o+residual, RMSNorm->gate/up, SwiGLU->down+residual, "
                                         "RMSNorm->head"),
+                "attention": (None if fuse_mode == "off" or args.attention == "off" else
+                              f"RoPE q,k; {args.attention} KV cache update; GQA attention over {args.context} "
+                              f"positions ({cfg['heads']} heads / {cfg['kv_heads']} KV heads of {cfg['head_dim']})"),
                 "weights_gb": round(job_bytes / 1e9, 3),
                 "l2": "weights per step far above the 126 MB L2; no flush",
             },

@@ -31,7 +31,8 @@ namespace {
 constexpr int kQ8Group = 32;          // local/kv-cache.lisp:20
 constexpr int kAttnThreads = 128;     // 4 warps per CTA
 constexpr int kMaxGroup = 16;         // query heads per KV head
-constexpr int kMaxPerSplit = 256;     // positions per CTA
+constexpr int kSplitRows = 64;        // positions per CTA, staged in shared memory
+constexpr int kMaxSplits = 1024;      // position ranges merged per (row, head)
 constexpr int kMaxHeadDim = 256;
 
 // ---- the Q8 codec --------------------------------------------------------
@@ -51,10 +52,19 @@ __device__ __forceinline__ float q8_decode(int8_t code, float scale) {
 // sets scale = max(FLT_MIN, peak / 127) (1 for an all-zero group), and each
 // value becomes clamp(round-half-even(value / scale), -127, 127)
 // (local/kv-cache.lisp:37-60).  A non-finite value sets *ERR.
-__global__ void kv_store_q8_kernel(int8_t* __restrict__ codes, float* __restrict__ scales,
-                                   const float* __restrict__ src, int64_t count, int kvh, int hd,
-                                   int64_t ps, int64_t hs, int64_t start, int* err) {
+// Keys (blockIdx.y = 0) and values (1) in one launch.
+struct KvStore {
+    const float* src[2];
+    uint8_t* buf[2];
+    size_t code_bytes;
+};
+
+__global__ void kv_store_q8_kernel(const KvStore S, int64_t count, int kvh, int hd, int64_t ps, int64_t hs,
+                                   int64_t start, int* err) {
     const int groups = (hd + kQ8Group - 1) / kQ8Group;
+    const float* __restrict__ src = S.src[blockIdx.y];
+    int8_t* __restrict__ codes = reinterpret_cast<int8_t*>(S.buf[blockIdx.y]);
+    float* __restrict__ scales = reinterpret_cast<float*>(S.buf[blockIdx.y] + S.code_bytes);
     const int64_t items = count * kvh * groups;
     const int lane = threadIdx.x & 31;
     for (int64_t w = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5; w < items;
@@ -80,8 +90,10 @@ __global__ void kv_store_q8_kernel(int8_t* __restrict__ codes, float* __restrict
     }
 }
 
-__global__ void kv_store_f32_kernel(float* __restrict__ dst, const float* __restrict__ src, int64_t count, int kvh,
-                                    int hd, int64_t ps, int64_t hs, int64_t start) {
+__global__ void kv_store_f32_kernel(const KvStore S, int64_t count, int kvh, int hd, int64_t ps, int64_t hs,
+                                    int64_t start) {
+    const float* __restrict__ src = S.src[blockIdx.y];
+    float* __restrict__ dst = reinterpret_cast<float*>(S.buf[blockIdx.y]);
     const int64_t total = count * kvh * hd;
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
         const int i = (int)(e % hd);
@@ -147,31 +159,95 @@ struct AttnParams {
     float* part;           // [count][n_heads][splits][hd + 2]: weighted sum, then max, sum
 };
 
+// The split's rows of one KV head, keys and values, into shared memory as
+// f32: every thread issues its 16-byte loads (4 f32 or 16 codes) before any
+// is used, so the split costs about one memory round trip.
 template <bool Q8>
-__device__ __forceinline__ float kv_at(const AttnParams& P, const void* buf, const float* scl, int64_t pos, int kv,
-                                       int e) {
-    const int64_t slot = pos * P.kvh + kv;
+__device__ __forceinline__ void stage_rows(const AttnParams& P, const void* buf, const float* scl, int64_t p0, int np,
+                                           int kv, float* dst) {
+    const int hd = P.hd;
+    if (hd % (Q8 ? 16 : 4)) {  // rows off the 16-byte grid: element by element
+        for (int e = threadIdx.x; e < np * hd; e += kAttnThreads) {
+            const int j = e / hd, d = e - j * hd;
+            const int64_t slot = (p0 + j) * P.kvh + kv;
+            if constexpr (Q8) {
+                dst[e] = q8_decode(reinterpret_cast<const int8_t*>(buf)[slot * hd + d], scl[slot * P.groups + d / kQ8Group]);
+            } else {
+                dst[e] = reinterpret_cast<const float*>(buf)[slot * hd + d];
+            }
+        }
+        return;
+    }
+    // vector rows: eight 16-byte loads per thread in flight before any store
+    constexpr int B = 8;
     if constexpr (Q8) {
-        const int8_t c = reinterpret_cast<const int8_t*>(buf)[slot * P.hd + e];
-        return q8_decode(c, scl[slot * P.groups + e / kQ8Group]);
+        const int per_row = hd / 16, n = np * per_row;
+        for (int e0 = threadIdx.x; e0 < n; e0 += B * kAttnThreads) {
+            uint4 w[B];
+            float sc[B];
+#pragma unroll
+            for (int b = 0; b < B; b++) {
+                const int e = e0 + b * kAttnThreads;
+                if (e < n) {
+                    const int j = e / per_row, c = e - j * per_row;
+                    const int64_t slot = (p0 + j) * P.kvh + kv;
+                    w[b] = *reinterpret_cast<const uint4*>(reinterpret_cast<const int8_t*>(buf) + slot * hd + c * 16);
+                    sc[b] = scl[slot * P.groups + (c * 16) / kQ8Group];
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < B; b++) {
+                const int e = e0 + b * kAttnThreads;
+                if (e < n) {
+                    const int j = e / per_row, c = e - j * per_row;
+                    const uint32_t ws[4] = {w[b].x, w[b].y, w[b].z, w[b].w};
+                    float* o = dst + j * hd + c * 16;
+#pragma unroll
+                    for (int i = 0; i < 16; i++) o[i] = q8_decode((int8_t)(ws[i >> 2] >> (8 * (i & 3))), sc[b]);
+                }
+            }
+        }
     } else {
-        return reinterpret_cast<const float*>(buf)[slot * P.hd + e];
+        const int per_row = hd / 4, n = np * per_row;
+        for (int e0 = threadIdx.x; e0 < n; e0 += B * kAttnThreads) {
+            float4 v[B];
+#pragma unroll
+            for (int b = 0; b < B; b++) {
+                const int e = e0 + b * kAttnThreads;
+                if (e < n) {
+                    const int j = e / per_row, c = e - j * per_row;
+                    const int64_t slot = (p0 + j) * P.kvh + kv;
+                    v[b] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(buf) + slot * hd + c * 4);
+                }
+            }
+#pragma unroll
+            for (int b = 0; b < B; b++) {
+                const int e = e0 + b * kAttnThreads;
+                if (e < n) {
+                    const int j = e / per_row, c = e - j * per_row;
+                    *reinterpret_cast<float4*>(dst + j * hd + c * 4) = v[b];
+                }
+            }
+        }
     }
 }
 
-// CTA (split, kv head, query row).  Scores s = (q . k) * scale for the
-// group's query heads over the split's unmasked positions (key position <=
-// query_start + row), kept in shared memory; then the split's maximum m,
-// the sum l of exp(s - m) and the sum of exp(s - m) * v.
-template <bool Q8>
+// CTA (split, kv head, query row).  The split's unmasked positions (key
+// position <= query_start + row) are staged; scores s = (q . k) * scale for
+// the group's query heads; then the split's maximum m, the sum l of
+// exp(s - m) and the sum of exp(s - m) * v.
+template <bool Q8, int G>
 __global__ void __launch_bounds__(kAttnThreads) attend_split_kernel(const AttnParams P) {
-    __shared__ float qs[kMaxGroup * kMaxHeadDim];
-    __shared__ float sc[kMaxGroup * kMaxPerSplit];
+    extern __shared__ __align__(16) float sh[];
     const int split = blockIdx.x, kv = blockIdx.y;
     const int64_t row = blockIdx.z;
-    const int G = P.n_heads / P.kvh, hd = P.hd;
+    const int hd = P.hd;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int NW = kAttnThreads / 32;
+    float* qs = sh;                                 // [G][hd]
+    float* sc = qs + G * hd;                        // [G][kSplitRows]
+    float* ks = sc + G * kSplitRows;                // [kSplitRows][hd]
+    float* vs = ks + kSplitRows * hd;               // [kSplitRows][hd]
     const int64_t last = P.query_start + row + 1 < P.end ? P.query_start + row + 1 : P.end;  // causal
     const int64_t p0 = (int64_t)split * P.per_split;
     int64_t p1 = p0 + P.per_split;
@@ -182,26 +258,26 @@ __global__ void __launch_bounds__(kAttnThreads) attend_split_kernel(const AttnPa
         const int g = e / hd, d = e - g * hd;
         qs[e] = P.q[row * P.q_ps + (int64_t)(kv * G + g) * hd + d];
     }
+    stage_rows<Q8>(P, P.keys, P.kscale, p0, np, kv, ks);
+    stage_rows<Q8>(P, P.values, P.vscale, p0, np, kv, vs);
     __syncthreads();
 
     // scores: a warp per position, lanes over the head dimension
     for (int j = warp; j < np; j += NW) {
-        float dot[kMaxGroup];
+        float dot[G];
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) dot[g] = 0.f;
+        for (int g = 0; g < G; g++) dot[g] = 0.f;
         for (int d = lane; d < hd; d += 32) {
-            const float k = kv_at<Q8>(P, P.keys, P.kscale, p0 + j, kv, d);
+            const float k = ks[j * hd + d];
 #pragma unroll
-            for (int g = 0; g < kMaxGroup; g++)
-                if (g < G) dot[g] = fmaf(qs[g * hd + d], k, dot[g]);
+            for (int g = 0; g < G; g++) dot[g] = fmaf(qs[g * hd + d], k, dot[g]);
         }
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) {
-            if (g >= G) break;
+        for (int g = 0; g < G; g++) {
             float v = dot[g];
 #pragma unroll
             for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-            if (lane == 0) sc[g * kMaxPerSplit + j] = __fmul_rn(v, P.scale);
+            if (lane == 0) sc[g * kSplitRows + j] = __fmul_rn(v, P.scale);
         }
     }
     __syncthreads();
@@ -209,13 +285,13 @@ __global__ void __launch_bounds__(kAttnThreads) attend_split_kernel(const AttnPa
     // the split's maximum and sum per query head: warp g handles heads g, g + NW, ...
     for (int g = warp; g < G; g += NW) {
         float m = -INFINITY;
-        for (int j = lane; j < np; j += 32) m = fmaxf(m, sc[g * kMaxPerSplit + j]);
+        for (int j = lane; j < np; j += 32) m = fmaxf(m, sc[g * kSplitRows + j]);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
         float l = 0.f;
         for (int j = lane; j < np; j += 32) {
-            const float p = expf(sc[g * kMaxPerSplit + j] - m);
-            sc[g * kMaxPerSplit + j] = p;
+            const float p = expf(sc[g * kSplitRows + j] - m);
+            sc[g * kSplitRows + j] = p;
             l += p;
         }
 #pragma unroll
@@ -230,52 +306,111 @@ __global__ void __launch_bounds__(kAttnThreads) attend_split_kernel(const AttnPa
 
     // weighted value sums: each thread owns dimensions d = threadIdx.x, + 128, ...
     for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
-        float acc[kMaxGroup];
+        float acc[G];
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) acc[g] = 0.f;
+        for (int g = 0; g < G; g++) acc[g] = 0.f;
         for (int j = 0; j < np; j++) {
-            const float v = kv_at<Q8>(P, P.values, P.vscale, p0 + j, kv, d);
+            const float v = vs[j * hd + d];
 #pragma unroll
-            for (int g = 0; g < kMaxGroup; g++)
-                if (g < G) acc[g] = fmaf(sc[g * kMaxPerSplit + j], v, acc[g]);
+            for (int g = 0; g < G; g++) acc[g] = fmaf(sc[g * kSplitRows + j], v, acc[g]);
         }
 #pragma unroll
-        for (int g = 0; g < kMaxGroup; g++) {
-            if (g >= G) break;
+        for (int g = 0; g < G; g++) {
             P.part[(((row * P.n_heads) + kv * G + g) * P.splits + split) * (int64_t)(hd + 2) + d] = acc[g];
         }
     }
 }
 
-// One CTA per (query row, head): merges the splits -- M = max m_s, output
-// sum_s exp(m_s - M) acc_s / sum_s exp(m_s - M) l_s -- into out[row][head * hd + d].
-__global__ void attend_merge_kernel(const float* __restrict__ part, int n_heads, int hd, int splits,
-                                    float* __restrict__ out, int64_t ldo) {
-    const int head = blockIdx.x;
+size_t attend_smem(int G, int hd) {
+    return ((size_t)G * hd + (size_t)G * kSplitRows + 2 * (size_t)kSplitRows * hd) * sizeof(float);
+}
+
+// Merges the splits of (query row, head) for a slice of 32 dimensions (one
+// warp per CTA): M = max m_s, output sum_s exp(m_s - M) acc_s / sum_s
+// exp(m_s - M) l_s into out[row][head * hd + d].  Every load is issued before
+// any is used (the kernel is one round trip to L2, not one per split).
+__global__ void __launch_bounds__(32) attend_merge_kernel(const float* __restrict__ part, int n_heads, int hd,
+                                                          int splits, float* __restrict__ out, int64_t ldo) {
+    __shared__ float wgt[kMaxSplits];
+    __shared__ float lsum[kMaxSplits];
+    const int head = blockIdx.x, lane = threadIdx.x;
     const int64_t row = blockIdx.y;
-    const float* base = part + ((row * n_heads) + head) * (int64_t)splits * (hd + 2);
-    float M = -INFINITY;
-    for (int s = 0; s < splits; s++) {
-        const float l = base[s * (int64_t)(hd + 2) + hd + 1];
-        if (l > 0.f) M = fmaxf(M, base[s * (int64_t)(hd + 2) + hd]);
-    }
-    float L = 0.f;
-    for (int s = 0; s < splits; s++) {
-        const float l = base[s * (int64_t)(hd + 2) + hd + 1];
-        if (l > 0.f) L += expf(base[s * (int64_t)(hd + 2) + hd] - M) * l;
-    }
-    for (int d = threadIdx.x; d < hd; d += blockDim.x) {
-        float a = 0.f;
-        for (int s = 0; s < splits; s++) {
-            const float l = base[s * (int64_t)(hd + 2) + hd + 1];
-            if (l > 0.f) a += expf(base[s * (int64_t)(hd + 2) + hd] - M) * base[s * (int64_t)(hd + 2) + d];
+    const int d = blockIdx.z * 32 + lane;
+    const int64_t stride = hd + 2;
+    const float* base = part + ((row * n_heads) + head) * (int64_t)splits * stride;
+    constexpr int B = 16;
+    float m = -INFINITY;
+    for (int s0 = 0; s0 < splits; s0 += 32 * B) {
+        float lv[B], mv[B];
+#pragma unroll
+        for (int b = 0; b < B; b++) {
+            const int s = s0 + b * 32 + lane;
+            lv[b] = s < splits ? base[s * stride + hd + 1] : 0.f;
+            mv[b] = s < splits ? base[s * stride + hd] : -INFINITY;
         }
-        out[row * ldo + (int64_t)head * hd + d] = a / L;
+#pragma unroll
+        for (int b = 0; b < B; b++) {
+            const int s = s0 + b * 32 + lane;
+            if (s < splits) {
+                lsum[s] = lv[b];
+                wgt[s] = lv[b] > 0.f ? mv[b] : -INFINITY;
+                m = fmaxf(m, wgt[s]);
+            }
+        }
     }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    __syncwarp();
+    float L = 0.f;
+    for (int s = lane; s < splits; s += 32) {
+        const float w = lsum[s] > 0.f ? expf(wgt[s] - m) : 0.f;
+        wgt[s] = w;
+        L = fmaf(w, lsum[s], L);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
+    __syncwarp();
+    if (d >= hd) return;
+    float a = 0.f;
+    for (int s0 = 0; s0 < splits; s0 += B) {
+        float v[B];
+#pragma unroll
+        for (int b = 0; b < B; b++) v[b] = s0 + b < splits ? base[(s0 + b) * stride + d] : 0.f;
+#pragma unroll
+        for (int b = 0; b < B; b++)
+            if (s0 + b < splits) a = fmaf(wgt[s0 + b], v[b], a);
+    }
+    out[row * ldo + (int64_t)head * hd + d] = a / L;
 }
 
 __global__ void fill_kernel(float* __restrict__ p, int64_t n, float v) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) p[i] = v;
+}
+
+template <typename Kern>
+cudaError_t attend_smem_limit(Kern kern, size_t smem) {
+    if (smem <= 48 * 1024) return cudaSuccess;
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+// The split kernel for G query heads per KV head (1, 2, 4, 8 or 16).
+template <bool Q8>
+cudaError_t launch_split(int G, dim3 grid, size_t smem, cudaStream_t s, const AttnParams& P) {
+    cudaError_t e = cudaErrorNotSupported;
+    switch (G) {
+#define CLQ_SPLIT_CASE(n)                                                        \
+    case n:                                                                     \
+        e = attend_smem_limit(attend_split_kernel<Q8, n>, smem);                \
+        if (e == cudaSuccess) attend_split_kernel<Q8, n><<<grid, kAttnThreads, smem, s>>>(P); \
+        break;
+        CLQ_SPLIT_CASE(1)
+        CLQ_SPLIT_CASE(2)
+        CLQ_SPLIT_CASE(4)
+        CLQ_SPLIT_CASE(8)
+        CLQ_SPLIT_CASE(16)
+#undef CLQ_SPLIT_CASE
+    }
+    return e;
 }
 
 unsigned grid_for(int64_t work, int threads) {
@@ -416,22 +551,23 @@ int clq_kv_cache_update(clq_kv_cache* c, int layer, const float* k, const float*
     int rc;
     if ((rc = kv_check_device(c))) return rc;
     cudaStream_t s = (cudaStream_t)stream;
-    for (int which = 0; which < 2; which++) {
-        const float* src = which ? v : k;
-        uint8_t* buf = kv_buffer(c, layer, which);
-        if (c->type == CLQ_KV_F32) {
-            const int64_t n = count * c->kvh * c->hd;
-            clq::kv_store_f32_kernel<<<clq::grid_for(n, 256), 256, 0, s>>>(reinterpret_cast<float*>(buf), src, count, c->kvh,
-                                                                            c->hd, pos_stride, head_stride, start);
-        } else {
-            const int64_t warps = count * c->kvh * c->groups;
-            clq::kv_store_q8_kernel<<<clq::grid_for(warps * 32, 256), 256, 0, s>>>(
-                reinterpret_cast<int8_t*>(buf), reinterpret_cast<float*>(buf + c->code_bytes), src, count, c->kvh, c->hd,
-                pos_stride, head_stride, start, c->err);
-        }
-        const cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return clq::set_error(CLQ_ERR_CUDA, "KV cache store: %s", cudaGetErrorString(e));
+    clq::KvStore S;
+    S.src[0] = k;
+    S.src[1] = v;
+    S.buf[0] = kv_buffer(c, layer, 0);
+    S.buf[1] = kv_buffer(c, layer, 1);
+    S.code_bytes = c->code_bytes;
+    if (c->type == CLQ_KV_F32) {
+        const int64_t n = count * c->kvh * c->hd;
+        clq::kv_store_f32_kernel<<<dim3(clq::grid_for(n, 256), 2), 256, 0, s>>>(S, count, c->kvh, c->hd, pos_stride,
+                                                                                 head_stride, start);
+    } else {
+        const int64_t warps = count * c->kvh * c->groups;
+        clq::kv_store_q8_kernel<<<dim3(clq::grid_for(warps * 32, 256), 2), 256, 0, s>>>(S, count, c->kvh, c->hd, pos_stride,
+                                                                                         head_stride, start, c->err);
     }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return clq::set_error(CLQ_ERR_CUDA, "KV cache store: %s", cudaGetErrorString(e));
     return CLQ_OK;
 }
 
@@ -502,9 +638,9 @@ int clq_attend_device(const float* q, int64_t count, int n_heads, int64_t q_pos_
     if (!c) return kv_fail(CLQ_ERR_ARGUMENT, "null cache");
     if (layer < 0 || layer >= c->layers) return clq::set_error(CLQ_ERR_ARGUMENT, "layer %d outside 0..%d", layer, c->layers - 1);
     if (count < 0 || query_start < 0) return kv_fail(CLQ_ERR_SHAPE, "negative query rows or start");
-    if (n_heads < c->kvh || n_heads % c->kvh || n_heads / c->kvh > clq::kMaxGroup)
-        return clq::set_error(CLQ_ERR_SHAPE, "%d query heads over %d KV heads (groups of at most %d)", n_heads, c->kvh,
-                              clq::kMaxGroup);
+    if (n_heads < c->kvh || n_heads % c->kvh || n_heads / c->kvh > clq::kMaxGroup ||
+        ((n_heads / c->kvh) & (n_heads / c->kvh - 1)))
+        return clq::set_error(CLQ_ERR_SHAPE, "%d query heads over %d KV heads (groups of 1, 2, 4, 8 or 16)", n_heads, c->kvh);
     if (c->hd > clq::kMaxHeadDim) return clq::set_error(CLQ_ERR_UNSUPPORTED, "head dimension %d above %d", c->hd, clq::kMaxHeadDim);
     if (end < 1 || end > c->n_ctx) return clq::set_error(CLQ_ERR_SHAPE, "prefix %lld of a %lld context", (long long)end, (long long)c->n_ctx);
     if (q_pos_stride < (int64_t)n_heads * c->hd || ldo < (int64_t)n_heads * c->hd)
@@ -530,12 +666,15 @@ int clq_attend_device(const float* q, int64_t count, int n_heads, int64_t q_pos_
     P.hd = c->hd;
     P.groups = c->groups;
     P.scale = 1.f / sqrtf((float)c->hd);  // local/blocks.lisp:311
-    // positions split so that the grid covers the SMs about twice, at most 256 a CTA
+    // positions split so that the grid covers the SMs about twice, at most 64 a CTA
     const int64_t ctas_per_split = (int64_t)c->kvh * count;
     int64_t splits = (2 * (int64_t)clq::sm_count() + ctas_per_split - 1) / ctas_per_split;
-    const int64_t min_splits = (end + clq::kMaxPerSplit - 1) / clq::kMaxPerSplit;
+    const int64_t min_splits = (end + clq::kSplitRows - 1) / clq::kSplitRows;
     if (splits < min_splits) splits = min_splits;
     if (splits > (end + 15) / 16) splits = (end + 15) / 16 > min_splits ? (end + 15) / 16 : min_splits;
+    if (splits > clq::kMaxSplits)
+        return clq::set_error(CLQ_ERR_UNSUPPORTED, "prefix %lld above %d positions", (long long)end,
+                              clq::kMaxSplits * clq::kSplitRows);
     if (splits > 65535 || count > 65535) return kv_fail(CLQ_ERR_UNSUPPORTED, "too many query rows or positions for one launch");
     P.splits = (int)splits;
     P.per_split = (end + splits - 1) / splits;
@@ -545,12 +684,13 @@ int clq_attend_device(const float* q, int64_t count, int n_heads, int64_t q_pos_
     if (e != cudaSuccess) return clq::set_error(CLQ_ERR_CUDA, "attention scratch: %s", cudaGetErrorString(e));
     P.part = part;
     const dim3 grid((unsigned)splits, (unsigned)c->kvh, (unsigned)count);
-    if (c->type == CLQ_KV_Q8) clq::attend_split_kernel<true><<<grid, clq::kAttnThreads, 0, s>>>(P);
-    else clq::attend_split_kernel<false><<<grid, clq::kAttnThreads, 0, s>>>(P);
-    e = cudaGetLastError();
+    const int G = n_heads / c->kvh;
+    const size_t smem = clq::attend_smem(G, c->hd);
+    e = c->type == CLQ_KV_Q8 ? clq::launch_split<true>(G, grid, smem, s, P) : clq::launch_split<false>(G, grid, smem, s, P);
+    if (e == cudaSuccess) e = cudaGetLastError();
     if (e == cudaSuccess) {
-        clq::attend_merge_kernel<<<dim3((unsigned)n_heads, (unsigned)count), 128, 0, s>>>(part, n_heads, c->hd, (int)splits,
-                                                                                          out, ldo);
+        clq::attend_merge_kernel<<<dim3((unsigned)n_heads, (unsigned)count, (unsigned)((c->hd + 31) / 32)), 32, 0, s>>>(
+            part, n_heads, c->hd, (int)splits, out, ldo);
         e = cudaGetLastError();
     }
     const cudaError_t f = cudaFreeAsync(part, s);
