@@ -10,8 +10,10 @@
 // (rows past the weight's end read as zeros); the warp waits for a slot,
 // reads its words, refills the
 // slot with the unit DEPTH ahead and multiplies with the integer-MMA product
-// of gemv_i8.cuh.  No warp waits for another except once, after the
-// activations are staged, so a slow warp never stalls the others' streams.
+// of gemv_i8.cuh -- for several activation rows, one MMA per pair of rows on
+// the same unpacked weight fragments (NP pairs, up to eight rows).  No warp
+// waits for another except once, after the activations are staged, so a slow
+// warp never stalls the others' streams.
 //
 // A tile's K range can be split between consecutive warps.  A tile inside one
 // warp's run is finished by that warp from its registers.  For a tile shared
