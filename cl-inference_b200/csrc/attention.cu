@@ -17,8 +17,6 @@
 #include <cfloat>
 #include <cmath>
 #include <cstdint>
-#include <mutex>
-#include <vector>
 
 #include <cuda_runtime.h>
 
@@ -625,6 +623,8 @@ int clq_rope_device(float* x, int64_t count, int heads, int head_dim, int64_t po
     if (!rows_disjoint(count, pos_stride, heads, head_stride, head_dim))
         return clq::set_error(CLQ_ERR_SHAPE, "rows of strides (%lld, %lld) overlap (%lld positions, %d heads of %d)",
                               (long long)pos_stride, (long long)head_stride, (long long)count, heads, head_dim);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return kv_fail(CLQ_ERR_NO_DEVICE, "no CUDA device");
     const int64_t n = count * heads * (rope_dims / 2);
     clq::rope_kernel<<<clq::grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
         x, count, heads, pos_stride, head_stride, rope_dims, start, theta, factors, pairing == CLQ_ROPE_NEOX);

@@ -85,3 +85,50 @@ def test_cache_starts_empty_and_forget_is_safe(clq):
     assert lib.clq_cache_stats(ctypes.byref(n), ctypes.byref(b)) == 0
     assert (n.value, b.value) == (0, 0)
     assert lib.clq_forget(None, 0) == 0
+
+
+def test_kv_cache_rope_and_attention_argument_checks(clq):
+    """The cache, RoPE and attention entry points reject bad arguments before
+    any device work (so these run without a GPU)."""
+    lib = clq._lib.lib
+    out = ctypes.c_void_p()
+    assert lib.clq_kv_cache_create(0, 1, 1, 8, 0, ctypes.byref(out)) == 2      # no positions
+    assert lib.clq_kv_cache_create(4, 1, 1, 8, 7, ctypes.byref(out)) == 1      # unknown cache type
+    assert "unknown cache type 7" in clq._lib.last_error()
+    assert lib.clq_kv_cache_create(4, 1, 1, 8, 0, None) == 1
+    assert lib.clq_kv_cache_destroy(None) == 0
+    assert lib.clq_kv_cache_info(None, None, None, None, None, None) == 1
+    assert lib.clq_kv_cache_update(None, 0, None, None, 1, 8, 8, 0, None) == 1
+    status = ctypes.c_int()
+    assert lib.clq_kv_cache_status(None, ctypes.byref(status)) == 1
+    assert lib.clq_kv_cache_read(None, 0, 1, None, None, None) == 1
+    assert lib.clq_attend_device(None, 1, 4, 32, None, 0, 1, 0, None, 32, None) == 1
+    fake = 256  # a non-null address that the checks below never reach
+    rope = lib.clq_rope_device
+    assert rope(fake, 1, 2, 8, 16, 8, 7, 0, 10000.0, None, 0, None) == 2      # odd rotated width
+    assert rope(fake, 1, 2, 8, 16, 8, 10, 0, 10000.0, None, 0, None) == 2     # wider than the head
+    assert rope(fake, 1, 2, 8, 16, 8, 8, 0, 10000.0, None, 5, None) == 1      # unknown pairing
+    assert rope(fake, 1, 2, 8, 16, 8, 8, 0, 0.0, None, 0, None) == 1          # theta must be positive
+    assert rope(fake, 1, 2, 8, 8, 4, 8, 0, 10000.0, None, 0, None) == 2       # heads overlap
+    assert rope(fake, 3, 2, 8, 8, 16, 8, 0, 10000.0, None, 0, None) == 2      # positions overlap heads
+    # positions inside each head (a transposed layout) are fine: without a GPU the call then fails as such
+    rc = rope(fake, 3, 2, 8, 8, 24, 8, 0, 10000.0, None, 0, None)
+    import torch
+    if not torch.cuda.is_available():
+        assert rc == 8, clq._lib.last_error()
+    assert rope(None, 0, 2, 8, 16, 8, 8, 0, 10000.0, None, 0, None) == 0      # no rows: nothing to do
+    assert rope(None, 1, 2, 8, 16, 8, 8, 0, 10000.0, None, 0, None) == 1      # null rows
+
+
+def test_kv_cache_needs_a_device(clq):
+    import importlib
+
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    att = importlib.import_module("cl-inference_b200.attention")
+    with pytest.raises(clq.ClqError) as err:
+        att.KVCache(16, 1, 2, 8)
+    assert err.value.status == "CLQ_ERR_NO_DEVICE"
+    with pytest.raises(clq.ClqError):
+        att.KVCache(16, 1, 2, 8, "q4")
