@@ -101,3 +101,22 @@ def test_llama3_rope_factors_follow_the_reference_formula():
         att.llama3_rope_factors(128, 500000.0, {"rope_type": "yarn"})
     with pytest.raises(ValueError):
         att.llama3_rope_factors(128, 500000.0, dict(scaling, high_freq_factor=0.5))
+
+
+@pytest.mark.parametrize("pairing", ["adjacent", "neox"])
+def test_rope_is_relative(pairing):
+    """Shifting every position leaves attention unchanged (tests/local/blocks.lisp,
+    blocks-rope-is-relative): the rotation of q and k at positions p and p + 5
+    gives the same scores up to the f32 rounding of the tables."""
+    rng = np.random.default_rng(3)
+    count, heads, kvh, hd = 2, 4, 2, 8
+    q = rng.standard_normal((count, heads, hd)).astype(np.float32)
+    k = rng.standard_normal((count, kvh, hd)).astype(np.float32)
+    v = rng.standard_normal((count, kvh, hd)).astype(np.float32)
+    outs = []
+    for start in (0, 5):
+        cos, sin = ref.rope_tables(start, count, hd, 10000.0)
+        qr = ref.apply_rope(q, cos, sin, pairing, hd)
+        kr = ref.apply_rope(k, cos, sin, pairing, hd)
+        outs.append(ref.attend_f64(qr, kr, v, ref.causal_mask(count, count, start, start), heads, kvh))
+    assert np.allclose(outs[0], outs[1], rtol=1e-5, atol=1e-5)

@@ -165,3 +165,32 @@ def test_attention_argument_checks(cuda, att, clq):
             att.attend(q, cache, 0, 9, 3)  # past the context
         with pytest.raises(clq.ClqError):
             att.attend(q, cache, 1, 4, 3)  # no such layer
+
+
+@pytest.mark.parametrize("cache_type", ["f32", "q8"])
+def test_cache_filled_in_chunks_matches_a_full_pass(cuda, att, cache_type):
+    """tests/local/blocks.lisp, blocks-cache-matches-a-full-pass: rows stored 3,
+    then 1, then 1 at a time and attended as they arrive give, for the last
+    row, what one pass over all five rows gives."""
+    torch = cuda
+    rng = np.random.default_rng(9)
+    heads, kv, hd, n = 4, 2, 32, 5
+    keys = rng.standard_normal((n, kv, hd)).astype(np.float32)
+    vals = rng.standard_normal((n, kv, hd)).astype(np.float32)
+    q = rng.standard_normal((n, heads, hd)).astype(np.float32)
+    k_used, v_used = keys, vals
+    if cache_type == "q8":
+        k_used = ref.q8_prefix(*ref.q8_store(keys))
+        v_used = ref.q8_prefix(*ref.q8_store(vals))
+    want = ref.attend_f64(q, k_used, v_used, ref.causal_mask(n, n, 0, 0), heads, kv)
+    scale = np.abs(want).max()
+    dk, dv, dq = (torch.from_numpy(a).cuda() for a in (keys, vals, q))
+    with att.KVCache(8, 1, kv, hd, cache_type) as full, att.KVCache(8, 1, kv, hd, cache_type) as chunked:
+        full.update(0, dk, dv, 0, check=True)
+        whole = att.attend(dq, full, 0, n, 0).cpu().numpy()
+        assert np.abs(whole - want).max() <= 1e-5 * scale
+        for b, e in ((0, 3), (3, 4), (4, 5)):
+            chunked.update(0, dk[b:e], dv[b:e], b, check=True)
+            part = att.attend(dq[b:e].contiguous(), chunked, 0, e, b).cpu().numpy()
+            assert np.abs(part - want[b:e]).max() <= 1e-5 * scale
+
