@@ -1,7 +1,9 @@
 """The CPU oracle of the KV cache codec, RoPE and attention, pinned to the
 reference's own cases (no GPU needed).
 
-The Q8 cases are those of tests/local/cache.lisp: rounding and groups
+The Q8 cases are those of tests/local/cache.lisp (as the fixture
+tests/golden/kv_golden.json, made from that file's text by
+tests/golden/make_kv_golden.py): rounding and groups
 (q8-cache-groups-rounding-and-overwrite), finite extrema
 (q8-cache-reconstructs-finite-extrema), strided rows
 (q8-cache-encodes-strided-rows) and non-finite rows
@@ -9,45 +11,52 @@ The Q8 cases are those of tests/local/cache.lisp: rounding and groups
 are checked against their definitions in local/blocks.lisp.
 """
 import importlib
+import json
 import math
+import pathlib
 
 import numpy as np
 import pytest
 
 import attention as ref  # oracle/attention.py
 
+# the reference's cases, read from tests/local/cache.lisp by tests/golden/make_kv_golden.py
+KV = json.loads((pathlib.Path(__file__).resolve().parent / "golden" / "kv_golden.json").read_text())
+F32_MAX = np.finfo(np.float32).max
+NONFINITE = {"single-float-positive-infinity": np.inf, "single-float-nan": np.nan}
+
 
 def test_q8_rounding_groups_and_zero_scales():
-    values = [127.0, -127.0, 0.5, 1.5, 2.5, -0.5, -1.5] + [0.0] * 25 + [0.0] * 3
-    rows = np.array(values, dtype=np.float32).reshape(1, 1, 35)
+    case = KV["rounding"]
+    rows = np.array(case["row"], dtype=np.float32).reshape(case["shape"])
     codes, scales = ref.q8_store(rows)
-    decoded = ref.q8_prefix(codes, scales).reshape(35)
-    want = [127.0, -127.0, 0.0, 2.0, 2.0, 0.0, -2.0] + [0.0] * 28
-    assert decoded.tolist() == want
-    assert scales.shape == (1, 1, 2) and scales[0, 0, 1] == 1.0  # all-zero group
-    # a cache of three positions holds 3 x 35 codes and 3 x 2 scales
-    assert codes.size * 3 == 105 and scales.size * 3 == 6
+    decoded = ref.q8_prefix(codes, scales).reshape(-1)
+    assert decoded.tolist() == case["decoded"]
+    assert scales.reshape(-1)[case["zero_group_index"]] == case["zero_group_scale"]  # all-zero group
+    # the cache's buffers for n_ctx positions
+    assert codes.size * case["n_ctx"] == case["bytes"] and scales.size * case["n_ctx"] == case["scales"]
 
 
 def test_q8_reconstructs_finite_extrema():
-    big = float(np.finfo(np.float32).max)
-    codes, scales = ref.q8_store(np.array([big, -big], dtype=np.float32).reshape(1, 1, 2))
-    decoded = ref.q8_prefix(codes, scales).reshape(2)
-    assert decoded[0] == np.float32(big) and decoded[1] == np.float32(-big)
+    row = [F32_MAX if v == "most-positive-single-float" else -F32_MAX for v in KV["extrema"]["row"]]
+    codes, scales = ref.q8_store(np.array(row, dtype=np.float32).reshape(1, 1, len(row)))
+    decoded = ref.q8_prefix(codes, scales).reshape(-1)
+    assert decoded.tolist() == [float(np.float32(v)) for v in row]
 
 
 def test_q8_strided_rows_encode_as_their_copy():
-    source = np.arange(210, dtype=np.float32).reshape(2, 3, 35)
-    rows = source.transpose(1, 0, 2)
+    case = KV["strided"]
+    source = np.arange(case["arange"], dtype=np.float32).reshape(case["shape"])
+    rows = source.transpose(case["axes"])
     a = ref.q8_store(rows)
     b = ref.q8_store(np.ascontiguousarray(rows))
     assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
 
 
-@pytest.mark.parametrize("bad", [np.inf, np.nan])
-def test_q8_rejects_non_finite(bad):
+@pytest.mark.parametrize("name", KV["nonfinite"])
+def test_q8_rejects_non_finite(name):
     with pytest.raises(ref.NonFinite):
-        ref.q8_store(np.array([bad], dtype=np.float32).reshape(1, 1, 1))
+        ref.q8_store(np.array([NONFINITE[name]], dtype=np.float32).reshape(1, 1, 1))
 
 
 def test_rope_tables_and_pairings():
