@@ -179,3 +179,22 @@ def test_matches_the_gguf_package_reader(mod, tmp_path, synth):
         assert f.metadata("llama.block_count") == 2
         assert f.metadata("tokenizer.ggml.model") == "gpt2"
         assert f.metadata("general.architecture") == "llama"
+
+
+@pytest.mark.parametrize("dtype", ["q4_0", "q4_k", "q6_k", "q8_0"])
+def test_golden_blocks_through_a_gguf_file(mod, tmp_path, golden, oracle, dtype):
+    """tests/local/packed.lisp, packed-gguf-uses-mapped-storage: the golden
+    blocks written as a GGUF tensor read back as the same bytes (from the
+    mapping) and decode (the oracle here; the device in tests/test_gpu_gguf.py)
+    to the golden values bit for bit."""
+    g, _ = mod
+    gd = golden[dtype]
+    nblocks = gd["bytes"].size // gd["block_bytes"]
+    path = write(tmp_path, gb.build(tensors=[("packed", (gd["elements"], nblocks), gd["ggml_type"], gd["bytes"])]))
+    with g.GGUFFile(path) as f:
+        info = f.tensors["packed"]
+        assert info.ggml_type == gd["ggml_type"] and info.shape == (nblocks, gd["elements"])
+        raw = f.tensor_bytes("packed")
+        assert raw.tobytes() == gd["bytes"].tobytes()
+        out = np.asarray(oracle.dequantize(dtype, raw), np.float32)
+        assert np.array_equal(out.view(np.uint32), gd["values"].view(np.uint32))
