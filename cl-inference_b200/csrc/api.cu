@@ -4,6 +4,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <memory>
 #include <mutex>
@@ -906,6 +907,14 @@ int clq_tp_create(int rank, int world, int64_t cap, void* const* recv, void* con
     for (int r = 0; r < world; r++) L.peer_recv[r] = static_cast<uint2*>(recv[r]);
     L.my_recv = L.peer_recv[rank];
     L.epochs = static_cast<uint32_t*>(flags[rank]);
+    // polls of one peer word before a wait gives up (about 1 us each under
+    // load, so seconds); CLQ_TP_WAIT_POLLS lowers it for tests that make the
+    // wait run out on purpose
+    L.wait_polls = 1u << 22;
+    if (const char* e = getenv("CLQ_TP_WAIT_POLLS")) {
+        const long long v = atoll(e);
+        if (v >= 1 && v <= (1ll << 30)) L.wait_polls = (uint32_t)v;
+    }
     *out = t;
     return CLQ_OK;
 }

@@ -69,6 +69,7 @@ struct TpLink {
     uint32_t* epochs;               // [kMaxTpCtas]
     int rank, world;
     int64_t cap;                    // words per (parity, writer, CTA) region
+    uint32_t wait_polls;            // polls of one peer word before the wait gives up
 };
 // out = sum over ranks of x_r W_r^T (the row-parallel shard product of each
 // rank), computed by the bulk GEMV with the reduction over peer memory fused

@@ -7,14 +7,16 @@
 //   prep kernel  x -> fp16 scaled by a per-token power of two, written to
 //                scratch pre-swizzled (SWIZZLE_128B image of every 64-wide
 //                K block), so a plain 1-D bulk copy lands a ready MMA operand;
-//   warps 0-3    dequantize the weight tile (fp32 math, one rounding to fp16)
-//                straight into the swizzled A stage; later the epilogue;
-//   warp 4       bulk-copies the activation stage (B), mbarrier tx-count;
-//   warp 5       one thread issues the MMAs and commits stages back.
+//   warps 0-7    dequantize the weight tile (fp32 math, one rounding to fp16)
+//                straight into the swizzled A stage, two threads per weight
+//                row; later the epilogue;
+//   warp 8       bulk-copies the activation stage (B), mbarrier tx-count;
+//   warp 9       one thread issues the MMAs and commits stages back.
 // The MMA operands are fp16 (weights rounded once; activations rounded once
 // after the power-of-two scaling), products accumulate in fp32.
-// Every mbarrier wait is bounded; on expiry the CTA records an error code,
-// stops issuing, drains what it issued and frees its tensor memory.
+// Every mbarrier wait is bounded; on expiry the CTA records CLQ_ERR_TIMEOUT in
+// the library's device status word (read by clq_device_status), stops
+// issuing, drains what it issued and frees its tensor memory.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -62,7 +64,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
         if (*(volatile int*)err) return false;
         if (i > 64) __nanosleep(32);
     }
-    atomicExch(err, 1);
+    atomicExch(err, CLQ_ERR_TIMEOUT);
     return false;
 }
 // Bounded wait that ignores the error flag: used before teardown so that copies
@@ -371,7 +373,7 @@ struct GemmParams {
     int64_t ldo;
     int tn;             // tokens per tile (power of two, 32..256)
     int kb_per_split;
-    int* err;
+    int* err;           // the device status word
 };
 
 template <int D>
@@ -574,7 +576,7 @@ GemmPlan plan_gemm_tc_capped(int64_t rows, int64_t k, int64_t m, size_t cap) {
 
 size_t gemm_tc_scratch_bytes(const GemmPlan& g) {
     auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
-    return al(sizeof(int)) + al(g.xs_bytes) + al(g.us_bytes) + al(g.part_bytes);
+    return al(g.xs_bytes) + al(g.us_bytes) + al(g.part_bytes);
 }
 
 bool gemm_tc_supported(const WeightView& w, int64_t m) { return w.k > 0 && w.k % 256 == 0 && m > 0; }
@@ -582,12 +584,13 @@ bool gemm_tc_supported(const WeightView& w, int64_t m) { return w.k > 0 && w.k %
 cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m, float* out,
                            int64_t ldo, uint8_t* scratch, const GemmPlan& g, cudaStream_t stream) {
     auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
-    int* err = reinterpret_cast<int*>(scratch);
-    uint8_t* xs = scratch + al(sizeof(int));
+    // an expired wait is reported through the status word clq_device_status reads
+    int* err = device_status_word();
+    if (!err) return cudaErrorNotSupported;
+    uint8_t* xs = scratch;
     float* us = reinterpret_cast<float*>(xs + al(g.xs_bytes));
     float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(us) + al(g.us_bytes));
-    cudaError_t e = cudaMemsetAsync(err, 0, sizeof(int), stream);
-    if (e != cudaSuccess) return e;
+    cudaError_t e = cudaSuccess;
     const unsigned prep_grid = (unsigned)(g.token_tiles * g.tn);
     switch (xtype) {
     case CLQ_X_F32: prep_x_kernel<float><<<prep_grid, 256, 0, stream>>>((const float*)x, m, w.k, g.tn, xs, us); break;

@@ -443,16 +443,20 @@ __device__ __forceinline__ void compute_chunk(const uint32_t (&w)[2][Words<D>::n
     }
 }
 
-// One 8-byte (epoch, value) word to / from another GPU's memory: the store and
-// the load are single-copy atomic, so a word carrying the expected epoch also
-// carries its value -- no fences or flags.
+// One 8-byte (epoch, value) word to / from another GPU's memory, as ONE 64-bit
+// scalar access (epoch in the low half, the value's bits in the high half).
+// The PTX memory model makes an aligned scalar access single-copy atomic
+// (a vector access is a set of element accesses in no set order), so a word
+// read with the expected epoch also carries that call's value: no fences or
+// flags are needed.
 __device__ __forceinline__ void st_word(uint2* p, uint32_t ep, float v) {
-    asm volatile("st.volatile.global.v2.u32 [%0], {%1, %2};" ::"l"(p), "r"(ep), "r"(__float_as_uint(v)) : "memory");
+    const unsigned long long w = (unsigned long long)ep | ((unsigned long long)__float_as_uint(v) << 32);
+    asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
 }
 __device__ __forceinline__ uint2 ld_word(const uint2* p) {
-    uint2 v;
-    asm volatile("ld.volatile.global.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p) : "memory");
-    return v;
+    unsigned long long w;
+    asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(w) : "l"(p) : "memory");
+    return make_uint2((uint32_t)w, (uint32_t)(w >> 32));
 }
 
 // The all-reduce tail of the tensor-parallel GEMVs: this CTA's outputs are the
@@ -476,7 +480,7 @@ __device__ void tp_gather_sum(const TP& tp, const Member& M, int t_begin, int t_
         for (int q = 0; q < tp.world; q++) {  // fixed rank order
             const uint2* src = slots + q * rank_stride + i;
             uint2 w = ld_word(src);
-            for (uint32_t it = 0; w.x != ep && it < (1u << 22); it++) {
+            for (uint32_t it = 0; w.x != ep && it < tp.wait_polls; it++) {
                 if (*(volatile int*)err) break;
                 if (it > 32) __nanosleep(32);
                 w = ld_word(src);

@@ -304,9 +304,11 @@ int parse(clq_gguf* g) {
             return format_error("Tensor %s offset %llu is not aligned to %llu", t->name.c_str(),
                                 (unsigned long long)t->offset, (unsigned long long)g->alignment);
         if (t->offset < end) return format_error("Tensor %s overlaps another tensor", t->name.c_str());
-        end = t->offset + t->nbytes;
-        if (end < t->offset || g->data_start + end > g->size)
+        // compared without sums that could wrap: data_start <= size holds here
+        const uint64_t room = g->size - g->data_start;
+        if (t->offset > room || t->nbytes > room - t->offset)
             return format_error("Tensor %s extends past the end of the file", t->name.c_str());
+        end = t->offset + t->nbytes;
     }
     return CLQ_OK;
 }

@@ -7,46 +7,19 @@ the GPU; this module only validates, views and moves host buffers.
 Paths in docstrings are relative to the cl-inference project.
 """
 import weakref
-from dataclasses import dataclass
 
 import numpy as np
 
 from . import _lib
+# the dtypes of quant/q8-0.lisp:5-6 and the registrations of quant/packed.lisp:156-158
+from .geometry import BY_GGML_TYPE, DTYPES, PackedDtype, UnsupportedOperation, find_dtype  # noqa: F401
 
 
 class PackedError(ValueError):
     """The reference's Lisp `error` for bad storage, views or copies."""
 
 
-class UnsupportedOperation(TypeError):
-    """ct:unsupported-operation: no executor resolves (quant/packed.lisp:126-139)."""
-
-
-@dataclass(frozen=True)
-class PackedDtype:
-    name: str
-    ggml_type: int
-    block_size: int
-    block_bytes: int
-
-
-# quant/q8-0.lisp:5-6 and the registrations of quant/packed.lisp:156-158
-DTYPES = {
-    "q8_0": PackedDtype("q8_0", _lib.CLQ_Q8_0, 32, 34),
-    "q4_0": PackedDtype("q4_0", _lib.CLQ_Q4_0, 32, 18),
-    "q4_k": PackedDtype("q4_k", _lib.CLQ_Q4_K, 256, 144),
-    "q6_k": PackedDtype("q6_k", _lib.CLQ_Q6_K, 256, 210),
-}
-BY_GGML_TYPE = {d.ggml_type: d for d in DTYPES.values()}
-
-
-def find_dtype(dtype):
-    if isinstance(dtype, PackedDtype):
-        return dtype
-    try:
-        return DTYPES[str(dtype).lower().lstrip(":")]
-    except KeyError:
-        raise UnsupportedOperation(f"{dtype!r} is not a packed dtype") from None
+assert all(getattr(_lib, "CLQ_" + d.name.upper()) == d.ggml_type for d in DTYPES.values())
 
 
 class PackedStorage:

@@ -10,7 +10,7 @@ over their bit fields:
 """
 import numpy as np
 
-from .quant import find_dtype
+from .geometry import find_dtype
 
 
 def _half_bytes(values):

@@ -21,7 +21,7 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from .quant import find_dtype
+from .geometry import find_dtype
 
 
 @dataclass(frozen=True)

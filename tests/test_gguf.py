@@ -139,6 +139,21 @@ def test_rejects_overlapping_tensors(mod, tmp_path):
     open_bad(mod, tmp_path, gb.build(tensors=[("a", (4,), 0, four, 0), ("b", (4,), 0, four, 0)]))
 
 
+def test_rejects_offsets_that_wrap_past_the_end(mod, tmp_path):
+    """A tensor whose aligned offset sits just below 2^64 would pass a check of
+    data_start + offset + nbytes against the file size once the sum wraps; the
+    reader rejects it like any tensor past the end of the file."""
+    four = gb.f32_bytes([1.0, 2.0, 3.0, 4.0])
+    good = gb.build(tensors=[("t", (4,), 0, four, 0)])
+    # the tensor record ends with its u64 offset (0) right before the header padding
+    rec = gb._string("t") + gb._uint(1, 4) + gb._uint(4, 8) + gb._uint(0, 4)
+    at = good.index(rec) + len(rec)
+    assert good[at:at + 8] == bytes(8)
+    for offset in (2**64 - 32, 2**64 - 4096, 2**63):
+        bad = good[:at] + gb._uint(offset, 8) + good[at + 8:]
+        open_bad(mod, tmp_path, bad)
+
+
 def test_missing_file_is_an_io_error(mod, tmp_path):
     g, lib = mod
     with pytest.raises(lib.ClqError) as err:

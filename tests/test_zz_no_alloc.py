@@ -1,10 +1,11 @@
-"""clq_linear_device_noalloc against clq_linear_device (needs a B200).
+"""clq_linear_device_noalloc against clq_linear_device and the fp64 oracle (needs a B200).
 
 The allocation-free entry point runs the tensor-core prefill GEMM with its
 staging in the library's fixed device buffer.  Called through the C-ABI on two
 different requests in a row, each result must agree with the allocating entry
 point within the linear-output tolerance (the two may split K differently, so
-the sums can round differently); a repeated request must repeat its result
+the sums can round differently) and meet the GEMM's bounds against the fp64
+oracle on a slice of weight rows; a repeated request must repeat its result
 bit for bit whatever the buffer held before; a request too big for the buffer
 must be refused before any device work.  This file sorts last so the buffer is
 also exercised after the rest of the suite has run in the process.
@@ -54,7 +55,7 @@ CASES = [
 ]
 
 
-def test_noalloc_matches_allocating_entry_point_on_consecutive_calls(cuda, clq, synth):
+def test_noalloc_matches_allocating_entry_point_on_consecutive_calls(cuda, clq, synth, oracle):
     torch = cuda
     for dtype, n, k, m, xt in CASES:
         data = synth.packed_blocks(dtype, n, k, seed=n + m)
@@ -64,6 +65,14 @@ def test_noalloc_matches_allocating_entry_point_on_consecutive_calls(cuda, clq, 
         want = store.linear(x)
         torch.cuda.synchronize()
         agree(got, want)
+        # the fp64 oracle on the first 128 weight rows: the norm gate and the
+        # GEMM's per-element bound for its two fp16 roundings
+        rows = 128
+        rb = k // clq.DTYPES[dtype].block_size * clq.DTYPES[dtype].block_bytes
+        ref, mag = oracle.matmul_f64(dtype, x.float().cpu().numpy(), data[:rows * rb], rows)
+        g = got.cpu().numpy()[:, :rows].astype(np.float64)
+        assert max_row_relative_error(g, ref) <= NORM_REL
+        assert np.all(np.abs(g - ref) <= 1e-3 * mag + 1e-6)
         store.close()
 
 
