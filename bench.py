@@ -84,6 +84,8 @@ def parse():
                          "that type and attends over --context cached positions (local/blocks.lisp:327-353)")
     ap.add_argument("--context", type=int, default=1024, help="cached positions attended over (with --attention)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip the named workloads measured after the headline step")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     return ap.parse_args()
@@ -211,12 +213,135 @@ def device_weight(torch, dtype, n, k, seed):
     return raw.reshape(-1)
 
 
+# Named workloads measured after the headline (one GPU: every shape list the
+# benchmark configurations name; several GPUs: the 70B step tensor-parallel).
+# Each is a bounded run: at most 30 timed steps after 3 warm-up steps.
+def config_runs(world):
+    if world > 1:
+        return [(f"c5_llama3_70b_decode_m{m}", dict(model="70b", m=m)) for m in (1, 8)]
+    runs = [("c1_q8_0_4096_m1", dict(workload="q8_0-4096", m=1))]
+    runs += [(f"c2_llama32_1b_q4_m{m}", dict(workload="q4-llama32-1b", m=m)) for m in (1, 4, 16)]
+    runs += [(f"c3_q6k_vocab_qwen3_8b_m{m}", dict(workload="q6k-vocab-qwen3-8b", m=m)) for m in (1, 8, 64)]
+    runs += [(f"c4_llama3_8b_prefill_m{m}", dict(m=m)) for m in (128, 512, 2048)]
+    runs += [(f"c5_llama3_70b_decode_m{m}", dict(model="70b", m=m)) for m in (1, 8)]
+    runs += [("llama3_8b_decode_m8", dict(m=8))]
+    return runs
+
+
 def run_clq(args):
+    import gc
+
     import torch
-    clq = importlib.import_module("cl-inference_b200")
-    tp = importlib.import_module("cl-inference_b200.tp")
     rank, world, local = dist_setup(torch)
     dist = torch.distributed if world > 1 else None
+    result = measure(args, torch, rank, world, local, dist)
+    headline = (args.workload == "step" and args.model == "8b" and args.m == 1 and args.fusions == "off"
+                and args.layers is None and args.xtype is None)
+    if headline and not args.no_configs:
+        subs = {}
+        for name, over in config_runs(world):
+            sub = argparse.Namespace(**vars(args))
+            sub.workload, sub.model = "step", "8b"
+            for key, val in over.items():
+                setattr(sub, key, val)
+            sub.steps, sub.warmup = min(args.steps, 30), max(3, min(args.warmup, 5))
+            sub.no_e2e = sub.no_cpu = True
+            gc.collect()
+            torch.cuda.empty_cache()
+            r = measure(sub, torch, rank, world, local, dist)
+            if rank == 0:
+                subs[name] = summary(r)
+        if rank == 0:
+            result["workloads"] = subs
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def summary(r):
+    """The compact form of a named workload's line."""
+    keep = ("value", "unit", "ms_per_step", "tok_per_s", "tflops", "steps", "gpu_launches_per_step", "check")
+    out = {key: r[key] for key in keep if key in r}
+    out["workload"] = r["config"]["workload"]
+    rf = r.get("roofline") or {}
+    out["roofline"] = {key: rf.get(key) for key in ("bound", "kernel", "achieved", "peak", "unit", "frac",
+                                                    "us_per_launch")}
+    out["clocks"] = {key: r["clocks"].get(key) for key in ("sm_mhz", "reasons")}
+    return out
+
+
+def check_outputs(torch, stores, outs, inputs, m, gemm, world):
+    """Per-run correctness: sampled output columns against float64 products.
+
+    The reference product is x . dequant(W)^T in float64, with dequant(W) from
+    the store's bit-exact dequantize kernel (clq_dequantize_device, the
+    reference's element formulas, bit-checked by the tests), for the first and
+    last 16 rows of each checked linear.  Reported as the maximum over
+    activation rows of ||y - y64|| / ||y64|| (the reference's metric,
+    tests/acceptance/helpers.lisp:153-154) and whether every element meets the
+    per-element bound: 1e-5 + 1e-5 * sum|x*w| for the GEMV
+    (tests/local/packed.lisp:5-12), 1e-3 * sum|x*w| + 1e-6 for the GEMM's fp16
+    operands.  Under tensor parallelism only column-parallel shards are
+    checked (a row-parallel output is a sum over ranks)."""
+    import numpy as np
+    worst, ok, checked = 0.0, True, 0
+    rel_tol, abs_tol = (1e-3, 1e-6) if gemm else (1e-5, 1e-5)
+    picks = range(len(stores))
+    if gemm:  # the first decoder layer and the head: the fp64 products grow with M
+        picks = list(range(min(7, len(stores)))) + [len(stores) - 1]
+    for i in picks:
+        store, s, dtype, kind, src, name = stores[i]
+        if world > 1 and kind != "rows":
+            continue
+        x = inputs[src].float().cpu().numpy().astype(np.float64)
+        for r0 in sorted({0, max(0, s.n - 16)}):
+            cnt = min(16, s.n - r0)
+            w = store.dequantize(r0, cnt).cpu().numpy().astype(np.float64)
+            ref = x @ w.T
+            mag = np.abs(x) @ np.abs(w).T
+            got = outs[i][:, r0:r0 + cnt].cpu().numpy().astype(np.float64)
+            num = np.linalg.norm(got - ref, axis=-1)
+            den = np.maximum(np.linalg.norm(ref, axis=-1), 1e-300)
+            worst = max(worst, float(np.max(num / den)))
+            ok = ok and bool(np.all(np.abs(got - ref) <= abs_tol + rel_tol * mag))
+        checked += 1
+    return {"max_rel_err": worst, "gate": 1e-3, "element_bound": f"{abs_tol:g} + {rel_tol:g}*sum|x*w|",
+            "element_bound_ok": ok, "passed": ok and worst <= 1e-3, "linears_checked": checked,
+            "rows_per_linear": 32,
+            "reference": "float64 x . dequant(W)^T, dequant by the store's bit-exact dequantize kernel"}
+
+
+def config_dict(args, cfg, m, xtype, prefill, world, fuse_mode, job_bytes, n_linears):
+    """The line's "config": the workload by name and sizes (shared by both arms)."""
+    if args.workload == "step":
+        workload = (f"llama3-{args.model}-shape Q4_K-M {'prefill' if prefill else 'decode'} linears, "
+                    f"M={m}, {xtype} activations: {cfg['layers']} layers x (q,k,v,o,gate,up Q4_K; "
+                    f"down Q6_K) + Q6_K output")
+    else:
+        shapes = SWEEPS[args.workload]
+        workload = (f"GEMV sweep {args.workload}: " + ", ".join(f"{d} {n}x{k}" for d, n, k in shapes)
+                    + f"; M={m}, {xtype} activations; {n_linears // len(shapes)} weight copies")
+    return {
+        "workload": workload, "m": m, "xtype": xtype, "layers": cfg["layers"], "parallelism": f"tp{world}",
+        "allreduce": (args.allreduce if world > 1 else None),
+        "fusions": (None if fuse_mode == "off" else
+                    fuse_mode + ": RMSNorm->q/k/v, o+residual, RMSNorm->gate/up, SwiGLU->down+residual, "
+                                "RMSNorm->head"),
+        "attention": (None if fuse_mode == "off" or args.attention == "off" else
+                      f"RoPE q,k; {args.attention} KV cache update; GQA attention over {args.context} "
+                      f"positions ({cfg['heads']} heads / {cfg['kv_heads']} KV heads of {cfg['head_dim']})"),
+        "weights_gb": round(job_bytes / 1e9, 3),
+        "l2": "weights per step far above the 126 MB L2; no flush",
+    }
+
+
+def measure(args, torch, rank, world, local, dist):
+    """One configuration: build this rank's stores, capture the step in a graph,
+    time it, and return the JSON line (rank 0; None elsewhere)."""
+    clq = importlib.import_module("cl-inference_b200")
+    tp = importlib.import_module("cl-inference_b200.tp")
     cfg = dict(tp.LLAMA3_8B if args.model == "8b" else tp.LLAMA3_70B)
     if args.layers:
         cfg["layers"] = args.layers
@@ -431,6 +556,17 @@ def run_clq(args):
         ms = float(t.item())
     gbs = job_bytes / (ms * 1e-3) / 1e9
     peak, peak_kind = peaks()
+    # the outputs of the last timed step, checked against float64 products
+    check = None
+    if fuse_mode == "off":
+        check = check_outputs(torch, stores, outs, inputs, m, prefill, world)
+        if dist is not None:
+            t = torch.tensor([check["max_rel_err"], 0.0 if check["element_bound_ok"] else 1.0],
+                             dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            check["max_rel_err"] = float(t[0].item())
+            check["element_bound_ok"] = bool(t[1].item() == 0.0)
+            check["passed"] = check["element_bound_ok"] and check["max_rel_err"] <= 1e-3
 
     # ---- dominant kernel: the Q4_K GEMV launches alone, back to back ----------
     by_dtype = {}
@@ -479,28 +615,14 @@ def run_clq(args):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic",
-            "config": {
-                "workload": (f"llama3-{args.model}-shape Q4_K-M {'prefill' if prefill else 'decode'} linears, "
-                             f"M={m}, {xtype} activations: {cfg['layers']} layers x (q,k,v,o,gate,up Q4_K; "
-                             f"down Q6_K) + Q6_K output") if args.workload == "step" else
-                            (f"GEMV sweep {args.workload}: " + ", ".join(f"{d} {n}x{k}" for d, n, k in SWEEPS[args.workload])
-                             + f"; M={m}, {xtype} activations; {len(stores) // len(SWEEPS[args.workload])} weight copies"),
-                "m": m, "xtype": xtype, "layers": cfg["layers"], "parallelism": f"tp{world}",
-                "allreduce": (args.allreduce if world > 1 else None),
-                "fusions": (None if fuse_mode == "off" else
-                            fuse_mode + ": RMSNorm->q/k/v, o+residual, RMSNorm->gate/up, SwiGLU->down+residual, "
-                                        "RMSNorm->head"),
-                "attention": (None if fuse_mode == "off" or args.attention == "off" else
-                              f"RoPE q,k; {args.attention} KV cache update; GQA attention over {args.context} "
-                              f"positions ({cfg['heads']} heads / {cfg['kv_heads']} KV heads of {cfg['head_dim']})"),
-                "weights_gb": round(job_bytes / 1e9, 3),
-                "l2": "weights per step far above the 126 MB L2; no flush",
-            },
+            "config": config_dict(args, cfg, m, xtype, prefill, world, fuse_mode, job_bytes, len(stores)),
             "tok_per_s": round(1000.0 * m / ms, 2),
             "hbm_frac": round(gbs / world / peak, 4),
             "gpu_launches": ours_per_step * args.steps if ours_per_step is not None else None,
             "gpu_launches_per_step": {"clq": ours_per_step, "all_kernel_nodes": kernels_per_step},
             "clocks": clock,
+            "check": check,
+            "libraries_mapped": repo_libraries(),
         }
         if prefill:
             tpeak, tpeak_kind = peak_tflops()
@@ -525,9 +647,10 @@ def run_clq(args):
             result["cpu_baseline"] = cpu_baseline(args, tp, cfg, m)
     if dist is not None:
         dist.barrier()
-        dist.destroy_process_group()
-    if result is not None:
-        print(json.dumps(result), flush=True)
+    for entry in stores:
+        entry[0].close()
+    return result
+
 
 
 def e2e_dropin(args, clq, stores, host_copies, m, job_bytes, prefill=False):
@@ -655,26 +778,59 @@ def cpu_baseline(args, tp, cfg, m):
                       f"fp32 CPU port of the packed kernel contract, OpenMP"}
 
 
+def workload_modules():
+    """The package's shape tables (tp) and synthetic weights (synth) without
+    running its __init__, which loads libclq.so: the reference arm maps no
+    code of this library."""
+    import types
+    name = "cl-inference_b200"
+    if name not in sys.modules:
+        pkg = types.ModuleType(name)
+        pkg.__path__ = [str(ROOT / name)]
+        sys.modules[name] = pkg
+    return importlib.import_module(name + ".tp"), importlib.import_module(name + ".synth")
+
+
 def run_reference(args):
-    """The reference arm: the CPU port of cl-inference's packed kernels on the host cores."""
+    """The reference arm: the CPU port of cl-inference's packed kernels
+    (oracle/clq_oracle.c: the six-argument kernel contract of
+    quant/packed.lisp:68-75 and quant/q8-0.lisp:77-85, fp32, OpenMP over every
+    host core) on the same workload as the GPU arm -- every linear of the step,
+    the same shapes and distributions -- timed per step.  Only rank 0 runs."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    tp = importlib.import_module("cl-inference_b200.tp")
+    tp, synth = workload_modules()
     import oracle
-    cfg = tp.LLAMA3_8B if args.model == "8b" else tp.LLAMA3_70B
-    sample, nbytes = cpu_sample(tp, cfg, args.m, args.workload)
+    cfg = dict(tp.LLAMA3_8B if args.model == "8b" else tp.LLAMA3_70B)
+    if args.layers:
+        cfg["layers"] = args.layers
+    m = args.m
+    linears = workload_linears(args, tp, cfg)
+    widths = {}
+    for (_, _, n, k, _, src) in linears:
+        widths.setdefault(src, k)
+    xs = {src: synth.activations(m, k, seed=8100 + i) for i, (src, k) in enumerate(sorted(widths.items()))}
+    work = [(dtype, n, synth.packed_blocks(dtype, n, k, seed=8000 + i), xs[src])
+            for i, (_, dtype, n, k, _, src) in enumerate(linears)]
+    nbytes = float(sum(tp.weight_bytes(d, n, x.shape[1]) + 4 * m * x.shape[1] + 4 * m * n for d, n, _, x in work))
     threads = host_threads()
-    for _ in range(args.warmup):
-        for dtype, n, k, data, x in sample[:1]:
+
+    def step():
+        for dtype, n, data, x in work:
             oracle.matmul_f32(dtype, x, data, n, threads)
+
+    warm0 = time.perf_counter()
+    for _ in range(args.warmup):  # page-in and thread start-up
+        step()
+        if time.perf_counter() - warm0 > 60:
+            break
     times = []
     for _ in range(args.steps):
         t0 = time.perf_counter()
-        for dtype, n, k, data, x in sample:
-            oracle.matmul_f32(dtype, x, data, n, threads)
+        step()
         times.append(time.perf_counter() - t0)
-        if sum(times) > 120:
+        if sum(times) > 90:  # a bounded sample of the K steps asked for
             break
     sec = sum(times) / len(times)
     gbs = nbytes / sec / 1e9
@@ -683,16 +839,27 @@ def run_reference(args):
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": len(times), "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": (f"llama3-{args.model}-shape Q4_K-M decode linears, M={args.m}"
-                                if args.workload == "step" else f"GEMV sweep {args.workload}, M={args.m}")
-                               + f"; each step {sample_name(args.workload)} (bounded sample)", "m": args.m},
+        "config": config_dict(args, cfg, m, "f32", False, 1, "off", nbytes, len(work)),
+        "tok_per_s": round(m / sec, 4),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-                         "sample": f"{sample_name(args.workload)} ({nbytes/1e6:.1f} MB) per step"},
+                         "sample": f"the whole step ({nbytes / 1e9:.3f} GB of packed weights, {len(work)} linears) "
+                                   f"per step, {len(times)} of the {args.steps} steps asked for (90 s cap)"},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "cl-inference's CPU kernels (trivial-simd, Common Lisp host) cannot be built here; "
-                "this is the C port of their contract (oracle/clq_oracle.c)",
+                "this is the C port of their contract (oracle/clq_oracle.c) on the host cores",
+        "libraries_mapped": repo_libraries(),
     }
     print(json.dumps(line), flush=True)
+
+
+def repo_libraries():
+    """This repository's shared libraries mapped into the process."""
+    try:
+        with open("/proc/self/maps") as f:
+            paths = {ln.split()[-1] for ln in f if ln.rstrip().endswith(".so")}
+    except OSError:
+        return None
+    return sorted(os.path.relpath(p, ROOT) for p in paths if p.startswith(str(ROOT) + os.sep))
 
 
 def main():

@@ -11,7 +11,7 @@ The third-party decoder `gguf.quants.dequantize` (llama.cpp's Python package,
 when importable) is run over the same bytes as an independent cross-check and
 its agreement is recorded in the fixture.
 
-Usage: python tests/golden/make_golden.py [/path/to/cl-inference]
+Usage: python tests/golden/make_golden.py /path/to/cl-inference
 Only this script reads the reference checkout; tests read the JSON it writes.
 """
 import json
@@ -23,7 +23,6 @@ import sys
 import numpy as np
 
 HERE = pathlib.Path(__file__).resolve().parent
-DEFAULT_REFERENCE = pathlib.Path("/root/reference")
 
 
 def lisp_float(token):
@@ -74,7 +73,9 @@ def gguf_cross_check(dtype, raw, values):
 
 
 def main():
-    root = pathlib.Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REFERENCE
+    if len(sys.argv) != 2:
+        raise SystemExit(f"usage: python {sys.argv[0]} /path/to/cl-inference")
+    root = pathlib.Path(sys.argv[1])
     packed = parse_packed_goldens((root / "tests/local/quant-golden.lisp").read_text())
     raw8, values8 = q8_golden()
     fixtures = {"q8_0": (raw8, values8), **packed}

@@ -11,7 +11,7 @@ tests/local/cache.lisp:
   * q8-cache-rejects-nonfinite-values-and-invalid-options: +inf and NaN rows.
 Values are written as decimal floats; the extrema as the names the test uses.
 
-Usage: python tests/golden/make_kv_golden.py [/path/to/cl-inference]
+Usage: python tests/golden/make_kv_golden.py /path/to/cl-inference
 Only this script reads the reference checkout; tests read the JSON it writes.
 """
 import json
@@ -20,7 +20,6 @@ import re
 import sys
 
 HERE = pathlib.Path(__file__).resolve().parent
-DEFAULT_REFERENCE = pathlib.Path("/root/reference")
 
 
 def lisp_number(token):
@@ -64,7 +63,9 @@ def parse(text):
 
 
 def main():
-    root = pathlib.Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REFERENCE
+    if len(sys.argv) != 2:
+        raise SystemExit(f"usage: python {sys.argv[0]} /path/to/cl-inference")
+    root = pathlib.Path(sys.argv[1])
     text = (root / "tests" / "local" / "cache.lisp").read_text()
     out = parse(text)
     (HERE / "kv_golden.json").write_text(json.dumps(out, indent=1) + "\n")

@@ -1,5 +1,6 @@
 """bench.py's reference arm prints the one JSON line the driver reads (no GPU
-needed: it times the CPU restatement of the path on the host's cores)."""
+needed: it times the CPU restatement of the path on the host's cores, one
+decoder layer plus the head here to keep the test short)."""
 import json
 import pathlib
 import subprocess
@@ -9,7 +10,8 @@ ROOT = pathlib.Path(__file__).resolve().parents[1]
 
 
 def test_reference_arm_prints_the_contract_line():
-    proc = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "2", "--warmup", "3"],
+    proc = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "2", "--warmup", "3",
+                           "--layers", "1"],
                           capture_output=True, text=True, timeout=600, cwd=ROOT)
     assert proc.returncode == 0, proc.stderr[-2000:]
     lines = [ln for ln in proc.stdout.splitlines() if ln.startswith("{")]
@@ -25,3 +27,5 @@ def test_reference_arm_prints_the_contract_line():
     assert d["e2e"]["value"] == d["value"] and d["e2e"]["unit"] == d["unit"]
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert "workload" in d["config"]
+    # the arm runs the CPU port only: the CUDA library is never mapped
+    assert d["libraries_mapped"] == ["oracle/libclq_oracle.so"], d["libraries_mapped"]

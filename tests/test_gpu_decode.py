@@ -4,9 +4,10 @@ These shapes run the per-warp streaming GEMV: every warp copies its own
 (16-row, 256-column) units with a tensor-map box and the tile partials meet
 through a per-tile count in shared memory.  Where the activations of all of K
 do not fit in a CTA's shared memory (several rows, long rows) K is split
-between CTAs whose partials meet through a global per-tile count, added in
-split order: results are still the same bits on every call, also when calls
-of other shapes run in between.  Cases cover ragged row counts
+between the CTAs of a thread-block cluster, each of which reads the others'
+tile sums through distributed shared memory and adds them in split order:
+results are still the same bits on every call, also when calls of other
+shapes run in between.  Cases cover ragged row counts
 (boxes that run past the last row read zeros), row views written into a wider
 output, K from one superblock to a 14336-wide down projection, the three
 activation types, an activation pointer off the 16-byte grid, and activations
