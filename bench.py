@@ -83,6 +83,9 @@ def parse():
                     help="with --fusions: each layer also runs RoPE on q and k, stores k and v in a KV cache of "
                          "that type and attends over --context cached positions (local/blocks.lisp:327-353)")
     ap.add_argument("--context", type=int, default=1024, help="cached positions attended over (with --attention)")
+    ap.add_argument("--weights", choices=["auto", "quantized", "uniform"], default="auto",
+                    help="quantized: N(0, 0.02) weights quantized to Q4_K / Q6_K on the device; uniform: uniform "
+                         "codes and random scales; auto: quantized for decoder steps, uniform for GEMV sweeps")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-configs", action="store_true",
                     help="skip the named workloads measured after the headline step")
@@ -228,6 +231,33 @@ def config_runs(world):
     return runs
 
 
+def weights_kind(args):
+    """The decoder steps use N(0, 0.02) weights quantized to Q4_K / Q6_K (the
+    prefill and 70B configurations' recipe); the GEMV sweeps the uniform codes
+    their configurations name."""
+    if args.weights != "auto":
+        return args.weights
+    return "quantized" if args.workload == "step" else "uniform"
+
+
+def device_quantized_weight(torch, dtype, n, k, seed):
+    """N(0, 0.02) weights drawn and quantized on the device (synth.py's
+    quantizers, the torch form), in row chunks to bound the temporaries."""
+    synth = importlib.import_module("cl-inference_b200.synth")
+    quant = {"q4_k": synth.quantize_q4_k_torch, "q6_k": synth.quantize_q6_k_torch}.get(dtype)
+    if quant is None:
+        return device_weight(torch, dtype, n, k, seed)
+    g = torch.Generator(device="cuda")
+    g.manual_seed(seed)
+    parts, step = [], max(1, (1 << 26) // k)
+    for r0 in range(0, n, step):
+        rows = min(step, n - r0)
+        w = torch.randn(rows, k, device="cuda", generator=g) * 0.02
+        parts.append(quant(w))
+        del w
+    return torch.cat(parts)
+
+
 def run_clq(args):
     import gc
 
@@ -359,7 +389,10 @@ def measure(args, torch, rank, world, local, dist):
     keep_host = world == 1 and not args.no_e2e
     for i, (name, dtype, n, k, kind, src) in enumerate(linears):
         s = tp.plan(dtype, n, k, kind, rank, world)
-        data = device_weight(torch, dtype, s.n, s.k, seed=4000 + 97 * i + rank)
+        if weights_kind(args) == "quantized":
+            data = device_quantized_weight(torch, dtype, s.n, s.k, seed=4000 + 97 * i + rank)
+        else:
+            data = device_weight(torch, dtype, s.n, s.k, seed=4000 + 97 * i + rank)
         stores.append((clq.Store(dtype, s.n, s.k, data), s, dtype, kind, src, name))
         if keep_host:
             host_copies.append(data.cpu().numpy())
@@ -614,7 +647,9 @@ def measure(args, torch, rank, world, local, dist):
             "metric": METRIC, "value": round(gbs, 1), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic",
+            "data": ("synthetic: N(0, 0.02) weights quantized to Q4_K / Q6_K on the device (synth.py), N(0,1) "
+                     "activations" if weights_kind(args) == "quantized" else
+                     "synthetic: uniform codes, |N(0,1)|-scaled fp16 scales, N(0,1) activations"),
             "config": config_dict(args, cfg, m, xtype, prefill, world, fuse_mode, job_bytes, len(stores)),
             "tok_per_s": round(1000.0 * m / ms, 2),
             "hbm_frac": round(gbs / world / peak, 4),
@@ -838,7 +873,8 @@ def run_reference(args):
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": len(times), "warmup": args.warmup,
         "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: uniform codes and random fp16 scales (the CPU kernel's time does not depend on the values)",
         "config": config_dict(args, cfg, m, "f32", False, 1, "off", nbytes, len(work)),
         "tok_per_s": round(m / sec, 4),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",

@@ -798,11 +798,11 @@ extern "C" int clq_linear_device_noalloc(const clq_store* w, int64_t row_begin, 
     if ((rc = current_device(&device))) return rc;
     if (device != w->device)
         return fail(CLQ_ERR_ARGUMENT, "store lives on device %d, current device is %d", w->device, device);
-    const clq::GemmPlan g = clq::plan_gemm_tc_capped(rows, w->k, m, CLQ_NOALLOC_SCRATCH_BYTES);
+    const clq::GemmPlan g = clq::plan_gemm_tc_capped(w->dtype, rows, w->k, m, CLQ_NOALLOC_SCRATCH_BYTES);
     if (g.splits == 0)
         return fail(CLQ_ERR_SHAPE,
                     "%lld activation rows x %lld columns need %zu bytes of staging; the fixed buffer holds %u",
-                    (long long)m, (long long)w->k, clq::gemm_tc_scratch_bytes(clq::plan_gemm_tc_capped(rows, w->k, m, (size_t)-1)),
+                    (long long)m, (long long)w->k, clq::gemm_tc_scratch_bytes(clq::plan_gemm_tc_capped(w->dtype, rows, w->k, m, (size_t)-1)),
                     (unsigned)CLQ_NOALLOC_SCRATCH_BYTES);
     uint8_t* scratch = nullptr;
     if ((rc = noalloc_scratch(device, &scratch))) return rc;

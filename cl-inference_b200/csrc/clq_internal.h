@@ -119,17 +119,21 @@ cudaError_t launch_gemv_mma_group(const WeightView* const* w, const int64_t* row
 // Tensor-core (tcgen05) prefill GEMM: tiling and scratch layout for one call.
 struct GemmPlan {
     int tn;                // tokens per tile
+    int row_tile;          // weight rows per CTA: 128, or 256 (the Q4_K kernel)
     int64_t token_tiles, row_tiles;
     int splits;            // K splits (partials reduced in a second kernel)
     int kb_per_split;      // 64-wide K blocks per split
     size_t xs_bytes, us_bytes, part_bytes;
     size_t smem;           // dynamic shared memory per CTA
 };
-GemmPlan plan_gemm_tc(int64_t rows, int64_t k, int64_t m);
+// DTYPE picks the kernel: Q4_K weights of at least 256 rows take the one with
+// 256-row tiles and tensor-map staged packed bytes (any multiple of 16 tokens
+// per tile, chosen to fill whole waves).
+GemmPlan plan_gemm_tc(int dtype, int64_t rows, int64_t k, int64_t m);
 size_t gemm_tc_scratch_bytes(const GemmPlan& g);
 // plan_gemm_tc with fewer K splits until the scratch fits in CAP bytes;
 // splits = 0 when it cannot fit.
-GemmPlan plan_gemm_tc_capped(int64_t rows, int64_t k, int64_t m, size_t cap);
+GemmPlan plan_gemm_tc_capped(int dtype, int64_t rows, int64_t k, int64_t m, size_t cap);
 bool gemm_tc_supported(const WeightView& w, int64_t m);
 // SCRATCH: gemm_tc_scratch_bytes(g) device bytes, 256-byte aligned, private to
 // this call until it completes on STREAM.

@@ -17,12 +17,17 @@
 // Every mbarrier wait is bounded; on expiry the CTA records CLQ_ERR_TIMEOUT in
 // the library's device status word (read by clq_device_status), stops
 // issuing, drains what it issued and frees its tensor memory.
+#include <algorithm>
+#include <cstdlib>
+
+#include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
 #include "../../include/clq.h"
 #include "clq_internal.h"
 #include "layout.cuh"
+#include "tma_host.h"
 
 namespace clq {
 namespace {
@@ -116,9 +121,6 @@ __host__ __device__ __forceinline__ uint32_t swz(uint32_t r, uint32_t c) { retur
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
-}
-__device__ __forceinline__ float nibf(uint32_t v) {  // small non-negative integer -> float, exact
-    return __uint_as_float(0x4B000000u | v) - 8388608.f;
 }
 
 // ---- activation prep ------------------------------------------------------
@@ -222,7 +224,6 @@ constexpr uint32_t kMagic = 0x64646464u;
 constexpr uint32_t kH1024 = 0x64006400u;
 constexpr uint32_t kH1056 = 0x64206420u;  // 1024 + 32
 constexpr uint32_t kHSixteenth = 0x2C002C00u;
-constexpr uint32_t kHNeg96 = 0xD600D600u;
 constexpr uint32_t kHNeg1024 = 0xE400E400u;
 constexpr uint32_t kHNeg64 = 0xD400D400u;
 constexpr uint32_t kLoNib = 0x640F640Fu;
@@ -515,6 +516,229 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
     }
 }
 
+// ---- Q4_K prefill GEMM: 256-row tiles, packed bytes staged by TMA ------------
+//
+// The Q4_K form of the GEMM above for weights of at least 256 rows.  One CTA
+// computes 256 weight rows x TN tokens as two 128-row MMAs into two tensor-
+// memory accumulators that read the same activation stage, so every
+// activation byte staged from L2 serves twice the products of a 128-row tile.
+// The packed bytes of each 64-wide K block are staged by a copy warp with two
+// tensor-map boxes of 256 rows (this GPU's own store, no multicast): the
+// superblock headers (16 bytes a row: d, dmin, the 12 scale bytes) and the
+// block's 32 code bytes a row.  Sixteen converting warps (two threads a row)
+// dequantize from shared memory into the two swizzled A halves.  A, B and the
+// packed boxes each have their own ring:
+//   warps 0-15  convert; later the epilogue (warp w: TMEM lanes 32 (w % 4)..,
+//               accumulator (w / 8), half of its columns by (w / 4) % 2)
+//   warp 16     bulk-copies the activation stages (B)
+//   warp 17     one thread issues the MMAs, committing each stage back
+//   warp 18     tensor-map copies of the packed boxes
+constexpr int kRT = 256;                     // weight rows per CTA
+constexpr int kTConv = 16;                   // converting warps
+constexpr int kTThreads = (kTConv + 3) * 32;
+constexpr int kTMaxStages = 4, kTPD = 4;     // A / B ring depths at most; packed ring depth
+constexpr uint32_t kPackHdr = kRT * 16, kPackCodes = kRT * 32, kPackStage = kPackHdr + kPackCodes;
+
+struct GemmTmaParams {
+    CUtensorMap hmap;  // q plane as [rows][nb * 144] bytes, box 16 x 256 (headers)
+    CUtensorMap cmap;  // the same plane, box 32 x 256 (one block's codes)
+    int64_t rows, k, m;
+    const uint8_t* xs;
+    const float* us;
+    float* out;
+    int64_t ldo;
+    int tn;            // tokens per tile: a multiple of 16, at most 256
+    int na, nbs;       // A and B ring depths
+    int kb_per_split;
+    int* err;
+};
+
+__device__ __forceinline__ void tma_box(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// Bounded wait that spins without sleeping (stages are a few hundred cycles).
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, int* err) {
+    for (uint32_t i = 0; i < kWaitLimit; i++) {
+        if (mbar_test(bar, parity)) return true;
+        if ((i & 1023) == 1023 && *(volatile int*)err) return false;
+    }
+    atomicExch(err, CLQ_ERR_TIMEOUT);
+    return false;
+}
+
+__global__ void __launch_bounds__(kTThreads, 1) gemm_q4k_tma_kernel(const __grid_constant__ GemmTmaParams P) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    const int tn = P.tn, NA = P.na, NB = P.nbs;
+    const uint32_t a_stage = 2u * kTM * 128, b_stage = (uint32_t)tn * 128;
+    uint8_t* A = smem;                                // NA x 32 KB (two 128-row halves)
+    uint8_t* B = A + (size_t)NA * a_stage;            // NB x tn * 128
+    uint8_t* Pk = B + (size_t)NB * b_stage;           // kTPD x (headers, codes)
+    Pk = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(Pk) + 127) & ~(uintptr_t)127);
+    uint64_t* full_a = reinterpret_cast<uint64_t*>(Pk + kTPD * kPackStage);
+    uint64_t* empty_a = full_a + kTMaxStages;
+    uint64_t* full_b = empty_a + kTMaxStages;
+    uint64_t* empty_b = full_b + kTMaxStages;
+    uint64_t* full_p = empty_b + kTMaxStages;
+    uint64_t* empty_p = full_p + kTPD;
+    uint64_t* done = empty_p + kTPD;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t tt = blockIdx.x;
+    const int64_t row0 = (int64_t)blockIdx.y * kRT;
+    const int split = blockIdx.z;
+    const int64_t kbt = P.k / kKB;
+    const int64_t kb0 = (int64_t)split * P.kb_per_split;
+    const int64_t kb1 = (kb0 + P.kb_per_split) < kbt ? (kb0 + P.kb_per_split) : kbt;
+    const int nk = (int)(kb1 - kb0);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NA; s++) {
+            mbar_init(&full_a[s], kTConv);
+            mbar_init(&empty_a[s], 1);
+        }
+        for (int s = 0; s < NB; s++) {
+            mbar_init(&full_b[s], 1);
+            mbar_init(&empty_b[s], 1);
+        }
+        for (int s = 0; s < kTPD; s++) {
+            mbar_init(&full_p[s], 1);
+            mbar_init(&empty_p[s], kTConv);
+        }
+        mbar_init(done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {  // two accumulators of up to 256 fp32 columns
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(512)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    int* err = P.err;
+
+    if (warp < kTConv) {
+        // ---- convert: thread i takes half (i / 256) of row (i % 256) ----
+        const uint32_t row = (uint32_t)(threadIdx.x & 255);
+        const int hv = threadIdx.x >> 8;
+        const uint32_t half_row = row & 127;
+        uint8_t* a_half = A + (row >> 7) * (kTM * 128);
+        const Planes none{};
+        for (int it = 0; it < nk; it++) {
+            const int ps = it % kTPD;
+            if (!mbar_wait_spin(&full_p[ps], (uint32_t)(it / kTPD) & 1u, err)) break;
+            const int sa = it % NA;
+            if (it >= NA && !mbar_wait_spin(&empty_a[sa], (uint32_t)((it / NA) - 1) & 1u, err)) break;
+            const uint8_t* pk = Pk + ps * kPackStage;
+            Raw<kQ4_K> rw;
+            rw.hd = *reinterpret_cast<const uint4*>(pk + row * 16);
+            rw.cw = *reinterpret_cast<const uint4*>(pk + kPackHdr + row * 32 + 16 * hv);
+            convert_raw<kQ4_K>(none, 0, kb0 + it, hv, rw, half_row, a_half + sa * a_stage);
+            fence_async_shared();
+            __syncwarp();
+            if (lane == 0) {
+                mbar_arrive(&full_a[sa]);
+                mbar_arrive(&empty_p[ps]);
+            }
+        }
+        // ---- epilogue: tensor memory -> out ----
+        const bool fin = mbar_wait(done, 0, err);
+        tc_fence_after();
+        if (fin) {
+            const int lq = warp & 3, acc = warp >> 3, ch = (warp >> 2) & 1;
+            const int64_t r = row0 + acc * kTM + 32 * lq + lane;
+            const uint32_t taddr = tmem + ((uint32_t)(32 * lq) << 16) + (uint32_t)(acc * 256);
+            const int cbeg = ch * (tn / 2), cend = cbeg + tn / 2;
+            for (int c0 = cbeg; c0 < cend; c0 += 8) {
+                uint32_t v[8];
+                asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                             : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+                               "=r"(v[7])
+                             : "r"(taddr + (uint32_t)c0));
+                asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+                if (r < P.rows) {
+#pragma unroll
+                    for (int j = 0; j < 8; j++) {
+                        const int64_t t = tt * tn + c0 + j;
+                        if (t < P.m) {
+                            const float val = __uint_as_float(v[j]) * P.us[t];
+                            if (gridDim.z == 1) P.out[t * P.ldo + r] = val;
+                            else P.out[((int64_t)split * P.m + t) * P.rows + r] = val;
+                        }
+                    }
+                }
+            }
+        }
+    } else if (warp == kTConv) {
+        // ---- activation stages: one bulk copy each ----
+        if (lane == 0) {
+            int it = 0;
+            for (; it < nk; it++) {
+                const int s = it % NB;
+                if (it >= NB && !mbar_wait(&empty_b[s], (uint32_t)((it / NB) - 1) & 1u, err)) break;
+                mbar_arrive_tx(&full_b[s], b_stage);
+                bulk_copy(B + (size_t)s * b_stage, P.xs + ((tt * kbt + kb0 + it) * tn) * 128, b_stage, &full_b[s]);
+            }
+            // copies in flight land before the CTA exits
+            for (int v = it - NB < 0 ? 0 : it - NB; v < it; v++) mbar_drain(&full_b[v % NB], (uint32_t)(v / NB) & 1u);
+        }
+    } else if (warp == kTConv + 1) {
+        // ---- MMA issue: both 128-row halves against the same activation stage ----
+        if (lane == 0) {
+            const uint32_t idesc = instr_desc(tn);
+            for (int it = 0; it < nk; it++) {
+                const int sa = it % NA, sbs = it % NB;
+                if (!mbar_wait_spin(&full_a[sa], (uint32_t)(it / NA) & 1u, err) ||
+                    !mbar_wait_spin(&full_b[sbs], (uint32_t)(it / NB) & 1u, err))
+                    break;
+                tc_fence_after();
+                const uint32_t a_addr = smem_u32(A + (size_t)sa * a_stage), b_addr = smem_u32(B + (size_t)sbs * b_stage);
+#pragma unroll
+                for (int h = 0; h < 2; h++)
+#pragma unroll
+                    for (int kk = 0; kk < kKB / 16; kk++)
+                        mma_f16(tmem + (uint32_t)(h * 256), smem_desc(a_addr + h * (kTM * 128) + 32 * kk),
+                                smem_desc(b_addr + 32 * kk), idesc, (it > 0 || kk > 0) ? 1u : 0u);
+                mma_commit(&empty_a[sa]);
+                mma_commit(&empty_b[sbs]);
+            }
+            mma_commit(done);  // arrives once every MMA issued above has completed
+            mbar_drain(done, 0);
+        }
+    } else {
+        // ---- packed boxes: the block's superblock headers and codes ----
+        if (lane == 0) {
+            int it = 0;
+            for (; it < nk; it++) {
+                const int ps = it % kTPD;
+                if (it >= kTPD && !mbar_wait(&empty_p[ps], (uint32_t)((it / kTPD) - 1) & 1u, err)) break;
+                const int64_t kb = kb0 + it;
+                mbar_arrive_tx(&full_p[ps], kPackStage);
+                uint8_t* dst = Pk + ps * kPackStage;
+                tma_box(dst, &P.hmap, (int)((kb >> 2) * 144), (int)row0, &full_p[ps]);
+                tma_box(dst + kPackHdr, &P.cmap, (int)((kb >> 2) * 144 + 16 + 32 * (kb & 3)), (int)row0, &full_p[ps]);
+            }
+            for (int v = it - kTPD < 0 ? 0 : it - kTPD; v < it; v++)
+                mbar_drain(&full_p[v % kTPD], (uint32_t)(v / kTPD) & 1u);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+    }
+}
+
 // out[t * ldo + r] = sum over splits of part[split][t][r], fixed order.
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t m, int64_t rows,
                                      float* __restrict__ out, int64_t ldo) {
@@ -525,6 +749,17 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
         const int64_t t = i / rows, r = i % rows;
         out[t * ldo + r] = s;
     }
+}
+
+// The 256-row, tensor-map staged kernel for Q4_K (CLQ_GEMM_TMA=0, a tuning
+// knob, keeps the register-fed one).
+bool gemm_tma_enabled() {
+    static int on = -1;
+    if (on < 0) {
+        const char* e = getenv("CLQ_GEMM_TMA");
+        on = (e && e[0] == '0') ? 0 : 1;
+    }
+    return on == 1;
 }
 
 int sm_count_gemm() {
@@ -540,30 +775,92 @@ int sm_count_gemm() {
 
 }  // namespace
 
-GemmPlan plan_gemm_tc(int64_t rows, int64_t k, int64_t m) {
-    GemmPlan g;
-    int tn = 32;
-    while (tn < 256 && tn < m) tn *= 2;
-    g.tn = tn;
-    g.token_tiles = (m + tn - 1) / tn;
-    g.row_tiles = (rows + kTM - 1) / kTM;
-    const int64_t kbt = k / kKB;
-    const int64_t ctas = g.token_tiles * g.row_tiles;
+namespace {
+bool takes_tma(int dtype, int64_t rows) { return gemm_tma_enabled() && rows >= kRT && dtype == kQ4_K; }
+
+// Shared memory of the Q4_K kernel and its ring depths: B as deep as fits
+// (at least two), then A (at least two).
+size_t tma_smem(int tn, int* na, int* nb) {
+    const size_t fixed = 1024 + 128 + (size_t)kTPD * kPackStage + 512, b_stage = (size_t)tn * 128;
+    const size_t a_stage = 2 * (size_t)kTM * 128, limit = 227 * 1024;
+    for (int b = kTMaxStages; b >= 2; b--)
+        for (int a = 3; a >= 2; a--) {
+            const size_t total = fixed + (size_t)a * a_stage + (size_t)b * b_stage;
+            if (total <= limit) {
+                *na = a;
+                *nb = b;
+                return total;
+            }
+        }
+    *na = *nb = 2;
+    return fixed + 2 * a_stage + 2 * b_stage;
+}
+
+int split_count(int64_t ctas, int64_t kbt) {
     int64_t splits = 1;
     const int64_t want = sm_count_gemm();
     while (ctas * splits < want && kbt / (splits * 2) >= 4) splits *= 2;
     while (splits > 1 && kbt % splits) splits /= 2;  // every split gets the same, non-zero K range
-    g.splits = (int)splits;
-    g.kb_per_split = (int)((kbt + splits - 1) / splits);
-    g.xs_bytes = (size_t)g.token_tiles * tn * k * 2;
-    g.us_bytes = (size_t)g.token_tiles * tn * sizeof(float);
-    g.part_bytes = splits > 1 ? (size_t)splits * m * rows * sizeof(float) : 0;
-    g.smem = 1024 + (size_t)kStages * (kTM * 128 + tn * 128) + 256;
+    return (int)splits;
+}
+
+// Tuning knob: CLQ_GEMM_TN fixes the Q4_K kernel's tokens per tile (a
+// multiple of 16 up to 256); by default the plan picks it.
+int env_tn() {
+    static int v = -2;
+    if (v == -2) {
+        const char* e = getenv("CLQ_GEMM_TN");
+        v = e ? atoi(e) : -1;
+        if (v != -1 && (v < 16 || v > 256 || v % 16)) v = -1;
+    }
+    return v;
+}
+}  // namespace
+
+GemmPlan plan_gemm_tc(int dtype, int64_t rows, int64_t k, int64_t m) {
+    GemmPlan g;
+    const int64_t kbt = k / kKB;
+    if (takes_tma(dtype, rows)) {
+        // 256-row tiles; tokens per tile chosen so the tiles fill whole waves:
+        // a tile costs max(4 tn, 900) cycles per 64-wide K block (its MMAs,
+        // or the dequantization of 256 rows), a wave costs its slowest tile
+        g.row_tile = kRT;
+        g.row_tiles = (rows + kRT - 1) / kRT;
+        const int64_t sms = sm_count_gemm();
+        int best_tn = 256;
+        double best = 1e300;
+        for (int tn = 256; tn >= 32; tn -= 16) {
+            if (env_tn() > 0 && tn != env_tn()) continue;
+            if (tn < 256 && (tn - 16) >= m) continue;  // a smaller tile than the tokens need
+            const int64_t tiles = (m + tn - 1) / tn * g.row_tiles;
+            const int sp = split_count(tiles, kbt);
+            const double waves = (double)((tiles * sp + sms - 1) / sms);
+            const double cost = waves * (4.0 * tn > 900.0 ? 4.0 * tn : 900.0) / sp;
+            if (cost < best * 0.999) {
+                best = cost;
+                best_tn = tn;
+            }
+        }
+        g.tn = best_tn;
+    } else {
+        g.row_tile = kTM;
+        g.row_tiles = (rows + kTM - 1) / kTM;
+        int tn = 32;
+        while (tn < 256 && tn < m) tn *= 2;
+        g.tn = tn;
+    }
+    g.token_tiles = (m + g.tn - 1) / g.tn;
+    g.splits = split_count(g.token_tiles * g.row_tiles, kbt);
+    g.kb_per_split = (int)((kbt + g.splits - 1) / g.splits);
+    g.xs_bytes = (size_t)g.token_tiles * g.tn * k * 2;
+    g.us_bytes = (size_t)g.token_tiles * g.tn * sizeof(float);
+    g.part_bytes = g.splits > 1 ? (size_t)g.splits * m * rows * sizeof(float) : 0;
+    g.smem = 1024 + (size_t)kStages * (kTM * 128 + g.tn * 128) + 256;
     return g;
 }
 
-GemmPlan plan_gemm_tc_capped(int64_t rows, int64_t k, int64_t m, size_t cap) {
-    GemmPlan g = plan_gemm_tc(rows, k, m);
+GemmPlan plan_gemm_tc_capped(int dtype, int64_t rows, int64_t k, int64_t m, size_t cap) {
+    GemmPlan g = plan_gemm_tc(dtype, rows, k, m);
     while (g.splits > 1 && gemm_tc_scratch_bytes(g) > cap) {
         g.splits /= 2;
         const int64_t kbt = k / kKB;
@@ -620,12 +917,37 @@ cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int
         kern<<<grid, kThreads, g.smem, stream>>>(P);
         return cudaGetLastError();
     };
-    switch (w.dtype) {
-    case kQ4_K: e = launch(gemm_tc_kernel<kQ4_K>); break;
-    case kQ6_K: e = launch(gemm_tc_kernel<kQ6_K>); break;
-    case kQ4_0: e = launch(gemm_tc_kernel<kQ4_0>); break;
-    case kQ8_0: e = launch(gemm_tc_kernel<kQ8_0>); break;
-    default: return cudaErrorInvalidValue;
+    // Q4_K of at least 256 rows: 256-row tiles with tensor-map staged packed bytes
+    if (g.row_tile == kRT) {
+        if (w.dtype != kQ4_K || rows < kRT) return cudaErrorInvalidValue;  // a plan made for another weight
+        GemmTmaParams T;
+        const int64_t row_bytes = w.nb * 144;
+        if (!encode_rows(&T.hmap, w.q, rows, row_bytes, 16, kRT) || !encode_rows(&T.cmap, w.q, rows, row_bytes, 32, kRT))
+            return cudaErrorNotSupported;
+        T.rows = rows;
+        T.k = w.k;
+        T.m = m;
+        T.xs = xs;
+        T.us = us;
+        T.out = P.out;
+        T.ldo = ldo;
+        T.tn = g.tn;
+        T.kb_per_split = g.kb_per_split;
+        T.err = err;
+        const size_t smem = tma_smem(g.tn, &T.na, &T.nbs);
+        e = cudaFuncSetAttribute(gemm_q4k_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        dim3 tgrid((unsigned)g.token_tiles, (unsigned)g.row_tiles, (unsigned)g.splits);
+        gemm_q4k_tma_kernel<<<tgrid, kTThreads, smem, stream>>>(T);
+        e = cudaGetLastError();
+    } else {
+        switch (w.dtype) {
+        case kQ4_K: e = launch(gemm_tc_kernel<kQ4_K>); break;
+        case kQ6_K: e = launch(gemm_tc_kernel<kQ6_K>); break;
+        case kQ4_0: e = launch(gemm_tc_kernel<kQ4_0>); break;
+        case kQ8_0: e = launch(gemm_tc_kernel<kQ8_0>); break;
+        default: return cudaErrorInvalidValue;
+        }
     }
     if (e != cudaSuccess || g.splits == 1) return e;
     const int64_t total = m * rows;

@@ -55,6 +55,7 @@
 #include "gemv_common.cuh"
 #include "gemv_i8.cuh"
 #include "pipeline.cuh"
+#include "tma_host.h"
 
 namespace clq {
 namespace {
@@ -481,32 +482,6 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
     }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-    static std::once_flag once;
-    std::call_once(once, [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-            q == cudaDriverEntryPointSuccess)
-            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    });
-    return fn;
-}
-
-// ROWS rows of ROW_BYTES bytes at BASE, read as boxes of 16 rows x BOX bytes.
-bool encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box) {
-    PFN_cuTensorMapEncodeTiled_v12000 fn = encode_tiled();
-    if (!fn || (uintptr_t)base % 16 || row_bytes % 16 || box % 16) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-    const cuuint32_t boxd[2] = {(cuuint32_t)box, 16u};
-    const cuuint32_t estr[2] = {1u, 1u};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, boxd, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 // Encoded maps, per thread, by (base, rows, row bytes, box): a map is a pure
 // function of these, so an entry never goes stale.  Decode calls one weight at
 // a time, so the per-call encode is the common case to avoid.
@@ -532,7 +507,7 @@ bool cached_encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_
         *map = it->second;
         return true;
     }
-    if (!encode_rows(map, base, rows, row_bytes, box)) return false;
+    if (!encode_rows(map, base, rows, row_bytes, box, 16)) return false;
     if (cache.size() >= 4096) cache.clear();
     cache.emplace(key, *map);
     return true;
@@ -736,6 +711,32 @@ cudaError_t launch_warp_dtype(const WarpParams& P, int dtype, bool fuse, cudaStr
 }
 
 }  // namespace
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_tiled() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+bool encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box, int box_rows) {
+    PFN_cuTensorMapEncodeTiled_v12000 fn = encode_tiled();
+    if (!fn || (uintptr_t)base % 16 || row_bytes % 16 || box % 16 || box > 256 || box_rows < 1 || box_rows > 256)
+        return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t boxd[2] = {(cuuint32_t)box, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1u, 1u};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, boxd, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 
 cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, int count, const void* x, int xtype,
                              int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,

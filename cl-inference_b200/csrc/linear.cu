@@ -54,7 +54,7 @@ bool uses_gemm_tc(const WeightView& w, int xtype, int64_t m, unsigned flags) {
 cudaError_t launch_linear(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
                           float* out, int64_t ldo, unsigned flags, cudaStream_t stream) {
     if (uses_gemm_tc(w, xtype, m, flags)) {
-        const GemmPlan g = plan_gemm_tc(rows, w.k, m);
+        const GemmPlan g = plan_gemm_tc(w.dtype, rows, w.k, m);
         cudaError_t e = keep_pool_memory();
         if (e != cudaSuccess) return e;
         void* scratch = nullptr;
