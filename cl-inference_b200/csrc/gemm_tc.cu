@@ -522,26 +522,26 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
 // computes 256 weight rows x TN tokens as two 128-row MMAs into two tensor-
 // memory accumulators that read the same activation stage, so every
 // activation byte staged from L2 serves twice the products of a 128-row tile.
-// The packed bytes of each 64-wide K block are staged by a copy warp with two
-// tensor-map boxes of 256 rows (this GPU's own store, no multicast): the
-// superblock headers (16 bytes a row: d, dmin, the 12 scale bytes) and the
-// block's 32 code bytes a row.  Sixteen converting warps (two threads a row)
-// dequantize from shared memory into the two swizzled A halves.  A, B and the
-// packed boxes each have their own ring:
+// The packed bytes are staged a superblock column at a time (256 rows x 144
+// bytes, four 64-wide K blocks) by a copy warp with one tensor-map box (this
+// GPU's own store, one destination), two superblocks ahead.  Sixteen
+// converting warps (two threads a row) dequantize from shared memory into
+// the two swizzled A halves.  A, B and the packed superblocks each have their
+// own ring:
 //   warps 0-15  convert; later the epilogue (warp w: TMEM lanes 32 (w % 4)..,
 //               accumulator (w / 8), half of its columns by (w / 4) % 2)
 //   warp 16     bulk-copies the activation stages (B)
 //   warp 17     one thread issues the MMAs, committing each stage back
-//   warp 18     tensor-map copies of the packed boxes
+//   warp 18     tensor-map copies of the packed superblocks
 constexpr int kRT = 256;                     // weight rows per CTA
 constexpr int kTConv = 16;                   // converting warps
 constexpr int kTThreads = (kTConv + 3) * 32;
-constexpr int kTMaxStages = 4, kTPD = 4;     // A / B ring depths at most; packed ring depth
-constexpr uint32_t kPackHdr = kRT * 16, kPackCodes = kRT * 32, kPackStage = kPackHdr + kPackCodes;
+constexpr int kTMaxStages = 4, kTPD = 2;     // A / B ring depths at most; superblocks in flight
+constexpr uint32_t kPackStage = kRT * 144;
 
 struct GemmTmaParams {
-    CUtensorMap hmap;  // q plane as [rows][nb * 144] bytes, box 16 x 256 (headers)
-    CUtensorMap cmap;  // the same plane, box 32 x 256 (one block's codes)
+    CUtensorMap qmap;  // q plane as [rows][nb * 144] bytes, box 144 x 256 (a superblock column)
+    Planes p;          // the register-fed form reads the packed words directly
     int64_t rows, k, m;
     const uint8_t* xs;
     const float* us;
@@ -571,6 +571,10 @@ __device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, i
     return false;
 }
 
+// STAGED: the packed superblocks come through the tensor-map ring; otherwise
+// each converting thread loads its packed words from global memory into
+// registers two blocks ahead (as gemm_tc_kernel's converters do).
+template <bool STAGED>
 __global__ void __launch_bounds__(kTThreads, 1) gemm_q4k_tma_kernel(const __grid_constant__ GemmTmaParams P) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -580,7 +584,7 @@ __global__ void __launch_bounds__(kTThreads, 1) gemm_q4k_tma_kernel(const __grid
     uint8_t* B = A + (size_t)NA * a_stage;            // NB x tn * 128
     uint8_t* Pk = B + (size_t)NB * b_stage;           // kTPD x (headers, codes)
     Pk = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(Pk) + 127) & ~(uintptr_t)127);
-    uint64_t* full_a = reinterpret_cast<uint64_t*>(Pk + kTPD * kPackStage);
+    uint64_t* full_a = reinterpret_cast<uint64_t*>(Pk + (STAGED ? kTPD * kPackStage : 0u));
     uint64_t* empty_a = full_a + kTMaxStages;
     uint64_t* full_b = empty_a + kTMaxStages;
     uint64_t* empty_b = full_b + kTMaxStages;
@@ -633,21 +637,42 @@ __global__ void __launch_bounds__(kTThreads, 1) gemm_q4k_tma_kernel(const __grid
         const uint32_t half_row = row & 127;
         uint8_t* a_half = A + (row >> 7) * (kTM * 128);
         const Planes none{};
-        for (int it = 0; it < nk; it++) {
-            const int ps = it % kTPD;
-            if (!mbar_wait_spin(&full_p[ps], (uint32_t)(it / kTPD) & 1u, err)) break;
+        // the split starts at block kb0: superblock kb0 / 4, quarter kb0 % 4
+        const int q0 = (int)(kb0 & 3);
+        if constexpr (!STAGED) {
+            const int64_t grow_u = row0 + row;
+            const int64_t grow = grow_u < P.rows ? grow_u : P.rows - 1;
+            Raw<kQ4_K> r0, r1, r2;  // blocks it, it + 1, it + 2
+            if (nk > 0) load_raw<kQ4_K>(P.p, grow, kb0, hv, r0);
+            if (nk > 1) load_raw<kQ4_K>(P.p, grow, kb0 + 1, hv, r1);
+            for (int it = 0; it < nk; it++) {
+                if (it + 2 < nk) load_raw<kQ4_K>(P.p, grow, kb0 + it + 2, hv, r2);
+                const int sa = it % NA;
+                if (it >= NA && !mbar_wait_spin(&empty_a[sa], (uint32_t)((it / NA) - 1) & 1u, err)) break;
+                convert_raw<kQ4_K>(none, 0, kb0 + it, hv, r0, half_row, a_half + sa * a_stage);
+                fence_async_shared();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full_a[sa]);
+                r0 = r1;
+                r1 = r2;
+            }
+        }
+        for (int it = 0; STAGED && it < nk; it++) {
+            const int sbi = (q0 + it) >> 2, qt = (q0 + it) & 3;
+            const int ps = sbi % kTPD;
+            if ((qt == 0 || it == 0) && !mbar_wait_spin(&full_p[ps], (uint32_t)(sbi / kTPD) & 1u, err)) break;
             const int sa = it % NA;
             if (it >= NA && !mbar_wait_spin(&empty_a[sa], (uint32_t)((it / NA) - 1) & 1u, err)) break;
-            const uint8_t* pk = Pk + ps * kPackStage;
+            const uint8_t* pk = Pk + ps * kPackStage + row * 144;
             Raw<kQ4_K> rw;
-            rw.hd = *reinterpret_cast<const uint4*>(pk + row * 16);
-            rw.cw = *reinterpret_cast<const uint4*>(pk + kPackHdr + row * 32 + 16 * hv);
+            rw.hd = *reinterpret_cast<const uint4*>(pk);
+            rw.cw = *reinterpret_cast<const uint4*>(pk + 16 + 32 * qt + 16 * hv);
             convert_raw<kQ4_K>(none, 0, kb0 + it, hv, rw, half_row, a_half + sa * a_stage);
             fence_async_shared();
             __syncwarp();
             if (lane == 0) {
                 mbar_arrive(&full_a[sa]);
-                mbar_arrive(&empty_p[ps]);
+                if (qt == 3 || it == nk - 1) mbar_arrive(&empty_p[ps]);  // this warp is done with the superblock
             }
         }
         // ---- epilogue: tensor memory -> out ----
@@ -714,21 +739,18 @@ __global__ void __launch_bounds__(kTThreads, 1) gemm_q4k_tma_kernel(const __grid
             mma_commit(done);  // arrives once every MMA issued above has completed
             mbar_drain(done, 0);
         }
-    } else {
-        // ---- packed boxes: the block's superblock headers and codes ----
+    } else if (STAGED) {
+        // ---- packed superblocks: one tensor-map box each ----
         if (lane == 0) {
-            int it = 0;
-            for (; it < nk; it++) {
-                const int ps = it % kTPD;
-                if (it >= kTPD && !mbar_wait(&empty_p[ps], (uint32_t)((it / kTPD) - 1) & 1u, err)) break;
-                const int64_t kb = kb0 + it;
+            const int nsb = (int)(((kb1 + 3) >> 2) - (kb0 >> 2));
+            int s = 0;
+            for (; s < nsb; s++) {
+                const int ps = s % kTPD;
+                if (s >= kTPD && !mbar_wait(&empty_p[ps], (uint32_t)((s / kTPD) - 1) & 1u, err)) break;
                 mbar_arrive_tx(&full_p[ps], kPackStage);
-                uint8_t* dst = Pk + ps * kPackStage;
-                tma_box(dst, &P.hmap, (int)((kb >> 2) * 144), (int)row0, &full_p[ps]);
-                tma_box(dst + kPackHdr, &P.cmap, (int)((kb >> 2) * 144 + 16 + 32 * (kb & 3)), (int)row0, &full_p[ps]);
+                tma_box(Pk + ps * kPackStage, &P.qmap, (int)(((kb0 >> 2) + s) * 144), (int)row0, &full_p[ps]);
             }
-            for (int v = it - kTPD < 0 ? 0 : it - kTPD; v < it; v++)
-                mbar_drain(&full_p[v % kTPD], (uint32_t)(v / kTPD) & 1u);
+            for (int v = s - kTPD < 0 ? 0 : s - kTPD; v < s; v++) mbar_drain(&full_p[v % kTPD], (uint32_t)(v / kTPD) & 1u);
         }
     }
     tc_fence_before();
@@ -751,16 +773,20 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
     }
 }
 
-// The 256-row, tensor-map staged kernel for Q4_K (CLQ_GEMM_TMA=0, a tuning
-// knob, keeps the register-fed one).
-bool gemm_tma_enabled() {
-    static int on = -1;
-    if (on < 0) {
+// Which kernel takes Q4_K weights of at least 256 rows (CLQ_GEMM_TMA, a
+// tuning knob): 0 the 128-row register-fed gemm_tc_kernel (the default, the
+// fastest measured), 1 the 256-row kernel with tensor-map staged packed
+// superblocks, 2 the 256-row kernel with register-fed packed words.
+int gemm_q4k_mode() {
+    static int mode = -1;
+    if (mode < 0) {
         const char* e = getenv("CLQ_GEMM_TMA");
-        on = (e && e[0] == '0') ? 0 : 1;
+        mode = e ? atoi(e) : 0;
+        if (mode < 0 || mode > 2) mode = 0;
     }
-    return on == 1;
+    return mode;
 }
+bool gemm_tma_enabled() { return gemm_q4k_mode() != 0; }
 
 int sm_count_gemm() {
     static int count = 0;
@@ -780,8 +806,8 @@ bool takes_tma(int dtype, int64_t rows) { return gemm_tma_enabled() && rows >= k
 
 // Shared memory of the Q4_K kernel and its ring depths: B as deep as fits
 // (at least two), then A (at least two).
-size_t tma_smem(int tn, int* na, int* nb) {
-    const size_t fixed = 1024 + 128 + (size_t)kTPD * kPackStage + 512, b_stage = (size_t)tn * 128;
+size_t tma_smem(int tn, bool staged, int* na, int* nb) {
+    const size_t fixed = 1024 + 128 + (staged ? (size_t)kTPD * kPackStage : 0) + 512, b_stage = (size_t)tn * 128;
     const size_t a_stage = 2 * (size_t)kTM * 128, limit = 227 * 1024;
     for (int b = kTMaxStages; b >= 2; b--)
         for (int a = 3; a >= 2; a--) {
@@ -922,8 +948,9 @@ cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int
         if (w.dtype != kQ4_K || rows < kRT) return cudaErrorInvalidValue;  // a plan made for another weight
         GemmTmaParams T;
         const int64_t row_bytes = w.nb * 144;
-        if (!encode_rows(&T.hmap, w.q, rows, row_bytes, 16, kRT) || !encode_rows(&T.cmap, w.q, rows, row_bytes, 32, kRT))
-            return cudaErrorNotSupported;
+        const bool staged = gemm_q4k_mode() == 1;
+        if (staged && !encode_rows(&T.qmap, w.q, rows, row_bytes, 144, kRT)) return cudaErrorNotSupported;
+        T.p = P.p;
         T.rows = rows;
         T.k = w.k;
         T.m = m;
@@ -934,11 +961,12 @@ cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int
         T.tn = g.tn;
         T.kb_per_split = g.kb_per_split;
         T.err = err;
-        const size_t smem = tma_smem(g.tn, &T.na, &T.nbs);
-        e = cudaFuncSetAttribute(gemm_q4k_tma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        const size_t smem = tma_smem(g.tn, staged, &T.na, &T.nbs);
+        auto kern = staged ? gemm_q4k_tma_kernel<true> : gemm_q4k_tma_kernel<false>;
+        e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
         dim3 tgrid((unsigned)g.token_tiles, (unsigned)g.row_tiles, (unsigned)g.splits);
-        gemm_q4k_tma_kernel<<<tgrid, kTThreads, smem, stream>>>(T);
+        kern<<<tgrid, kTThreads, smem, stream>>>(T);
         e = cudaGetLastError();
     } else {
         switch (w.dtype) {

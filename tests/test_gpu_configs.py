@@ -103,3 +103,21 @@ def test_q6k_output_head_batched(cuda, clq, synth, oracle, m, xtype):
     out = store.linear(x).cpu().numpy()
     check_rows(clq, oracle, "q6_k", out, x.float().cpu().numpy(), data, n, k, 256, gemm=xtype != "float32")
     store.close()
+
+
+@pytest.mark.parametrize("dtype,n,k,m", [
+    ("q4_k", 2048, 4096, 512),     # the 256-row Q4_K kernel, a slice of the q/gate rows
+    ("q4_k", 1000, 4096, 300),     # ragged rows and tokens
+    ("q6_k", 1024, 14336, 256),    # the down projection's format
+])
+def test_prefill_on_quantized_normal_weights(cuda, clq, synth, oracle, dtype, n, k, m):
+    """The prefill configuration's weights: N(0, 0.02) quantized to Q4_K /
+    Q6_K.  The GEMM's fp16 operands keep the norm-relative error under 1e-3
+    on them too."""
+    torch = cuda
+    data = getattr(synth, "quantize_" + dtype)(synth.normal_weight(n, k, seed=n + k))
+    x = torch.from_numpy(synth.activations(m, k, seed=m)).cuda().to(torch.bfloat16)
+    store = clq.Store(dtype, n, k, data)
+    out = store.linear(x).cpu().numpy()
+    check_rows(clq, oracle, dtype, out, x.float().cpu().numpy(), data, n, k, 128, gemm=True)
+    store.close()

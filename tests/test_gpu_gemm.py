@@ -94,3 +94,45 @@ def test_gemm_repeats_bit_identically(cuda, clq, synth):
     b = store.linear(x)
     assert torch.equal(a, b)
     store.close()
+
+
+_MODE_CHECK = r"""
+import sys
+sys.path[:0] = [{root!r}, {root!r} + "/oracle", {root!r} + "/tests"]
+import importlib
+import numpy as np
+import torch
+import oracle
+from helpers import NORM_REL, max_row_relative_error
+clq = importlib.import_module("cl-inference_b200")
+synth = importlib.import_module("cl-inference_b200.synth")
+torch.cuda.set_device(0)
+for n, k, m in ((2048, 4096, 512), (1000, 1024, 300), (300, 2048, 96)):
+    data = synth.quantize_q4_k(synth.normal_weight(n, k, seed=n + m))
+    x = torch.from_numpy(synth.activations(m, k, seed=m)).cuda().to(torch.bfloat16)
+    store = clq.Store("q4_k", n, k, data)
+    out = store.linear(x).cpu().numpy().astype(np.float64)
+    rb = k // 256 * 144
+    for start in sorted({{0, n - 128}}):
+        ref, mag = oracle.matmul_f64("q4_k", x.float().cpu().numpy(), data[start * rb:(start + 128) * rb], 128)
+        got = out[:, start:start + 128]
+        assert max_row_relative_error(got, ref) <= NORM_REL, (n, k, m, start)
+        assert np.all(np.abs(got - ref) <= 1e-3 * mag + 1e-6), (n, k, m, start)
+    store.close()
+print("ok")
+"""
+
+
+@pytest.mark.parametrize("mode", ["1", "2"])
+def test_256_row_q4k_kernels(mode):
+    """The 256-row Q4_K kernel in both forms (CLQ_GEMM_TMA=1: packed
+    superblocks staged by tensor-map copies; 2: register-fed), against the
+    fp64 oracle on N(0, 0.02) weights; a fresh process, since the knob is read
+    once per process."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    proc = subprocess.run([sys.executable, "-c", _MODE_CHECK.format(root=root)], capture_output=True, text=True,
+                          timeout=600, env={**os.environ, "CLQ_GEMM_TMA": mode})
+    assert proc.returncode == 0 and proc.stdout.strip().endswith("ok"), proc.stderr[-3000:]
