@@ -574,6 +574,33 @@ bool wplan(WarpParams& P, int64_t groups, int ks, size_t* smem) {
 
 constexpr int kWMaxSplit = 8;
 
+// When to split K across a cluster (CLQ_GEMV_SPLIT, a tuning knob): 0 only
+// when the activations of all of K do not fit one CTA (the default), 1 also
+// when the estimate says it evens out the CTAs' work, 2 always when a split
+// fits.  Measured on the Llama-3-8B decode step, 1 costs more than it saves
+// (1.60 against 1.51 ms; 70B: 10.76 against 10.35 ms): the cluster barriers
+// and cross-CTA sums outweigh the better balance.
+int split_mode() {
+    static int v = -1;
+    if (v < 0) {
+        const char* e = getenv("CLQ_GEMV_SPLIT");
+        v = e ? atoi(e) : 0;
+        if (v < 0 || v > 2) v = 0;
+    }
+    return v;
+}
+// The fixed cost of a split (two cluster barriers, the cross-CTA sums), in
+// units of one 16-row x 256-column weight block (CLQ_GEMV_SPLIT_COST).
+double split_cost() {
+    static double v = -1.0;
+    if (v < 0) {
+        const char* e = getenv("CLQ_GEMV_SPLIT_COST");
+        v = e ? atof(e) : 4.0;
+        if (v < 0) v = 0;
+    }
+    return v;
+}
+
 // Raises the kernel's dynamic shared-memory limit on the current device to
 // SMEM once (per instance and device).
 template <typename Kern>
@@ -641,26 +668,49 @@ cudaError_t launch_warp(WarpParams P, cudaStream_t stream) {
         return cudaErrorNotSupported;
     size_t smem = 0;
     int ks = 1;
-    if (!wplan<D>(P, groups, 1, &smem)) {
-        // the activations of all of K do not fit beside the rings: split K
-        // between the CTAs of a cluster (not under tensor parallelism or a
-        // fused prologue, which need whole rows in one CTA)
-        if (P.tp_on || FUSE) return cudaErrorNotSupported;
-        ks = 0;
-        const int64_t sms = sm_count();
-        for (int k2 = 2; k2 <= kWMaxSplit && k2 <= P.nchunks; k2 *= 2) {
-            groups = sms / k2 < P.tiles ? sms / k2 : P.tiles;
-            if (!wplan<D>(P, groups, k2, &smem)) continue;
-            const int64_t clusters = max_clusters(kern_split, set_for_split, k2, smem);
-            if (clusters < 1) continue;
-            if (clusters < groups) {  // fewer clusters fit than SMs / KS: more tiles each
-                groups = clusters;
-                if (!wplan<D>(P, groups, k2, &smem)) continue;
+    const bool whole = wplan<D>(P, groups, 1, &smem);
+    // Not under tensor parallelism or a fused prologue, which need whole rows
+    // in one CTA: K may be split between the CTAs of a cluster.  That is
+    // needed when the activations of all of K do not fit beside the rings,
+    // and it pays when whole tiles leave the CTAs unevenly loaded -- a CTA's
+    // time is its units (tiles x chunks of its split), and fewer, larger tile
+    // groups split K evenly (256 tiles over 148 CTAs: 2 against 1.73 on
+    // average; over 37 clusters of 4: 7 against 6.9).
+    if (!whole && (P.tp_on || FUSE)) return cudaErrorNotSupported;
+    if (!P.tp_on && !FUSE) {
+        const int mode = split_mode();
+        auto units = [&](int64_t g, int k2) {
+            return (double)((P.tiles + g - 1) / g) * (double)((P.nchunks + k2 - 1) / k2) + (k2 > 1 ? split_cost() : 0.0);
+        };
+        double best = whole && mode != 2 ? units(groups, 1) : 1e300;
+        int best_ks = whole && mode != 2 ? 1 : 0;
+        int64_t best_groups = groups;
+        if (!whole || mode != 0) {
+            const int64_t sms = sm_count();
+            for (int k2 = 2; k2 <= kWMaxSplit && k2 <= P.nchunks; k2 *= 2) {
+                int64_t g2 = sms / k2 < P.tiles ? sms / k2 : P.tiles;
+                WarpParams Q = P;
+                size_t s2 = 0;
+                if (!wplan<D>(Q, g2, k2, &s2)) continue;
+                const int64_t clusters = max_clusters(kern_split, set_for_split, k2, s2);
+                if (clusters < 1) continue;
+                if (clusters < g2) {  // fewer clusters fit than SMs / KS: more tiles each
+                    g2 = clusters;
+                    if (!wplan<D>(Q, g2, k2, &s2)) continue;
+                }
+                const double c = units(g2, k2);
+                if (!best_ks || (!whole && best_ks == 1) || c < best) {
+                    best = c;
+                    best_ks = k2;
+                    best_groups = g2;
+                }
+                if (!whole && mode == 0) break;  // the first split that fits, as needed
             }
-            ks = k2;
-            break;
         }
-        if (!ks) return cudaErrorNotSupported;
+        if (!best_ks) return cudaErrorNotSupported;
+        ks = best_ks;
+        groups = best_groups;
+        if (!wplan<D>(P, groups, ks, &smem)) return cudaErrorNotSupported;
     }
     P.ksplit = ks;
     cudaError_t e = ks > 1 ? ensure_smem(kern_split, set_for_split, smem) : ensure_smem(kern, set_for, smem);
