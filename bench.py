@@ -522,12 +522,21 @@ def measure(args, torch, rank, world, local, dist):
         def step():
             step_linears()
 
+    nccl_fallback = set()  # row-parallel linears the fused all-reduce GEMV does not take
+
     def step_linears():
         for idx in groups:
-            if comm is not None and stores[idx[0]][3] == "cols":
+            if comm is not None and stores[idx[0]][3] == "cols" and idx[0] not in nccl_fallback:
                 store = stores[idx[0]][0]
-                comm.linear_allreduce(store, inputs[stores[idx[0]][4]], out=outs[idx[0]])
-                continue
+                try:
+                    comm.linear_allreduce(store, inputs[stores[idx[0]][4]], out=outs[idx[0]])
+                    continue
+                except clq.ClqError as exc:
+                    # a shape the fused kernel does not plan (the same on every
+                    # rank, so every rank takes the same collective path)
+                    if exc.status != "CLQ_ERR_UNSUPPORTED":
+                        raise
+                    nccl_fallback.add(idx[0])
             run_group(idx)
             if dist is not None and stores[idx[0]][3] == "cols":
                 dist.all_reduce(outs[idx[0]])
@@ -660,6 +669,7 @@ def measure(args, torch, rank, world, local, dist):
             "gpu_launches_per_step": {"clq": ours_per_step, "all_kernel_nodes": kernels_per_step},
             "clocks": clock,
             "check": check,
+            "allreduce_nccl_fallbacks": len(nccl_fallback) if comm is not None else None,
             "libraries_mapped": repo_libraries(),
         }
         if prefill:
