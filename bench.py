@@ -226,6 +226,8 @@ def config_runs(world):
     runs += [(f"c2_llama32_1b_q4_m{m}", dict(workload="q4-llama32-1b", m=m)) for m in (1, 4, 16)]
     runs += [(f"c3_q6k_vocab_qwen3_8b_m{m}", dict(workload="q6k-vocab-qwen3-8b", m=m)) for m in (1, 8, 64)]
     runs += [(f"c4_llama3_8b_prefill_m{m}", dict(m=m)) for m in (128, 512, 2048)]
+    # the drop-in prefill: fp32 activations through the exact GEMM (fp32-class products)
+    runs += [("c4_llama3_8b_prefill_m512_f32_exact", dict(m=512, xtype="f32"))]
     runs += [(f"c5_llama3_70b_decode_m{m}", dict(model="70b", m=m)) for m in (1, 8)]
     runs += [("llama3_8b_decode_m8", dict(m=8))]
     return runs
@@ -302,7 +304,7 @@ def summary(r):
     return out
 
 
-def check_outputs(torch, stores, outs, inputs, m, gemm, world):
+def check_outputs(torch, stores, outs, inputs, m, gemm, world, wide=False):
     """Per-run correctness: sampled output columns against float64 products.
 
     The reference product is x . dequant(W)^T in float64, with dequant(W) from
@@ -319,7 +321,7 @@ def check_outputs(torch, stores, outs, inputs, m, gemm, world):
     worst, ok, checked = 0.0, True, 0
     rel_tol, abs_tol = (1e-3, 1e-6) if gemm else (1e-5, 1e-5)
     picks = range(len(stores))
-    if gemm:  # the first decoder layer and the head: the fp64 products grow with M
+    if wide:  # the first decoder layer and the head: the fp64 products grow with M
         picks = list(range(min(7, len(stores)))) + [len(stores) - 1]
     for i in picks:
         store, s, dtype, kind, src, name = stores[i]
@@ -328,7 +330,7 @@ def check_outputs(torch, stores, outs, inputs, m, gemm, world):
         x = inputs[src].float().cpu().numpy().astype(np.float64)
         # the norm over a row needs enough columns to be a stable estimate:
         # 16 per end for the GEMV's fp32-class products, 128 for the GEMM's
-        per_end = 128 if gemm else 16
+        per_end = 128 if wide else 16
         for r0 in sorted({0, max(0, s.n - per_end)}):
             cnt = min(per_end, s.n - r0)
             w = store.dequantize(r0, cnt).cpu().numpy().astype(np.float64)
@@ -342,7 +344,7 @@ def check_outputs(torch, stores, outs, inputs, m, gemm, world):
         checked += 1
     return {"max_rel_err": worst, "gate": 1e-3, "element_bound": f"{abs_tol:g} + {rel_tol:g}*sum|x*w|",
             "element_bound_ok": ok, "passed": ok and worst <= 1e-3, "linears_checked": checked,
-            "rows_per_linear": 256 if gemm else 32,
+            "rows_per_linear": 256 if wide else 32,
             "reference": "float64 x . dequant(W)^T, dequant by the store's bit-exact dequantize kernel"}
 
 
@@ -381,7 +383,8 @@ def measure(args, torch, rank, world, local, dist):
     m = args.m
     xtype = args.xtype or ("f32" if m < 64 else "bf16")
     xdtype = {"f32": torch.float32, "bf16": torch.bfloat16, "f16": torch.float16}[xtype]
-    prefill = m >= 64 and xtype != "f32"
+    prefill = m >= 64  # the tcgen05 GEMM: fp16 operands for 16-bit activations, the exact form for fp32
+    exact = prefill and xtype == "f32"
     if args.workload != "step" and world > 1:
         raise SystemExit("GEMV sweeps run on one GPU")
     linears = workload_linears(args, tp, cfg)
@@ -604,7 +607,7 @@ def measure(args, torch, rank, world, local, dist):
     # the outputs of the last timed step, checked against float64 products
     check = None
     if fuse_mode == "off":
-        check = check_outputs(torch, stores, outs, inputs, m, prefill, world)
+        check = check_outputs(torch, stores, outs, inputs, m, prefill and not exact, world, wide=prefill)
         if dist is not None:
             t = torch.tensor([check["max_rel_err"], 0.0 if check["element_bound_ok"] else 1.0],
                              dtype=torch.float64, device="cuda")
@@ -646,7 +649,7 @@ def measure(args, torch, rank, world, local, dist):
     # ---- end to end -------------------------------------------------------------
     e2e = None
     if not args.no_e2e:
-        e2e = e2e_dropin(args, clq, stores, host_copies, m, job_bytes, prefill) if world == 1 else \
+        e2e = e2e_dropin(args, clq, stores, host_copies, m, job_bytes, prefill and not exact) if world == 1 else \
             e2e_tp(args, torch, dist, graph, inputs, logits, job_bytes)
 
     del graph, kgraph
@@ -677,7 +680,9 @@ def measure(args, torch, rank, world, local, dist):
             k_tf = k_flops / (k_ms * 1e-3) / 1e12
             result["tflops"] = round(step_flops * world / (ms * 1e-3) / 1e12, 1)
             result["roofline"] = {
-                "bound": "tensor", "kernel": "Q4_K linears (activation prep + tcgen05 GEMM + split-K reduce), "
+                "bound": "tensor", "kernel": ("Q4_K linears (activation prep + exact tcgen05 GEMM: three fp16 MMAs "
+                                              "per K step + split-K reduce), " if exact else
+                                              "Q4_K linears (activation prep + tcgen05 GEMM + split-K reduce), ")
                                             "M=%d" % m,
                 "achieved": round(k_tf, 1), "peak": tpeak, "peak_kind": tpeak_kind + " (burst, dense bf16)",
                 "unit": "TFLOP/s", "frac": round(k_tf / tpeak, 4), "traffic": None,

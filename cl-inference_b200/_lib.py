@@ -12,7 +12,7 @@ LIBRARY_PATH = _HERE / "libclq.so"
 
 CLQ_Q4_0, CLQ_Q8_0, CLQ_Q4_K, CLQ_Q6_K = 2, 8, 12, 14
 CLQ_X_F32, CLQ_X_BF16, CLQ_X_F16 = 0, 1, 2
-CLQ_MATH_DEFAULT, CLQ_MATH_FAST, CLQ_NO_CACHE = 0, 1, 2
+CLQ_MATH_DEFAULT, CLQ_MATH_FAST, CLQ_NO_CACHE, CLQ_MATH_EXACT = 0, 1, 2, 4
 
 STATUS_NAMES = {
     0: "CLQ_OK", 1: "CLQ_ERR_ARGUMENT", 2: "CLQ_ERR_SHAPE", 3: "CLQ_ERR_BLOCKS",

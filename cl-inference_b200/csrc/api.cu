@@ -404,7 +404,7 @@ int clq_linear_device(const clq_store* w, int64_t row_begin, int64_t rows, const
     if (!w) return fail(CLQ_ERR_ARGUMENT, "null store");
     if (xtype != CLQ_X_F32 && xtype != CLQ_X_BF16 && xtype != CLQ_X_F16)
         return fail(CLQ_ERR_ARGUMENT, "unknown activation type %d", xtype);
-    if (flags & ~(CLQ_MATH_FAST)) return fail(CLQ_ERR_ARGUMENT, "unknown product flags 0x%x", flags);
+    if (flags & ~(CLQ_MATH_FAST | CLQ_MATH_EXACT)) return fail(CLQ_ERR_ARGUMENT, "unknown product flags 0x%x", flags);
     if (row_begin < 0 || rows < 0 || row_begin + rows > w->n || m < 0)
         return fail(CLQ_ERR_SHAPE, "rows [%lld, %lld) / m %lld outside a (%lld %lld) weight",
                     (long long)row_begin, (long long)(row_begin + rows), (long long)m,
@@ -439,7 +439,7 @@ int clq_linear_group_device(const clq_store* const* w, const int64_t* row_begin,
         if (w[i]->dtype != w[0]->dtype || w[i]->k != w[0]->k)
             return fail(CLQ_ERR_SHAPE, "group members need one dtype and row length");
     }
-    bool fused = m > 0 && w[0]->k > 0 && w[0]->k % 256 == 0 && !(flags & ~CLQ_MATH_FAST) &&
+    bool fused = m > 0 && w[0]->k > 0 && w[0]->k % 256 == 0 && !(flags & ~(CLQ_MATH_FAST | CLQ_MATH_EXACT)) &&
                  !clq::uses_gemm_tc(view_of(w[0], 0), xtype, m, flags);
     for (int i = 0; i < count && fused; i++)
         fused = row_begin[i] >= 0 && rows[i] > 0 && row_begin[i] + rows[i] <= w[i]->n && ldo[i] >= rows[i] && out[i];
@@ -480,7 +480,7 @@ int clq_linear_group_fused_device(const clq_store* const* w, const int64_t* row_
     if (!w || !row_begin || !rows || !out || !ldo) return fail(CLQ_ERR_ARGUMENT, "null group array");
     if (xtype != CLQ_X_F32 && xtype != CLQ_X_BF16 && xtype != CLQ_X_F16)
         return fail(CLQ_ERR_ARGUMENT, "unknown activation type %d", xtype);
-    if (flags & ~(CLQ_MATH_FAST)) return fail(CLQ_ERR_ARGUMENT, "unknown product flags 0x%x", flags);
+    if (flags & ~(CLQ_MATH_FAST | CLQ_MATH_EXACT)) return fail(CLQ_ERR_ARGUMENT, "unknown product flags 0x%x", flags);
     if (fusion->residual && count != 1) return fail(CLQ_ERR_ARGUMENT, "a residual needs a single weight");
     if (!(fusion->norm_epsilon >= 0.f) || fusion->norm_epsilon == INFINITY)
         return fail(CLQ_ERR_ARGUMENT, "RMSNorm epsilon must be finite and non-negative");
@@ -541,7 +541,8 @@ int clq_linear_group_fused_device(const clq_store* const* w, const int64_t* row_
     if (h && (e = clq::launch_fuse_input(x, xtype, m, k, f, h, s)) != cudaSuccess) rc = cuda_fail(e, "fused input");
     const void* xin = h ? (const void*)h : x;
     const int xt = h ? CLQ_X_F32 : xtype;
-    const unsigned pf = (h && clq::uses_gemm_tc(views[0], xtype, m, flags)) ? (flags | CLQ_MATH_FAST) : flags;
+    // the fused input is fp32; a 16-bit request keeps the GEMM form it would have had
+    const unsigned pf = (h && xtype != CLQ_X_F32 && !(flags & CLQ_MATH_EXACT)) ? (flags | CLQ_MATH_FAST) : flags;
     if (!rc) {
         if (f.res) rc = clq_linear_device(w[0], row_begin[0], rows[0], xin, xt, m, part, rows[0], pf, stream);
         else rc = clq_linear_group_device(w, row_begin, rows, count, xin, xt, m, out, ldo, pf, stream);
@@ -588,7 +589,7 @@ int clq_matmul(int dtype, float* out, const float* x, const uint8_t* bytes, int6
     int elems, bb, rc;
     if ((rc = check_shape(dtype, n, k, &elems, &bb))) return rc;
     if (m < 0) return fail(CLQ_ERR_SHAPE, "negative activation rows %lld", (long long)m);
-    if (flags & ~(CLQ_MATH_FAST | CLQ_NO_CACHE)) return fail(CLQ_ERR_ARGUMENT, "unknown flags 0x%x", flags);
+    if (flags & ~(CLQ_MATH_FAST | CLQ_NO_CACHE | CLQ_MATH_EXACT)) return fail(CLQ_ERR_ARGUMENT, "unknown flags 0x%x", flags);
     if (m == 0 || n == 0) return CLQ_OK;
     if (!out || (k && (!x || !bytes))) return fail(CLQ_ERR_ARGUMENT, "null out, x or weight bytes");
     if (k == 0) {
@@ -622,7 +623,7 @@ int clq_matmul(int dtype, float* out, const float* x, const uint8_t* bytes, int6
         return cuda_fail(e, "copy x to device");
     float* dout = staged ? (float*)ctx->hout.dptr : (float*)ctx->out.ptr;
     if ((e = clq::launch_linear(view_of(store.get(), row_begin), n, ctx->x.ptr, CLQ_X_F32, m, dout, n,
-                                flags & CLQ_MATH_FAST, ctx->stream)) != cudaSuccess)
+                                flags & (CLQ_MATH_FAST | CLQ_MATH_EXACT), ctx->stream)) != cudaSuccess)
         return cuda_fail(e, "linear kernel launch");
     if (!staged && (e = cudaMemcpyAsync(out, ctx->out.ptr, obytes, cudaMemcpyDeviceToHost, ctx->stream)) !=
                        cudaSuccess)

@@ -123,13 +123,15 @@ struct GemmPlan {
     int64_t token_tiles, row_tiles;
     int splits;            // K splits (partials reduced in a second kernel)
     int kb_per_split;      // 64-wide K blocks per split
+    bool exact, xlo;       // fp32-class products: weights (and activations, xlo) as hi + lo
+    int stages;            // pipeline depth
     size_t xs_bytes, us_bytes, part_bytes;
     size_t smem;           // dynamic shared memory per CTA
 };
-// DTYPE picks the kernel: Q4_K weights of at least 256 rows take the one with
-// 256-row tiles and tensor-map staged packed bytes (any multiple of 16 tokens
-// per tile, chosen to fill whole waves).
-GemmPlan plan_gemm_tc(int dtype, int64_t rows, int64_t k, int64_t m);
+// DTYPE picks the kernel: Q4_K weights of at least 256 rows may take the one
+// with 256-row tiles (a tuning knob).  EXACT: fp32-class products, the weights
+// split into fp16 hi + lo parts and, with XLO, the activations too.
+GemmPlan plan_gemm_tc(int dtype, int64_t rows, int64_t k, int64_t m, bool exact, bool xlo);
 size_t gemm_tc_scratch_bytes(const GemmPlan& g);
 // plan_gemm_tc with fewer K splits until the scratch fits in CAP bytes;
 // splits = 0 when it cannot fit.

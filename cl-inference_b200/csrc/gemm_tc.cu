@@ -131,7 +131,7 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
 // and us[t] = 1 / scale.  Rows t in [m, m_pad) are written as zeros.
 template <typename XT>
 __global__ void prep_x_kernel(const XT* __restrict__ x, int64_t m, int64_t k, int tn, uint8_t* __restrict__ xs,
-                              float* __restrict__ us) {
+                              float* __restrict__ us, uint8_t* __restrict__ xs_lo) {
     const int64_t t = blockIdx.x;
     const int64_t tt = t / tn, r = t % tn;
     const int64_t kbt = k / kKB;
@@ -167,7 +167,7 @@ __global__ void prep_x_kernel(const XT* __restrict__ x, int64_t m, int64_t k, in
     for (int64_t cidx = threadIdx.x; cidx < k / 8; cidx += blockDim.x) {
         const int64_t kb = cidx / 8;
         const int c = (int)(cidx % 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
+        uint4 v = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
         if (t < m) {
             float f[8];
 #pragma unroll
@@ -182,8 +182,26 @@ __global__ void prep_x_kernel(const XT* __restrict__ x, int64_t m, int64_t k, in
             v.y = pack_half2(f[2], f[3]);
             v.z = pack_half2(f[4], f[5]);
             v.w = pack_half2(f[6], f[7]);
+            if (xs_lo) {
+                // the rest of each value, times 2^11 (back in the fp16 range
+                // of the value itself), so that hi + lo / 2^11 carries ~22 bits
+                float g[8];
+                const uint32_t hv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&hv[j]));
+                    g[2 * j] = (f[2 * j] - h.x) * 2048.f;
+                    g[2 * j + 1] = (f[2 * j + 1] - h.y) * 2048.f;
+                }
+                vl.x = pack_half2(g[0], g[1]);
+                vl.y = pack_half2(g[2], g[3]);
+                vl.z = pack_half2(g[4], g[5]);
+                vl.w = pack_half2(g[6], g[7]);
+            }
         }
-        *reinterpret_cast<uint4*>(xs + (tt * kbt + kb) * tn * 128 + swz((uint32_t)r, (uint32_t)c)) = v;
+        const int64_t off = (tt * kbt + kb) * tn * 128 + swz((uint32_t)r, (uint32_t)c);
+        *reinterpret_cast<uint4*>(xs + off) = v;
+        if (xs_lo) *reinterpret_cast<uint4*>(xs_lo + off) = vl;
     }
 }
 
@@ -365,6 +383,107 @@ __device__ __forceinline__ void convert_raw(const Planes& p, int64_t grow, int64
     for (int i = 0; i < 4; i++) *reinterpret_cast<uint4*>(a + swz(row, (uint32_t)ci[i])) = ch[i];
 }
 
+// The exact form of convert_raw: each element's fp32 value as the reference
+// computes it (quant/packed.lisp:89-108, the oracle's element functions,
+// operations in the same order), split into hi = fp16(w) and
+// lo = fp16((w - hi) * 2^11), written to A (chunks as convert_raw's) and A_LO.
+__device__ __forceinline__ void put_split(float w0, float w1, uint32_t& hi, uint32_t& lo) {
+    const __half2 h = __floats2half2_rn(w0, w1);
+    const float2 hf = __half22float2(h);
+    hi = *reinterpret_cast<const uint32_t*>(&h);
+    lo = pack_half2(__fmul_rn(__fsub_rn(w0, hf.x), 2048.f), __fmul_rn(__fsub_rn(w1, hf.y), 2048.f));
+}
+__device__ __forceinline__ float u2f(uint32_t v) { return __uint_as_float(0x4B000000u | v) - 8388608.f; }  // v < 2^23
+
+template <int D>
+__device__ __forceinline__ void convert_raw_exact(const Planes& p, int64_t grow, int64_t kb, int hv, const Raw<D>& rw,
+                                                  uint32_t row, uint8_t* a, uint8_t* a_lo) {
+    uint32_t hi[4][4], lo[4][4];
+    int ci[4] = {2 * hv, 2 * hv + 1, 4 + 2 * hv, 5 + 2 * hv};
+    if constexpr (D == kQ4_K) {
+        const int qt = (int)(kb & 3);
+        auto sbyte = [&](int i) -> uint32_t {
+            const int wsel = i >> 2;
+            const uint32_t w = wsel == 0 ? rw.hd.y : wsel == 1 ? rw.hd.z : rw.hd.w;
+            return (w >> (8 * (i & 3))) & 0xFF;
+        };
+        float ds[2], dm[2];
+        const float d = __half2float(__ushort_as_half((unsigned short)(rw.hd.x & 0xFFFF)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(rw.hd.x >> 16)));
+#pragma unroll
+        for (int u = 0; u < 2; u++) {  // quant/packed.lisp:91-98
+            const int g = 2 * qt + u;
+            uint32_t sc, mn;
+            if (g < 4) {
+                sc = sbyte(g) & 63;
+                mn = sbyte(g + 4) & 63;
+            } else {
+                sc = (sbyte(g + 4) & 15) | ((sbyte(g - 4) & 192) >> 2);
+                mn = (sbyte(g + 4) >> 4) | ((sbyte(g) & 192) >> 2);
+            }
+            ds[u] = __fmul_rn(d, u2f(sc));
+            dm[u] = __fmul_rn(dmin, u2f(mn));
+        }
+        const uint32_t cw[4] = {rw.cw.x, rw.cw.y, rw.cw.z, rw.cw.w};
+        // code byte j: element j of this half of sub-block 2qt (low nibble) and 2qt + 1 (high)
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+            const uint32_t b0 = (cw[j >> 2] >> (8 * (j & 3))) & 0xFF, b1 = (cw[j >> 2] >> (8 * ((j + 1) & 3))) & 0xFF;
+            const float l0 = __fsub_rn(__fmul_rn(ds[0], u2f(b0 & 15)), dm[0]);
+            const float l1 = __fsub_rn(__fmul_rn(ds[0], u2f(b1 & 15)), dm[0]);
+            const float h0 = __fsub_rn(__fmul_rn(ds[1], u2f(b0 >> 4)), dm[1]);
+            const float h1 = __fsub_rn(__fmul_rn(ds[1], u2f(b1 >> 4)), dm[1]);
+            put_split(l0, l1, hi[j >> 3][(j & 7) >> 1], lo[j >> 3][(j & 7) >> 1]);
+            put_split(h0, h1, hi[2 + (j >> 3)][(j & 7) >> 1], lo[2 + (j >> 3)][(j & 7) >> 1]);
+        }
+    } else if constexpr (D == kQ6_K) {
+        const int odd = (int)(kb & 1);
+        const int hh = (int)((kb & 3) >> 1);
+        const float d = __half2float(__ushort_as_half((unsigned short)rw.d));
+        auto sc = [&](int i) -> int {
+            const int wsel = i >> 2;
+            const uint32_t w = wsel == 0 ? rw.sv.x : wsel == 1 ? rw.sv.y : wsel == 2 ? rw.sv.z : rw.sv.w;
+            return (int)(int8_t)((w >> (8 * (i & 3))) & 0xFF);
+        };
+        const uint32_t* wv = rw.w;
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int grp = 2 * odd + u;
+            const int lo_shift = 4 * (grp >> 1), qsh = 2 * grp;
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                const float ds = __fmul_rn(d, (float)sc(8 * hh + 2 * grp + half));  // quant/packed.lisp:107-108
+#pragma unroll
+                for (int tq = 0; tq < 2; tq++) {
+                    const uint32_t* w3 = &wv[6 * tq + 3 * half];
+                    const uint32_t q = ((w3[u] >> lo_shift) & 0x0F0F0F0Fu) | (((w3[2] >> qsh) & 0x03030303u) << 4);
+                    float e[4];
+#pragma unroll
+                    for (int b = 0; b < 4; b++) e[b] = __fmul_rn(ds, (float)((int)((q >> (8 * b)) & 0xFF) - 32));
+                    put_split(e[0], e[1], hi[2 * u + half][2 * tq], lo[2 * u + half][2 * tq]);
+                    put_split(e[2], e[3], hi[2 * u + half][2 * tq + 1], lo[2 * u + half][2 * tq + 1]);
+                }
+                ci[2 * u + half] = 4 * u + 2 * half + hv;
+            }
+        }
+    } else {
+        // Q4_0 / Q8_0: element by element (two 32-element blocks)
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            const int64_t e0 = kb * kKB + 16 * hv + 2 * j, e1 = e0 + 32;
+            put_split(element_planar<D>(p, grow, e0), element_planar<D>(p, grow, e0 + 1), hi[j >> 2][j & 3],
+                      lo[j >> 2][j & 3]);
+            put_split(element_planar<D>(p, grow, e1), element_planar<D>(p, grow, e1 + 1), hi[2 + (j >> 2)][j & 3],
+                      lo[2 + (j >> 2)][j & 3]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        *reinterpret_cast<uint4*>(a + swz(row, (uint32_t)ci[i])) = make_uint4(hi[i][0], hi[i][1], hi[i][2], hi[i][3]);
+        *reinterpret_cast<uint4*>(a_lo + swz(row, (uint32_t)ci[i])) = make_uint4(lo[i][0], lo[i][1], lo[i][2], lo[i][3]);
+    }
+}
+
 struct GemmParams {
     Planes p;
     int64_t rows, k, m;
@@ -374,18 +493,29 @@ struct GemmParams {
     int64_t ldo;
     int tn;             // tokens per tile (power of two, 32..256)
     int kb_per_split;
+    int stages;         // pipeline depth (2..4)
+    const uint8_t* xs_lo;  // exact form: the activations' scaled low parts, or null
     int* err;           // the device status word
 };
 
-template <int D>
+// EXACT: the weights as fp16 hi plus a low part times 2^11 (two A tiles per
+// stage), and for fp32 activations (P.xs_lo set) the activations likewise
+// (two B tiles).  The hi x hi products accumulate in tensor-memory columns
+// [0, tn), the lo x hi and hi x lo ones in [tn, 2 tn), and the epilogue adds
+// the second accumulator times 2^-11: fp32-class products (about 22 bits of
+// each operand) from fp16 MMAs, three per K step instead of one.
+template <int D, bool EXACT>
 __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzle atoms
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    const int tn = P.tn;
-    uint8_t* A = smem;                                   // kStages x 16 KB
-    uint8_t* B = A + kStages * kTM * 128;                // kStages x tn * 128
-    uint64_t* full_a = reinterpret_cast<uint64_t*>(B + (size_t)kStages * tn * 128);
+    const int tn = P.tn, NS = P.stages;
+    const bool xlo = EXACT && P.xs_lo != nullptr;
+    constexpr uint32_t kA = (EXACT ? 2u : 1u) * kTM * 128;  // per stage: hi (and lo) weight tiles
+    const uint32_t kBt = (uint32_t)tn * 128, kB = (xlo ? 2u : 1u) * kBt;
+    uint8_t* A = smem;                                   // NS x kA
+    uint8_t* B = A + (size_t)NS * kA;                    // NS x kB
+    uint64_t* full_a = reinterpret_cast<uint64_t*>(B + (size_t)NS * kB);
     uint64_t* full_b = full_a + kStages;
     uint64_t* empty = full_b + kStages;
     uint64_t* done = empty + kStages;
@@ -399,9 +529,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
     const int64_t kb0 = (int64_t)split * P.kb_per_split;
     const int64_t kb1 = (kb0 + P.kb_per_split) < kbt ? (kb0 + P.kb_per_split) : kbt;
     const int nk = (int)(kb1 - kb0);
+    const uint32_t cols = EXACT ? 2u * (uint32_t)tn : (uint32_t)tn;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; s++) {
+        for (int s = 0; s < NS; s++) {
             mbar_init(&full_a[s], 8);
             mbar_init(&full_b[s], 1);
             mbar_init(&empty[s], 1);
@@ -409,9 +540,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
         mbar_init(done, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 0) {  // tensor memory: tn fp32 columns x 128 lanes
+    if (warp == 0) {  // tensor memory: tn fp32 columns x 128 lanes (two accumulators when exact)
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(tn)
+                     "r"(cols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -431,10 +562,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
         if (nk > 0) load_raw<D>(P.p, grow, kb0, hv, r0);
         if (nk > 1) load_raw<D>(P.p, grow, kb0 + 1, hv, r1);
         for (int it = 0; it < nk; it++) {
-            const int s = it % kStages;
+            const int s = it % NS;
             if (it + 2 < nk) load_raw<D>(P.p, grow, kb0 + it + 2, hv, r2);  // two stages in flight
-            if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, err)) break;
-            convert_raw<D>(P.p, grow, kb0 + it, hv, r0, row, A + s * kTM * 128);
+            if (it >= NS && !mbar_wait(&empty[s], ((it / NS) - 1) & 1, err)) break;
+            if constexpr (EXACT)
+                convert_raw_exact<D>(P.p, grow, kb0 + it, hv, r0, row, A + (size_t)s * kA, A + (size_t)s * kA + kTM * 128);
+            else
+                convert_raw<D>(P.p, grow, kb0 + it, hv, r0, row, A + (size_t)s * kA);
             fence_async_shared();
             __syncwarp();
             if (lane == 0) mbar_arrive(&full_a[s]);
@@ -450,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
             const uint32_t taddr = tmem + ((uint32_t)(32 * q) << 16);
             const int cbeg = ch * (tn / 2), cend = cbeg + tn / 2;
             for (int c0 = cbeg; c0 < cend; c0 += 16) {
-                uint32_t v[16];
+                uint32_t v[16], vc[16];
                 asm volatile(
                     "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
                     "[%16];"
@@ -458,13 +592,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
                       "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]),
                       "=r"(v[15])
                     : "r"(taddr + (uint32_t)c0));
+                if constexpr (EXACT) {
+                    asm volatile(
+                        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, "
+                        "[%16];"
+                        : "=r"(vc[0]), "=r"(vc[1]), "=r"(vc[2]), "=r"(vc[3]), "=r"(vc[4]), "=r"(vc[5]), "=r"(vc[6]),
+                          "=r"(vc[7]), "=r"(vc[8]), "=r"(vc[9]), "=r"(vc[10]), "=r"(vc[11]), "=r"(vc[12]), "=r"(vc[13]),
+                          "=r"(vc[14]), "=r"(vc[15])
+                        : "r"(taddr + (uint32_t)(tn + c0)));
+                }
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 if (r < P.rows) {
 #pragma unroll
                     for (int j = 0; j < 16; j++) {
                         const int64_t t = tt * tn + c0 + j;
                         if (t < P.m) {
-                            const float val = __uint_as_float(v[j]) * P.us[t];
+                            float acc = __uint_as_float(v[j]);
+                            if constexpr (EXACT) acc = fmaf(__uint_as_float(vc[j]), 4.8828125e-4f, acc);  // + 2^-11 corr
+                            const float val = acc * P.us[t];
                             if (gridDim.z == 1) P.out[t * P.ldo + r] = val;
                             else P.out[((int64_t)split * P.m + t) * P.rows + r] = val;
                         }
@@ -475,12 +620,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
     } else if (warp == 8) {
         // ---- activation tiles: one bulk copy per stage ----
         if (lane == 0) {
-            const uint32_t bytes = (uint32_t)tn * 128;
             for (int it = 0; it < nk; it++) {
-                const int s = it % kStages;
-                if (it >= kStages && !mbar_wait(&empty[s], ((it / kStages) - 1) & 1, err)) break;
-                mbar_arrive_tx(&full_b[s], bytes);
-                bulk_copy(B + (size_t)s * tn * 128, P.xs + ((tt * kbt + kb0 + it) * tn) * 128, bytes, &full_b[s]);
+                const int s = it % NS;
+                if (it >= NS && !mbar_wait(&empty[s], ((it / NS) - 1) & 1, err)) break;
+                const int64_t off = ((tt * kbt + kb0 + it) * tn) * 128;
+                mbar_arrive_tx(&full_b[s], kB);
+                bulk_copy(B + (size_t)s * kB, P.xs + off, kBt, &full_b[s]);
+                if (xlo) bulk_copy(B + (size_t)s * kB + kBt, P.xs_lo + off, kBt, &full_b[s]);
             }
         }
     } else {
@@ -489,14 +635,24 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
             const uint32_t idesc = instr_desc(tn);
             int it = 0;
             for (; it < nk; it++) {
-                const int s = it % kStages;
-                const uint32_t ph = (it / kStages) & 1;
+                const int s = it % NS;
+                const uint32_t ph = (it / NS) & 1;
                 if (!mbar_wait(&full_a[s], ph, err) || !mbar_wait(&full_b[s], ph, err)) break;
                 tc_fence_after();
-                const uint32_t a_addr = smem_u32(A + s * kTM * 128), b_addr = smem_u32(B + (size_t)s * tn * 128);
+                const uint32_t a_addr = smem_u32(A + (size_t)s * kA), b_addr = smem_u32(B + (size_t)s * kB);
 #pragma unroll
-                for (int j = 0; j < kKB / 16; j++)
-                    mma_f16(tmem, smem_desc(a_addr + 32 * j), smem_desc(b_addr + 32 * j), idesc, (it > 0 || j > 0) ? 1u : 0u);
+                for (int j = 0; j < kKB / 16; j++) {
+                    const uint32_t acc = (it > 0 || j > 0) ? 1u : 0u;
+                    mma_f16(tmem, smem_desc(a_addr + 32 * j), smem_desc(b_addr + 32 * j), idesc, acc);
+                    if constexpr (EXACT) {
+                        // lo(w) x hi(x), then hi(w) x lo(x), into the correction accumulator
+                        mma_f16(tmem + (uint32_t)tn, smem_desc(a_addr + kTM * 128 + 32 * j), smem_desc(b_addr + 32 * j),
+                                idesc, acc);
+                        if (xlo)
+                            mma_f16(tmem + (uint32_t)tn, smem_desc(a_addr + 32 * j), smem_desc(b_addr + kBt + 32 * j),
+                                    idesc, 1u);
+                    }
+                }
                 mma_commit(&empty[s]);
             }
             mma_commit(done);  // arrives once every MMA issued above has completed
@@ -505,14 +661,13 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
     }
     // Bulk copies in flight must land before the CTA exits.
     if (warp == 8 && lane == 0) {
-        for (int it = nk - kStages < 0 ? 0 : nk - kStages; it < nk; it++)
-            mbar_drain(&full_b[it % kStages], (it / kStages) & 1);
+        for (int it = nk - NS < 0 ? 0 : nk - NS; it < nk; it++) mbar_drain(&full_b[it % NS], (it / NS) & 1);
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tn) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(cols) : "memory");
     }
 }
 
@@ -843,10 +998,12 @@ int env_tn() {
 }
 }  // namespace
 
-GemmPlan plan_gemm_tc(int dtype, int64_t rows, int64_t k, int64_t m) {
+GemmPlan plan_gemm_tc(int dtype, int64_t rows, int64_t k, int64_t m, bool exact, bool xlo) {
     GemmPlan g;
+    g.exact = exact;
+    g.xlo = exact && xlo;
     const int64_t kbt = k / kKB;
-    if (takes_tma(dtype, rows)) {
+    if (!exact && takes_tma(dtype, rows)) {
         // 256-row tiles; tokens per tile chosen so the tiles fill whole waves:
         // a tile costs max(4 tn, 900) cycles per 64-wide K block (its MMAs,
         // or the dequantization of 256 rows), a wave costs its slowest tile
@@ -872,21 +1029,26 @@ GemmPlan plan_gemm_tc(int dtype, int64_t rows, int64_t k, int64_t m) {
         g.row_tile = kTM;
         g.row_tiles = (rows + kTM - 1) / kTM;
         int tn = 32;
-        while (tn < 256 && tn < m) tn *= 2;
+        // the exact form doubles the weight tiles (and activation tiles for
+        // fp32 activations): at most 128 tokens a tile keeps three stages
+        while (tn < (exact ? 128 : 256) && tn < m) tn *= 2;
         g.tn = tn;
     }
     g.token_tiles = (m + g.tn - 1) / g.tn;
     g.splits = split_count(g.token_tiles * g.row_tiles, kbt);
     g.kb_per_split = (int)((kbt + g.splits - 1) / g.splits);
-    g.xs_bytes = (size_t)g.token_tiles * g.tn * k * 2;
+    g.xs_bytes = (size_t)g.token_tiles * g.tn * k * 2 * (g.xlo ? 2 : 1);  // hi image, then lo
     g.us_bytes = (size_t)g.token_tiles * g.tn * sizeof(float);
     g.part_bytes = g.splits > 1 ? (size_t)g.splits * m * rows * sizeof(float) : 0;
-    g.smem = 1024 + (size_t)kStages * (kTM * 128 + g.tn * 128) + 256;
+    const size_t per_stage = (size_t)kTM * 128 * (exact ? 2 : 1) + (size_t)g.tn * 128 * (g.xlo ? 2 : 1);
+    g.stages = kStages;
+    while (g.stages > 2 && 1024 + (size_t)g.stages * per_stage + 256 > 227 * 1024) g.stages--;
+    g.smem = 1024 + (size_t)g.stages * per_stage + 256;
     return g;
 }
 
 GemmPlan plan_gemm_tc_capped(int dtype, int64_t rows, int64_t k, int64_t m, size_t cap) {
-    GemmPlan g = plan_gemm_tc(dtype, rows, k, m);
+    GemmPlan g = plan_gemm_tc(dtype, rows, k, m, false, false);
     while (g.splits > 1 && gemm_tc_scratch_bytes(g) > cap) {
         g.splits /= 2;
         const int64_t kbt = k / kKB;
@@ -911,16 +1073,22 @@ cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int
     int* err = device_status_word();
     if (!err) return cudaErrorNotSupported;
     uint8_t* xs = scratch;
+    uint8_t* xs_lo = g.xlo ? xs + g.xs_bytes / 2 : nullptr;
     float* us = reinterpret_cast<float*>(xs + al(g.xs_bytes));
     float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(us) + al(g.us_bytes));
     cudaError_t e = cudaSuccess;
     const unsigned prep_grid = (unsigned)(g.token_tiles * g.tn);
     switch (xtype) {
-    case CLQ_X_F32: prep_x_kernel<float><<<prep_grid, 256, 0, stream>>>((const float*)x, m, w.k, g.tn, xs, us); break;
-    case CLQ_X_BF16:
-        prep_x_kernel<__nv_bfloat16><<<prep_grid, 256, 0, stream>>>((const __nv_bfloat16*)x, m, w.k, g.tn, xs, us);
+    case CLQ_X_F32:
+        prep_x_kernel<float><<<prep_grid, 256, 0, stream>>>((const float*)x, m, w.k, g.tn, xs, us, xs_lo);
         break;
-    case CLQ_X_F16: prep_x_kernel<__half><<<prep_grid, 256, 0, stream>>>((const __half*)x, m, w.k, g.tn, xs, us); break;
+    case CLQ_X_BF16:
+        prep_x_kernel<__nv_bfloat16><<<prep_grid, 256, 0, stream>>>((const __nv_bfloat16*)x, m, w.k, g.tn, xs, us,
+                                                                     xs_lo);
+        break;
+    case CLQ_X_F16:
+        prep_x_kernel<__half><<<prep_grid, 256, 0, stream>>>((const __half*)x, m, w.k, g.tn, xs, us, xs_lo);
+        break;
     default: return cudaErrorInvalidValue;
     }
     if ((e = cudaGetLastError()) != cudaSuccess) return e;
@@ -935,6 +1103,8 @@ cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int
     P.ldo = ldo;
     P.tn = g.tn;
     P.kb_per_split = g.kb_per_split;
+    P.stages = g.stages;
+    P.xs_lo = xs_lo;
     P.err = err;
     dim3 grid((unsigned)g.token_tiles, (unsigned)g.row_tiles, (unsigned)g.splits);
     auto launch = [&](auto kern) -> cudaError_t {
@@ -970,10 +1140,10 @@ cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int
         e = cudaGetLastError();
     } else {
         switch (w.dtype) {
-        case kQ4_K: e = launch(gemm_tc_kernel<kQ4_K>); break;
-        case kQ6_K: e = launch(gemm_tc_kernel<kQ6_K>); break;
-        case kQ4_0: e = launch(gemm_tc_kernel<kQ4_0>); break;
-        case kQ8_0: e = launch(gemm_tc_kernel<kQ8_0>); break;
+        case kQ4_K: e = g.exact ? launch(gemm_tc_kernel<kQ4_K, true>) : launch(gemm_tc_kernel<kQ4_K, false>); break;
+        case kQ6_K: e = g.exact ? launch(gemm_tc_kernel<kQ6_K, true>) : launch(gemm_tc_kernel<kQ6_K, false>); break;
+        case kQ4_0: e = g.exact ? launch(gemm_tc_kernel<kQ4_0, true>) : launch(gemm_tc_kernel<kQ4_0, false>); break;
+        case kQ8_0: e = g.exact ? launch(gemm_tc_kernel<kQ8_0, true>) : launch(gemm_tc_kernel<kQ8_0, false>); break;
         default: return cudaErrorInvalidValue;
         }
     }

@@ -11,8 +11,7 @@
 namespace clq {
 namespace {
 
-// Activation rows from which the tensor-core GEMM replaces the GEMV when the
-// activations are 16-bit or the caller accepts fp16 rounding (CLQ_MATH_FAST).
+// Activation rows from which the tensor-core GEMM replaces the GEMV.
 int64_t gemm_min_m() {
     static int64_t v = -1;
     if (v < 0) {
@@ -46,15 +45,23 @@ cudaError_t keep_pool_memory() {
     return cudaSuccess;
 }
 
+// Every request of at least CLQ_GEMM_MIN_M rows: fp32 activations without
+// CLQ_MATH_FAST take the exact form (fp32-class products), 16-bit ones (or
+// CLQ_MATH_FAST) the fp16-operand form unless CLQ_MATH_EXACT asks otherwise.
 bool uses_gemm_tc(const WeightView& w, int xtype, int64_t m, unsigned flags) {
-    const bool sixteen_bit = xtype != CLQ_X_F32 || (flags & CLQ_MATH_FAST);
-    return sixteen_bit && m >= gemm_min_m() && gemm_tc_supported(w, m);
+    (void)xtype;
+    (void)flags;
+    return m >= gemm_min_m() && gemm_tc_supported(w, m);
+}
+bool gemm_exact(int xtype, unsigned flags) {
+    return (flags & CLQ_MATH_EXACT) || (xtype == CLQ_X_F32 && !(flags & CLQ_MATH_FAST));
 }
 
 cudaError_t launch_linear(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
                           float* out, int64_t ldo, unsigned flags, cudaStream_t stream) {
     if (uses_gemm_tc(w, xtype, m, flags)) {
-        const GemmPlan g = plan_gemm_tc(w.dtype, rows, w.k, m);
+        const bool exact = gemm_exact(xtype, flags);
+        const GemmPlan g = plan_gemm_tc(w.dtype, rows, w.k, m, exact, exact && xtype == CLQ_X_F32);
         cudaError_t e = keep_pool_memory();
         if (e != cudaSuccess) return e;
         void* scratch = nullptr;

@@ -136,3 +136,32 @@ def test_256_row_q4k_kernels(mode):
     proc = subprocess.run([sys.executable, "-c", _MODE_CHECK.format(root=root)], capture_output=True, text=True,
                           timeout=600, env={**os.environ, "CLQ_GEMM_TMA": mode})
     assert proc.returncode == 0 and proc.stdout.strip().endswith("ok"), proc.stderr[-3000:]
+
+
+@pytest.mark.parametrize("dtype", ["q4_k", "q6_k", "q4_0", "q8_0"])
+@pytest.mark.parametrize("n,k,m", [(300, 1024, 64), (1024, 4096, 200)])
+def test_exact_gemm_meets_the_reference_bound(cuda, clq, synth, oracle, dtype, n, k, m):
+    """fp32 activations with default flags take the exact GEMM (weights and
+    activations split into fp16 hi + scaled lo parts, a second accumulator
+    for the cross terms): the reference's own bound 1e-5 + 1e-5 * sum|x*w|
+    (tests/local/packed.lisp:5-12), on uniform codes and on N(0, 0.02)
+    weights quantized to the K formats."""
+    torch = cuda
+    if dtype in ("q4_k", "q6_k"):
+        data = getattr(synth, "quantize_" + dtype)(synth.normal_weight(n, k, seed=n + k))
+    else:
+        data = synth.packed_blocks(dtype, n, k, seed=n + k + m)
+    x = synth.activations(m, k, seed=m + 1)
+    x[0] *= np.float32(1e-20)
+    x[1] *= np.float32(1e20)
+    store = clq.Store(dtype, n, k, data)
+    out = store.linear(torch.from_numpy(x).cuda()).cpu().numpy().astype(np.float64)
+    ref, mag = oracle.matmul_f64(dtype, x, data, n)
+    assert np.all(np.isfinite(out))
+    assert np.all(np.abs(out - ref) <= 1e-5 * mag + 1e-37), np.max(np.abs(out - ref) / (mag + 1e-37))
+    # bf16 activations with CLQ_MATH_EXACT take the same form
+    xb = torch.from_numpy(x[2:]).cuda().to(torch.bfloat16)
+    outb = store.linear(xb, flags=4).cpu().numpy().astype(np.float64)
+    refb, magb = oracle.matmul_f64(dtype, xb.float().cpu().numpy(), data, n)
+    assert np.all(np.abs(outb - refb) <= 1e-5 * magb + 1e-37)
+    store.close()
