@@ -683,7 +683,7 @@ def measure(args, torch, rank, world, local, dist):
                 "bound": "tensor", "kernel": ("Q4_K linears (activation prep + exact tcgen05 GEMM: three fp16 MMAs "
                                               "per K step + split-K reduce), " if exact else
                                               "Q4_K linears (activation prep + tcgen05 GEMM + split-K reduce), ")
-                                            "M=%d" % m,
+                                             + "M=%d" % m,
                 "achieved": round(k_tf, 1), "peak": tpeak, "peak_kind": tpeak_kind + " (burst, dense bf16)",
                 "unit": "TFLOP/s", "frac": round(k_tf / tpeak, 4), "traffic": None,
                 "algorithmic_flops_per_launch": round(k_flops), "us_per_launch": round(k_ms * 1e3, 3)}
