@@ -509,7 +509,8 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzle atoms
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    const int tn = P.tn, NS = P.stages;
+    // the fp16-operand form always plans kStages stages: a compile-time depth
+    const int tn = P.tn, NS = EXACT ? P.stages : kStages;
     const bool xlo = EXACT && P.xs_lo != nullptr;
     constexpr uint32_t kA = (EXACT ? 2u : 1u) * kTM * 128;  // per stage: hi (and lo) weight tiles
     const uint32_t kBt = (uint32_t)tn * 128, kB = (xlo ? 2u : 1u) * kBt;
@@ -1042,7 +1043,7 @@ GemmPlan plan_gemm_tc(int dtype, int64_t rows, int64_t k, int64_t m, bool exact,
     g.part_bytes = g.splits > 1 ? (size_t)g.splits * m * rows * sizeof(float) : 0;
     const size_t per_stage = (size_t)kTM * 128 * (exact ? 2 : 1) + (size_t)g.tn * 128 * (g.xlo ? 2 : 1);
     g.stages = kStages;
-    while (g.stages > 2 && 1024 + (size_t)g.stages * per_stage + 256 > 227 * 1024) g.stages--;
+    while (exact && g.stages > 2 && 1024 + (size_t)g.stages * per_stage + 256 > 227 * 1024) g.stages--;
     g.smem = 1024 + (size_t)g.stages * per_stage + 256;
     return g;
 }
