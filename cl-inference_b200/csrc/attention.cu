@@ -8,29 +8,32 @@
 // group ([n_ctx][kv_heads][ceil(head_dim / 32)]), the reference buffers'
 // order, so a position's row of every head is one contiguous span.
 //
-// Attention is split over positions (flash-decoding): a CTA takes one query
-// row, one KV head and a range of positions, reads each key and value row
-// once for all the query heads of that KV head (coalesced: lanes over the
-// head dimension), and leaves the range's softmax maximum, sum and weighted
-// value sum; a second kernel merges the ranges of each (row, head).  The
-// cache is read once per query row -- the step is bound by HBM.
+// Attention is split over positions (flash-decoding): a CTA takes a block of
+// query rows, one KV head and a range of 32 or 64 positions, stages each
+// key and value row of the range once (bulk copies for f32 rows) for all the
+// query heads of that KV head and all the rows of the block, and leaves the
+// range's softmax maximum, sum and weighted value sum; a second launch merges
+// the ranges of each (row, head).  A prefix that fits one range is written
+// directly.  The cache is read once per block of query rows.
 #include <cfloat>
 #include <cmath>
 #include <cstdint>
 
+#include <cstdlib>
 #include <cuda_runtime.h>
 
 #include "../../include/clq.h"
 #include "clq_internal.h"
+#include "pipeline.cuh"
 
 namespace clq {
 namespace {
 
 constexpr int kQ8Group = 32;          // local/kv-cache.lisp:20
-constexpr int kAttnThreads = 128;     // 4 warps per CTA
+constexpr int kMergeThreads = 256;
 constexpr int kMaxGroup = 16;         // query heads per KV head
-constexpr int kSplitRows = 64;        // positions per CTA, staged in shared memory
-constexpr int kMaxSplits = 1024;      // position ranges merged per (row, head)
+// A CTA stages SR = 32 or 64 positions and runs SR / 8 warps (8 positions each).
+constexpr int kMaxSplits = 2048;      // position ranges merged per (row, head)
 constexpr int kMaxHeadDim = 256;
 
 // ---- the Q8 codec --------------------------------------------------------
@@ -148,30 +151,45 @@ struct AttnParams {
     const void* values;
     const float* kscale;   // Q8: [n_ctx][kvh][groups]
     const float* vscale;
+    int64_t count;         // query rows
     int64_t end;           // keys in the prefix
     int64_t query_start;   // position of query row 0
     int n_heads, kvh, hd, groups;
+    int gshift;            // log2 of the query heads per KV head
+    int rows;              // query rows per CTA: rows << gshift query vectors
     int splits;
     int64_t per_split;
     float scale;           // 1 / sqrt(hd), rounded to f32
-    float* part;           // [count][n_heads][splits][hd + 2]: weighted sum, then max, sum
+    float* acc;            // [count][n_heads][splits][hd]: the splits' weighted value sums
+    float2* ml;            // [count][n_heads][splits]: their (max, sum)
+    float* out;            // one split: the output rows, stride ldo
+    int64_t ldo;
+    int bulk;              // f32 rows staged by bulk copies
+    int* err;              // device status word (a staging wait that gave up)
 };
 
-// The split's rows of one KV head, keys and values, into shared memory as
-// f32: every thread issues its 16-byte loads (4 f32 or 16 codes) before any
-// is used, so the split costs about one memory round trip.
-template <bool Q8>
+// Staged key rows are hd + 16 floats apart, so that the two positions of a
+// quarter warp (4 lanes each, float4 columns 16 apart) fall in distinct banks.
+__host__ __device__ constexpr int key_ld(int hd) { return hd + 16; }
+// Query rows in shared memory: hd rounded up to 4 floats (16-byte rows).
+__host__ __device__ constexpr int query_ld(int hd) { return (hd + 3) & ~3; }
+
+// The split's rows of one KV head, keys or values, into shared memory as f32
+// rows LD floats apart: every thread issues its 16-byte loads (4 f32 or 16
+// codes) before any is used, so the split costs about one memory round trip.
+template <bool Q8, int T>
 __device__ __forceinline__ void stage_rows(const AttnParams& P, const void* buf, const float* scl, int64_t p0, int np,
-                                           int kv, float* dst) {
+                                           int kv, float* dst, int ld) {
     const int hd = P.hd;
     if (hd % (Q8 ? 16 : 4)) {  // rows off the 16-byte grid: element by element
-        for (int e = threadIdx.x; e < np * hd; e += kAttnThreads) {
+        for (int e = threadIdx.x; e < np * hd; e += T) {
             const int j = e / hd, d = e - j * hd;
             const int64_t slot = (p0 + j) * P.kvh + kv;
             if constexpr (Q8) {
-                dst[e] = q8_decode(reinterpret_cast<const int8_t*>(buf)[slot * hd + d], scl[slot * P.groups + d / kQ8Group]);
+                dst[j * ld + d] =
+                    q8_decode(reinterpret_cast<const int8_t*>(buf)[slot * hd + d], scl[slot * P.groups + d / kQ8Group]);
             } else {
-                dst[e] = reinterpret_cast<const float*>(buf)[slot * hd + d];
+                dst[j * ld + d] = reinterpret_cast<const float*>(buf)[slot * hd + d];
             }
         }
         return;
@@ -180,12 +198,12 @@ __device__ __forceinline__ void stage_rows(const AttnParams& P, const void* buf,
     constexpr int B = 8;
     if constexpr (Q8) {
         const int per_row = hd / 16, n = np * per_row;
-        for (int e0 = threadIdx.x; e0 < n; e0 += B * kAttnThreads) {
+        for (int e0 = threadIdx.x; e0 < n; e0 += B * T) {
             uint4 w[B];
             float sc[B];
 #pragma unroll
             for (int b = 0; b < B; b++) {
-                const int e = e0 + b * kAttnThreads;
+                const int e = e0 + b * T;
                 if (e < n) {
                     const int j = e / per_row, c = e - j * per_row;
                     const int64_t slot = (p0 + j) * P.kvh + kv;
@@ -195,11 +213,11 @@ __device__ __forceinline__ void stage_rows(const AttnParams& P, const void* buf,
             }
 #pragma unroll
             for (int b = 0; b < B; b++) {
-                const int e = e0 + b * kAttnThreads;
+                const int e = e0 + b * T;
                 if (e < n) {
                     const int j = e / per_row, c = e - j * per_row;
                     const uint32_t ws[4] = {w[b].x, w[b].y, w[b].z, w[b].w};
-                    float* o = dst + j * hd + c * 16;
+                    float* o = dst + j * ld + c * 16;
 #pragma unroll
                     for (int i = 0; i < 16; i++) o[i] = q8_decode((int8_t)(ws[i >> 2] >> (8 * (i & 3))), sc[b]);
                 }
@@ -207,11 +225,11 @@ __device__ __forceinline__ void stage_rows(const AttnParams& P, const void* buf,
         }
     } else {
         const int per_row = hd / 4, n = np * per_row;
-        for (int e0 = threadIdx.x; e0 < n; e0 += B * kAttnThreads) {
+        for (int e0 = threadIdx.x; e0 < n; e0 += B * T) {
             float4 v[B];
 #pragma unroll
             for (int b = 0; b < B; b++) {
-                const int e = e0 + b * kAttnThreads;
+                const int e = e0 + b * T;
                 if (e < n) {
                     const int j = e / per_row, c = e - j * per_row;
                     const int64_t slot = (p0 + j) * P.kvh + kv;
@@ -220,165 +238,306 @@ __device__ __forceinline__ void stage_rows(const AttnParams& P, const void* buf,
             }
 #pragma unroll
             for (int b = 0; b < B; b++) {
-                const int e = e0 + b * kAttnThreads;
+                const int e = e0 + b * T;
                 if (e < n) {
                     const int j = e / per_row, c = e - j * per_row;
-                    *reinterpret_cast<float4*>(dst + j * hd + c * 4) = v[b];
+                    *reinterpret_cast<float4*>(dst + j * ld + c * 4) = v[b];
                 }
             }
         }
     }
 }
 
-// CTA (split, kv head, query row).  The split's unmasked positions (key
-// position <= query_start + row) are staged; scores s = (q . k) * scale for
-// the group's query heads; then the split's maximum m, the sum l of
-// exp(s - m) and the sum of exp(s - m) * v.
-template <bool Q8, int G>
-__global__ void __launch_bounds__(kAttnThreads) attend_split_kernel(const AttnParams P) {
+__device__ __forceinline__ void fma4(float4& a, float p, const float4& x) {
+    a.x = fmaf(p, x.x, a.x);
+    a.y = fmaf(p, x.y, a.y);
+    a.z = fmaf(p, x.z, a.z);
+    a.w = fmaf(p, x.w, a.w);
+}
+
+// CTA (split, KV head, block of query rows): the QV = rows * G query vectors
+// of `rows` consecutive query rows and the G query heads of one KV head.  The
+// split's key and value rows are staged once -- f32 rows by bulk copies on one
+// barrier, otherwise by 16-byte vector loads -- and serve every query vector:
+//   scores   4 lanes per position, each a quarter of the head dimension
+//            (float4 columns 16 apart), summed by two shuffles, times scale;
+//   softmax  a warp per query vector over its unmasked positions (key
+//            position <= query_start + row): m = max, p = exp(s - m), l = sum p;
+//   values   a thread per (query vector, 4 dimensions) and share of the
+//            positions; the shares summed in a fixed order.
+// One split writes acc / l to the output rows; otherwise (acc, m, l) go to
+// scratch for attend_merge_kernel.  HD: the head dimension when it is 64 or
+// 128 (constant strides and trip counts), 0 for any other.  Under
+// programmatic dependent launch nothing is read before the previous grid
+// completes.
+template <bool Q8, int QV, int HD, int SR>
+__global__ void __launch_bounds__(SR * 4, SR == 32 ? 4 : 2) attend_split_kernel(const AttnParams P) {
     extern __shared__ __align__(16) float sh[];
+    constexpr int T = SR * 4, NW = T / 32;  // one pass of 8 positions per warp covers a split
     const int split = blockIdx.x, kv = blockIdx.y;
-    const int64_t row = blockIdx.z;
-    const int hd = P.hd;
+    const int64_t r0 = (int64_t)blockIdx.z * P.rows;
+    const int hd = HD ? HD : P.hd, ld = key_ld(hd), qld = query_ld(hd);
+    const int gs = P.gshift, G = 1 << gs;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int NW = kAttnThreads / 32;
-    float* qs = sh;                                 // [G][hd]
-    float* sc = qs + G * hd;                        // [G][kSplitRows]
-    float* ks = sc + G * kSplitRows;                // [kSplitRows][hd]
-    float* vs = ks + kSplitRows * hd;               // [kSplitRows][hd]
-    const int64_t last = P.query_start + row + 1 < P.end ? P.query_start + row + 1 : P.end;  // causal
+    uint64_t* bar = reinterpret_cast<uint64_t*>(sh);  // the bulk copies' barrier (16 bytes)
+    float* qs = sh + 4;                     // [QV][qld]
+    float* sc = qs + QV * qld;              // [QV][SR]: scores, then weights
+    float* mls = sc + QV * SR;      // [QV][4]: max, sum
+    float* ks = mls + 4 * QV;               // [SR][ld]; after the scores, value partials
+    float* vs = ks + SR * ld;       // [SR][hd]
+
+    // positions [p0, p1) of this split that some row of the block may attend
+    const int64_t last_row = (r0 + P.rows < P.count ? r0 + P.rows : P.count) - 1;
+    const int64_t lim = P.query_start + last_row + 1 < P.end ? P.query_start + last_row + 1 : P.end;  // causal
     const int64_t p0 = (int64_t)split * P.per_split;
-    int64_t p1 = p0 + P.per_split;
-    if (p1 > last) p1 = last;
+    const int64_t p1 = p0 + P.per_split < lim ? p0 + P.per_split : lim;
     const int np = p1 > p0 ? (int)(p1 - p0) : 0;
 
-    for (int e = threadIdx.x; e < G * hd; e += kAttnThreads) {
-        const int g = e / hd, d = e - g * hd;
-        qs[e] = P.q[row * P.q_ps + (int64_t)(kv * G + g) * hd + d];
+    const bool bulk = !Q8 && P.bulk;
+    if (bulk && threadIdx.x == 0) {
+        pipe::mbar_init(bar, 1);
+        pipe::mbar_init_fence();
     }
-    stage_rows<Q8>(P, P.keys, P.kscale, p0, np, kv, ks);
-    stage_rows<Q8>(P, P.values, P.vscale, p0, np, kv, vs);
-    __syncthreads();
-
-    // scores: a warp per position, lanes over the head dimension
-    for (int j = warp; j < np; j += NW) {
-        float dot[G];
-#pragma unroll
-        for (int g = 0; g < G; g++) dot[g] = 0.f;
-        for (int d = lane; d < hd; d += 32) {
-            const float k = ks[j * hd + d];
-#pragma unroll
-            for (int g = 0; g < G; g++) dot[g] = fmaf(qs[g * hd + d], k, dot[g]);
-        }
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            float v = dot[g];
-#pragma unroll
-            for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
-            if (lane == 0) sc[g * kSplitRows + j] = __fmul_rn(v, P.scale);
+    pipe::grid_dependency_wait();  // the queries and the cache rows may come from the previous kernels
+    if (bulk) {
+        __syncthreads();
+        if (warp == 0 && np > 0) {  // every row of the split in flight on one barrier
+            const uint32_t rb = (uint32_t)hd * 4u;
+            if (lane == 0) pipe::mbar_arrive_tx(bar, 2u * (uint32_t)np * rb);
+            __syncwarp();
+            for (int j = lane; j < np; j += 32) {
+                const int64_t slot = (p0 + j) * P.kvh + kv;
+                pipe::bulk_copy(ks + j * ld, reinterpret_cast<const float*>(P.keys) + slot * hd, rb, bar);
+                pipe::bulk_copy(vs + j * hd, reinterpret_cast<const float*>(P.values) + slot * hd, rb, bar);
+            }
         }
     }
+    for (int e = threadIdx.x; e < QV * hd; e += T) {
+        const int v = e / hd, d = e - v * hd;
+        const int64_t row = r0 + (v >> gs);
+        qs[v * qld + d] = row < P.count ? P.q[row * P.q_ps + (int64_t)(kv * G + (v & (G - 1))) * hd + d] : 0.f;
+    }
+    if (bulk) {
+        if (np > 0 && !pipe::mbar_wait(bar, 0, P.err)) pipe::mbar_drain(bar, 0);
+    } else {
+        stage_rows<Q8, T>(P, P.keys, P.kscale, p0, np, kv, ks, ld);
+        stage_rows<Q8, T>(P, P.values, P.vscale, p0, np, kv, vs, hd);
+    }
+    __syncthreads();
+    pipe::allow_dependents();
+
+    // scores: position j = 8 warp + lane / 4, lane c = lane % 4 takes the
+    // float4 columns 16 i + 4 c (and the scalar tail d = c mod 4)
+    {
+        const int c = lane & 3, j = warp * 8 + (lane >> 2);
+        const int nfull = (hd & 3) ? 0 : hd >> 4;
+        const float* kr = ks + j * ld;
+        float dot[QV];
+#pragma unroll
+        for (int v = 0; v < QV; v++) dot[v] = 0.f;
+        for (int i = 0; i < nfull; i++) {
+            const int d = 16 * i + 4 * c;
+            const float4 k = *reinterpret_cast<const float4*>(kr + d);
+#pragma unroll
+            for (int v = 0; v < QV; v++) {
+                const float4 q = *reinterpret_cast<const float4*>(qs + v * qld + d);
+                dot[v] = fmaf(q.x, k.x, dot[v]);
+                dot[v] = fmaf(q.y, k.y, dot[v]);
+                dot[v] = fmaf(q.z, k.z, dot[v]);
+                dot[v] = fmaf(q.w, k.w, dot[v]);
+            }
+        }
+        for (int d = 16 * nfull + c; d < hd; d += 4) {
+            const float k = kr[d];
+#pragma unroll
+            for (int v = 0; v < QV; v++) dot[v] = fmaf(qs[v * qld + d], k, dot[v]);
+        }
+#pragma unroll
+        for (int v = 0; v < QV; v++) {
+            dot[v] += __shfl_xor_sync(0xffffffffu, dot[v], 1);
+            dot[v] += __shfl_xor_sync(0xffffffffu, dot[v], 2);
+            if ((v & 3) == c && j < np) sc[v * SR + j] = __fmul_rn(dot[v], P.scale);
+        }
+    }
     __syncthreads();
 
-    // the split's maximum and sum per query head: warp g handles heads g, g + NW, ...
-    for (int g = warp; g < G; g += NW) {
+    // softmax pieces per query vector: a warp each
+    for (int v = warp; v < QV; v += NW) {
+        const int64_t row = r0 + (v >> gs);
+        int nv = 0;  // this vector's unmasked positions of the split
+        if (row < P.count) {
+            const int64_t lv = P.query_start + row + 1 < P.end ? P.query_start + row + 1 : P.end;
+            nv = lv - p0 < 0 ? 0 : (lv - p0 > np ? np : (int)(lv - p0));
+        }
+        float* s = sc + v * SR;
         float m = -INFINITY;
-        for (int j = lane; j < np; j += 32) m = fmaxf(m, sc[g * kSplitRows + j]);
+        for (int j = lane; j < nv; j += 32) m = fmaxf(m, s[j]);
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
         float l = 0.f;
-        for (int j = lane; j < np; j += 32) {
-            const float p = expf(sc[g * kSplitRows + j] - m);
-            sc[g * kSplitRows + j] = p;
+        for (int j = lane; j < SR; j += 32) {
+            const float p = j < nv ? expf(s[j] - m) : 0.f;
+            s[j] = p;
             l += p;
         }
 #pragma unroll
         for (int off = 16; off > 0; off >>= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
         if (lane == 0) {
-            float* out = P.part + (((row * P.n_heads) + kv * G + g) * P.splits + split) * (int64_t)(hd + 2);
-            out[hd] = m;
-            out[hd + 1] = l;
+            mls[4 * v] = m;
+            mls[4 * v + 1] = l;
+            if (P.splits > 1 && row < P.count)
+                P.ml[(row * P.n_heads + kv * G + (v & (G - 1))) * P.splits + split] = make_float2(m, l);
         }
     }
     __syncthreads();
 
-    // weighted value sums: each thread owns dimensions d = threadIdx.x, + 128, ...
-    for (int d = threadIdx.x; d < hd; d += kAttnThreads) {
-        float acc[G];
-#pragma unroll
-        for (int g = 0; g < G; g++) acc[g] = 0.f;
-        for (int j = 0; j < np; j++) {
-            const float v = vs[j * hd + d];
-#pragma unroll
-            for (int g = 0; g < G; g++) acc[g] = fmaf(sc[g * kSplitRows + j], v, acc[g]);
+    // weighted value sums: W = QV x (hd / cw) columns of cw dimensions, each
+    // over the positions j = share (mod PS); the PS shares then summed in order
+    const int cw = (hd & 3) ? 1 : 4, nc = hd / cw, W = QV * nc;
+    const int PS = W >= T ? 1 : T / W;
+    float4* red = reinterpret_cast<float4*>(ks);  // [PS][W], the keys being done with
+    auto emit = [&](int w, float4 a) {
+        const int v = w / nc, col = w - v * nc;
+        const int64_t row = r0 + (v >> gs);
+        if (row >= P.count) return;
+        const int head = kv * G + (v & (G - 1));
+        const float o[4] = {a.x, a.y, a.z, a.w};
+        if (P.splits == 1) {
+            const float l = mls[4 * v + 1];
+            float* dst = P.out + row * P.ldo + (int64_t)head * hd + col * cw;
+            for (int i = 0; i < cw; i++) dst[i] = o[i] / l;
+        } else {
+            float* dst = P.acc + ((row * P.n_heads + head) * P.splits + split) * (int64_t)hd + col * cw;
+            if (cw == 4) *reinterpret_cast<float4*>(dst) = a;
+            else dst[0] = o[0];
         }
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            P.part[(((row * P.n_heads) + kv * G + g) * P.splits + split) * (int64_t)(hd + 2) + d] = acc[g];
+    };
+    for (int t = threadIdx.x; t < PS * W; t += T) {
+        const int w = t % W, ps = t / W;
+        const int v = w / nc, col = w - v * nc;
+        const float* pv = sc + v * SR;
+        float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (cw == 4) {
+            for (int j = ps; j < np; j += PS) fma4(a, pv[j], *reinterpret_cast<const float4*>(vs + j * hd + 4 * col));
+        } else {
+            for (int j = ps; j < np; j += PS) a.x = fmaf(pv[j], vs[j * hd + col], a.x);
+        }
+        if (PS > 1) red[t] = a;
+        else emit(w, a);
+    }
+    if (PS > 1) {
+        __syncthreads();
+        for (int w = threadIdx.x; w < W; w += T) {
+            float4 a = red[w];
+            for (int ps = 1; ps < PS; ps++) {
+                const float4 b = red[ps * W + w];
+                a.x += b.x;
+                a.y += b.y;
+                a.z += b.z;
+                a.w += b.w;
+            }
+            emit(w, a);
         }
     }
 }
 
-size_t attend_smem(int G, int hd) {
-    return ((size_t)G * hd + (size_t)G * kSplitRows + 2 * (size_t)kSplitRows * hd) * sizeof(float);
+size_t attend_smem(int QV, int hd, int SR) {
+    return 16 + ((size_t)QV * query_ld(hd) + (size_t)QV * SR + 4 * (size_t)QV + (size_t)SR * key_ld(hd) + (size_t)SR * hd) *
+                    sizeof(float);
 }
 
-// Merges the splits of (query row, head) for a slice of 32 dimensions (one
-// warp per CTA): M = max m_s, output sum_s exp(m_s - M) acc_s / sum_s
-// exp(m_s - M) l_s into out[row][head * hd + d].  Every load is issued before
-// any is used (the kernel is one round trip to L2, not one per split).
-__global__ void __launch_bounds__(32) attend_merge_kernel(const float* __restrict__ part, int n_heads, int hd,
-                                                          int splits, float* __restrict__ out, int64_t ldo) {
+// CTA per (head, query row): thread (column, split group) first puts the
+// weighted sums of its first eight splits in flight; meanwhile every split's
+// (m, l) gives M = max m_s over the non-empty splits, the weights
+// w_s = exp(m_s - M) (0 for an empty split) and L = sum w_s l_s.  Each thread
+// sums w_s acc_s over its splits, the groups are summed in order, and the
+// output is acc / L.
+__global__ void __launch_bounds__(kMergeThreads) attend_merge_kernel(const float* __restrict__ acc,
+                                                                     const float2* __restrict__ ml, int n_heads, int hd,
+                                                                     int splits, float* __restrict__ out, int64_t ldo) {
     __shared__ float wgt[kMaxSplits];
     __shared__ float lsum[kMaxSplits];
-    const int head = blockIdx.x, lane = threadIdx.x;
+    __shared__ float4 part[kMergeThreads];
+    __shared__ float red[kMergeThreads / 32];
+    constexpr int NW = kMergeThreads / 32, B = 8;
+    static_assert(kMaxHeadDim <= kMergeThreads, "one (column, split group) per thread");
+    const int head = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int64_t row = blockIdx.y;
-    const int d = blockIdx.z * 32 + lane;
-    const int64_t stride = hd + 2;
-    const float* base = part + ((row * n_heads) + head) * (int64_t)splits * stride;
-    constexpr int B = 16;
-    float m = -INFINITY;
-    for (int s0 = 0; s0 < splits; s0 += 32 * B) {
-        float lv[B], mv[B];
+    const int64_t base = (row * n_heads + head) * (int64_t)splits;
+    const int cw = (hd & 3) ? 1 : 4, nc = hd / cw, SG = kMergeThreads / nc;
+    const int col = threadIdx.x % nc, sg = threadIdx.x / nc;
+    const bool active = sg < SG;
+    const float* src = acc + base * hd + col * cw;
+    auto load = [&](float4* x, int s0) {
 #pragma unroll
         for (int b = 0; b < B; b++) {
-            const int s = s0 + b * 32 + lane;
-            lv[b] = s < splits ? base[s * stride + hd + 1] : 0.f;
-            mv[b] = s < splits ? base[s * stride + hd] : -INFINITY;
-        }
-#pragma unroll
-        for (int b = 0; b < B; b++) {
-            const int s = s0 + b * 32 + lane;
-            if (s < splits) {
-                lsum[s] = lv[b];
-                wgt[s] = lv[b] > 0.f ? mv[b] : -INFINITY;
-                m = fmaxf(m, wgt[s]);
+            const int s = s0 + b * SG;
+            x[b] = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (active && s < splits) {
+                if (cw == 4) x[b] = *reinterpret_cast<const float4*>(src + (int64_t)s * hd);
+                else x[b].x = src[(int64_t)s * hd];
             }
         }
+    };
+
+    pipe::grid_dependency_wait();  // the split kernel's partials
+    pipe::allow_dependents();
+    float4 x[B];
+    load(x, sg);
+    float m = -INFINITY;
+    for (int s = threadIdx.x; s < splits; s += kMergeThreads) {
+        const float2 v = ml[base + s];
+        lsum[s] = v.y;
+        wgt[s] = v.y > 0.f ? v.x : -INFINITY;
+        m = fmaxf(m, wgt[s]);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    __syncwarp();
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    m = red[0];
+#pragma unroll
+    for (int w = 1; w < NW; w++) m = fmaxf(m, red[w]);
+    __syncthreads();
     float L = 0.f;
-    for (int s = lane; s < splits; s += 32) {
+    for (int s = threadIdx.x; s < splits; s += kMergeThreads) {
         const float w = lsum[s] > 0.f ? expf(wgt[s] - m) : 0.f;
         wgt[s] = w;
         L = fmaf(w, lsum[s], L);
     }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) L += __shfl_xor_sync(0xffffffffu, L, off);
-    __syncwarp();
-    if (d >= hd) return;
-    float a = 0.f;
-    for (int s0 = 0; s0 < splits; s0 += B) {
-        float v[B];
+    if (lane == 0) red[warp] = L;
+    __syncthreads();
+    L = red[0];
 #pragma unroll
-        for (int b = 0; b < B; b++) v[b] = s0 + b < splits ? base[(s0 + b) * stride + d] : 0.f;
+    for (int w = 1; w < NW; w++) L += red[w];
+
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = sg;; s0 += B * SG) {  // splits s0, s0 + SG, ... in order
 #pragma unroll
-        for (int b = 0; b < B; b++)
-            if (s0 + b < splits) a = fmaf(wgt[s0 + b], v[b], a);
+        for (int b = 0; b < B; b++) {
+            const int s = s0 + b * SG;
+            if (active && s < splits) fma4(a, wgt[s], x[b]);
+        }
+        if (s0 + B * SG >= splits) break;
+        load(x, s0 + B * SG);
     }
-    out[row * ldo + (int64_t)head * hd + d] = a / L;
+    if (active) part[threadIdx.x] = a;
+    __syncthreads();
+    if (threadIdx.x < nc) {
+        a = part[threadIdx.x];
+        for (int g = 1; g < SG; g++) {
+            const float4 b = part[g * nc + threadIdx.x];
+            a.x += b.x;
+            a.y += b.y;
+            a.z += b.z;
+            a.w += b.w;
+        }
+        const float o[4] = {a.x, a.y, a.z, a.w};
+        float* dst = out + row * ldo + (int64_t)head * hd + threadIdx.x * cw;
+        for (int i = 0; i < cw; i++) dst[i] = o[i] / L;
+    }
 }
 
 __global__ void fill_kernel(float* __restrict__ p, int64_t n, float v) {
@@ -391,24 +550,61 @@ cudaError_t attend_smem_limit(Kern kern, size_t smem) {
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
 }
 
-// The split kernel for G query heads per KV head (1, 2, 4, 8 or 16).
-template <bool Q8>
-cudaError_t launch_split(int G, dim3 grid, size_t smem, cudaStream_t s, const AttnParams& P) {
-    cudaError_t e = cudaErrorNotSupported;
-    switch (G) {
-#define CLQ_SPLIT_CASE(n)                                                        \
-    case n:                                                                     \
-        e = attend_smem_limit(attend_split_kernel<Q8, n>, smem);                \
-        if (e == cudaSuccess) attend_split_kernel<Q8, n><<<grid, kAttnThreads, smem, s>>>(P); \
-        break;
-        CLQ_SPLIT_CASE(1)
-        CLQ_SPLIT_CASE(2)
-        CLQ_SPLIT_CASE(4)
-        CLQ_SPLIT_CASE(8)
-        CLQ_SPLIT_CASE(16)
-#undef CLQ_SPLIT_CASE
+// KERN<<<GRID, THREADS, SMEM, S>>>(ARGS...), a programmatic dependent launch
+// unless CLQ_PDL=0.
+template <typename... Args>
+cudaError_t launch_pdl(void (*kern)(Args...), dim3 grid, int threads, size_t smem, cudaStream_t s, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(threads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = gemv_pdl_enabled() ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+template <bool Q8, int QV, int HD, int SR>
+cudaError_t launch_split_sr(dim3 grid, size_t smem, cudaStream_t s, const AttnParams& P) {
+    const cudaError_t e = attend_smem_limit(attend_split_kernel<Q8, QV, HD, SR>, smem);
+    return e != cudaSuccess ? e : launch_pdl(attend_split_kernel<Q8, QV, HD, SR>, grid, SR * 4, smem, s, P);
+}
+template <bool Q8, int QV, int HD>
+cudaError_t launch_split_hd(int sr, dim3 grid, size_t smem, cudaStream_t s, const AttnParams& P) {
+    return sr == 32 ? launch_split_sr<Q8, QV, HD, 32>(grid, smem, s, P) : launch_split_sr<Q8, QV, HD, 64>(grid, smem, s, P);
+}
+template <bool Q8, int QV>
+cudaError_t launch_split_qv(int sr, dim3 grid, size_t smem, cudaStream_t s, const AttnParams& P) {
+    switch (P.hd) {
+    case 64: return launch_split_hd<Q8, QV, 64>(sr, grid, smem, s, P);
+    case 128: return launch_split_hd<Q8, QV, 128>(sr, grid, smem, s, P);
+    default: return launch_split_hd<Q8, QV, 0>(sr, grid, smem, s, P);
     }
-    return e;
+}
+// The split kernel for QV query vectors (1, 2, 4, 8 or 16) and SR positions per CTA.
+template <bool Q8>
+cudaError_t launch_split(int QV, int sr, dim3 grid, size_t smem, cudaStream_t s, const AttnParams& P) {
+    switch (QV) {
+    case 1: return launch_split_qv<Q8, 1>(sr, grid, smem, s, P);
+    case 2: return launch_split_qv<Q8, 2>(sr, grid, smem, s, P);
+    case 4: return launch_split_qv<Q8, 4>(sr, grid, smem, s, P);
+    case 8: return launch_split_qv<Q8, 8>(sr, grid, smem, s, P);
+    case 16: return launch_split_qv<Q8, 16>(sr, grid, smem, s, P);
+    default: return cudaErrorNotSupported;
+    }
+}
+
+// CLQ_ATTN_BULK=0 stages f32 key and value rows with vector loads instead of
+// bulk copies.
+bool attn_bulk_enabled() {
+    static const bool on = [] {
+        const char* v = getenv("CLQ_ATTN_BULK");
+        return !(v && v[0] == '0');
+    }();
+    return on;
 }
 
 unsigned grid_for(int64_t work, int threads) {
@@ -666,35 +862,58 @@ int clq_attend_device(const float* q, int64_t count, int n_heads, int64_t q_pos_
     P.hd = c->hd;
     P.groups = c->groups;
     P.scale = 1.f / sqrtf((float)c->hd);  // local/blocks.lisp:311
-    // positions split so that the grid covers the SMs about twice, at most 64 a CTA
-    const int64_t ctas_per_split = (int64_t)c->kvh * count;
+    const int G = n_heads / c->kvh;
+    const bool q8 = c->type == CLQ_KV_Q8;
+    P.count = count;
+    P.bulk = !q8 && clq::attn_bulk_enabled() && c->hd % 4 == 0 && ((uintptr_t)kb | (uintptr_t)vb) % 16 == 0;
+    P.err = clq::device_status_word();
+    // query rows per CTA: up to 16 query vectors (rows x G) share one staging
+    int rows = 1;
+    while (rows * 2 * G <= 16 && rows < count) rows *= 2;
+    P.rows = rows;
+    while ((1 << P.gshift) < G) P.gshift++;
+    const int QV = rows * G;
+    const int64_t blocks = (count + rows - 1) / rows;
+    // positions per CTA: 32 (twice the CTAs, each with less to do) unless
+    // blocks of many query vectors over a long prefix, where the partials'
+    // traffic grows with the split count
+    int sr = QV <= 4 || end <= 1024 ? 32 : 64;
+    if ((end + sr - 1) / sr > clq::kMaxSplits) sr = 64;
+    // positions split so that the grid covers the SMs about twice, at most sr a CTA
+    const int64_t ctas_per_split = (int64_t)c->kvh * blocks;
     int64_t splits = (2 * (int64_t)clq::sm_count() + ctas_per_split - 1) / ctas_per_split;
-    const int64_t min_splits = (end + clq::kSplitRows - 1) / clq::kSplitRows;
+    const int64_t min_splits = (end + sr - 1) / sr;
     if (splits < min_splits) splits = min_splits;
     if (splits > (end + 15) / 16) splits = (end + 15) / 16 > min_splits ? (end + 15) / 16 : min_splits;
     if (splits > clq::kMaxSplits)
-        return clq::set_error(CLQ_ERR_UNSUPPORTED, "prefix %lld above %d positions", (long long)end,
-                              clq::kMaxSplits * clq::kSplitRows);
-    if (splits > 65535 || count > 65535) return kv_fail(CLQ_ERR_UNSUPPORTED, "too many query rows or positions for one launch");
+        return clq::set_error(CLQ_ERR_UNSUPPORTED, "prefix %lld above %d positions", (long long)end, clq::kMaxSplits * 64);
+    if (blocks > 65535 || count > 65535) return kv_fail(CLQ_ERR_UNSUPPORTED, "too many query rows for one launch");
     P.splits = (int)splits;
     P.per_split = (end + splits - 1) / splits;
-    float* part = nullptr;
-    cudaError_t e = clq::keep_pool_memory();
-    if (e == cudaSuccess) e = cudaMallocAsync((void**)&part, (size_t)count * n_heads * splits * (c->hd + 2) * sizeof(float), s);
-    if (e != cudaSuccess) return clq::set_error(CLQ_ERR_CUDA, "attention scratch: %s", cudaGetErrorString(e));
-    P.part = part;
-    const dim3 grid((unsigned)splits, (unsigned)c->kvh, (unsigned)count);
-    const int G = n_heads / c->kvh;
-    const size_t smem = clq::attend_smem(G, c->hd);
-    e = c->type == CLQ_KV_Q8 ? clq::launch_split<true>(G, grid, smem, s, P) : clq::launch_split<false>(G, grid, smem, s, P);
-    if (e == cudaSuccess) e = cudaGetLastError();
-    if (e == cudaSuccess) {
-        clq::attend_merge_kernel<<<dim3((unsigned)n_heads, (unsigned)count, (unsigned)((c->hd + 31) / 32)), 32, 0, s>>>(
-            part, n_heads, c->hd, (int)splits, out, ldo);
-        e = cudaGetLastError();
+    P.out = out;
+    P.ldo = ldo;
+    const dim3 grid((unsigned)splits, (unsigned)c->kvh, (unsigned)blocks);
+    const size_t smem = clq::attend_smem(QV, c->hd, sr);
+    cudaError_t e = cudaSuccess;
+    void* scratch = nullptr;
+    if (splits > 1) {  // the splits' partials, merged by a second launch
+        const size_t acc_bytes = ((size_t)count * n_heads * splits * c->hd * sizeof(float) + 15) & ~(size_t)15;
+        e = clq::keep_pool_memory();
+        if (e == cudaSuccess) e = cudaMallocAsync(&scratch, acc_bytes + (size_t)count * n_heads * splits * sizeof(float2), s);
+        if (e != cudaSuccess) return clq::set_error(CLQ_ERR_CUDA, "attention scratch: %s", cudaGetErrorString(e));
+        P.acc = static_cast<float*>(scratch);
+        P.ml = reinterpret_cast<float2*>(static_cast<uint8_t*>(scratch) + acc_bytes);
     }
-    const cudaError_t f = cudaFreeAsync(part, s);
-    if (e == cudaSuccess) e = f;
+    e = q8 ? clq::launch_split<true>(QV, sr, grid, smem, s, P) : clq::launch_split<false>(QV, sr, grid, smem, s, P);
+    if (e == cudaSuccess) e = cudaGetLastError();
+    if (e == cudaSuccess && splits > 1) {
+        e = clq::launch_pdl(clq::attend_merge_kernel, dim3((unsigned)n_heads, (unsigned)count), clq::kMergeThreads, 0, s,
+                            (const float*)P.acc, (const float2*)P.ml, n_heads, c->hd, (int)splits, out, ldo);
+    }
+    if (scratch) {
+        const cudaError_t f = cudaFreeAsync(scratch, s);
+        if (e == cudaSuccess) e = f;
+    }
     if (e != cudaSuccess) return clq::set_error(CLQ_ERR_CUDA, "attention launch: %s", cudaGetErrorString(e));
     return CLQ_OK;
 }

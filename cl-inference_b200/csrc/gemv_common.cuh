@@ -21,6 +21,7 @@
 #include "../../include/clq.h"
 #include "clq_internal.h"
 #include "layout.cuh"
+#include "pipeline.cuh"
 
 namespace clq {
 namespace {
@@ -502,8 +503,8 @@ __device__ __forceinline__ void tp_put(const TP& tp, uint32_t ep, int cta, int64
     for (int q = 0; q < tp.world; q++) st_word(tp.peer_recv[q] + off, ep, sum);
 }
 
-__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
+using pipe::allow_dependents;
+using pipe::grid_dependency_wait;
 
 }  // namespace
 }  // namespace clq

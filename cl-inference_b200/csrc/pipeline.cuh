@@ -97,6 +97,11 @@ __device__ __forceinline__ void tensor_copy_2d_hint(void* dst, const void* map, 
         "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
+// Programmatic dependent launch: wait until the grids this one depends on
+// have completed and their writes are visible (a no-op without the launch
+// attribute), and let the next grid in the stream start its prologue.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_dependents() { asm volatile("griddepcontrol.launch_dependents;"); }
 // Named barrier over the first THREADS threads of the CTA (ID 0 is __syncthreads).
 __device__ __forceinline__ void named_sync(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

@@ -7,7 +7,11 @@ stored.  RoPE matches the oracle's tables and rotation to the last bit or one
 ulp (double-precision cos and sin rounded to f32).  Attention over the cached
 prefix matches the float64 restatement of attend with the causal mask within
 1e-5 of the output's scale, for decode rows, a chunk of prompt rows, grouped
-heads of 4 and 8 and the small heads of the reference's tests.  Past-context
+heads of 4, 8 and 16 and the small heads of the reference's tests, in every
+form of the kernel: blocks of 1 to 16 query rows per CTA (ragged last
+blocks), one position range written directly or several merged by a second
+launch, and f32 key and value rows staged by bulk copies or by vector loads
+(CLQ_ATTN_BULK=0, Q8 caches and odd head widths).  Past-context
 updates fail with CLQ_ERR_CONTEXT and non-finite Q8 rows with
 CLQ_ERR_NONFINITE_VALUE (local/kv-cache.lisp:49,94-96).
 """
@@ -134,6 +138,13 @@ def test_rope_matches_tables(cuda, att, pairing, rope_dims, factors):
     (1, 64, 8, 128, 300, 299),     # Llama-3-70B grouping (8 query heads per KV head)
     (6, 32, 8, 128, 70, 64),       # a chunk of prompt rows at positions 64..69 (causal)
     (4, 2, 1, 8, 4, 0),            # the reference tests' small heads
+    (1, 16, 1, 64, 1024, 1023),    # 16 query heads per KV head
+    (64, 32, 8, 128, 1024, 960),   # 64 prompt rows, 4 to a CTA
+    (3, 32, 8, 128, 4000, 3997),   # a long prefix, three rows (a ragged block of 4)
+    (5, 8, 8, 64, 40, 35),         # one query head per KV head: 8 rows to a CTA
+    (2, 8, 2, 128, 12, 10),        # a prefix of one range: written without the merge
+    (2, 4, 2, 36, 150, 148),       # a head width off the 16-column grid (scalar tail)
+    (3, 8, 4, 96, 300, 297),       # a head width with no specialised kernel
 ])
 def test_attention_matches_oracle(cuda, att, cache_type, count, heads, kv, hd, end, qstart):
     torch = cuda
@@ -141,7 +152,7 @@ def test_attention_matches_oracle(cuda, att, cache_type, count, heads, kv, hd, e
     keys = rng.standard_normal((end, kv, hd)).astype(np.float32)
     vals = rng.standard_normal((end, kv, hd)).astype(np.float32)
     q = (rng.standard_normal((count, heads, hd)) * 2).astype(np.float32)
-    with att.KVCache(1024, 2, kv, hd, cache_type) as cache:
+    with att.KVCache(max(1024, end), 2, kv, hd, cache_type) as cache:
         cache.update(1, torch.from_numpy(keys).cuda(), torch.from_numpy(vals).cuda(), 0, check=True)
         out = att.attend(torch.from_numpy(q).cuda(), cache, 1, end, qstart).cpu().numpy()
         k_used, v_used = (keys, vals)
@@ -194,3 +205,59 @@ def test_cache_filled_in_chunks_matches_a_full_pass(cuda, att, cache_type):
             part = att.attend(dq[b:e].contiguous(), chunked, 0, e, b).cpu().numpy()
             assert np.abs(part - want[b:e]).max() <= 1e-5 * scale
 
+
+
+def test_attention_into_strided_rows(cuda, att):
+    """Output rows wider than n_heads * head_dim: the padding stays untouched."""
+    torch = cuda
+    rng = np.random.default_rng(3)
+    count, heads, kv, hd, end = 3, 32, 8, 128, 200
+    keys = rng.standard_normal((end, kv, hd)).astype(np.float32)
+    vals = rng.standard_normal((end, kv, hd)).astype(np.float32)
+    q = rng.standard_normal((count, heads, hd)).astype(np.float32)
+    with att.KVCache(256, 1, kv, hd, "f32") as cache:
+        cache.update(0, torch.from_numpy(keys).cuda(), torch.from_numpy(vals).cuda(), 0, check=True)
+        wide = torch.full((count, heads * hd + 64), 7.0, device="cuda")
+        att.attend(torch.from_numpy(q).cuda(), cache, 0, end, end - count, out=wide[:, :heads * hd])
+        got = wide.cpu().numpy()
+    want = ref.attend_f64(q, keys, vals, ref.causal_mask(count, end, end - count, 0), heads, kv)
+    assert np.abs(got[:, :heads * hd] - want).max() <= 1e-5 * np.abs(want).max()
+    assert np.all(got[:, heads * hd:] == 7.0)
+
+
+_TWO_LAUNCH_CHECK = """
+import sys
+sys.path[:0] = [{root!r}, {root!r} + '/oracle', {root!r} + '/tests']
+import importlib
+import numpy as np
+import torch
+import attention as ref
+att = importlib.import_module('cl-inference_b200.attention')
+for count, heads, kv, hd, end, qstart, kind in [(1, 32, 8, 128, 1000, 999, 'f32'), (6, 64, 8, 128, 70, 64, 'q8'),
+                                               (4, 2, 1, 8, 4, 0, 'f32'), (2, 32, 8, 128, 2000, 1998, 'f32'),
+                                               (3, 16, 1, 64, 900, 897, 'f32')]:
+    rng = np.random.default_rng(end)
+    keys = rng.standard_normal((end, kv, hd)).astype(np.float32)
+    vals = rng.standard_normal((end, kv, hd)).astype(np.float32)
+    q = rng.standard_normal((count, heads, hd)).astype(np.float32)
+    with att.KVCache(2048, 1, kv, hd, kind) as cache:
+        cache.update(0, torch.from_numpy(keys).cuda(), torch.from_numpy(vals).cuda(), 0, check=True)
+        out = att.attend(torch.from_numpy(q).cuda(), cache, 0, end, qstart).cpu().numpy()
+    if kind == 'q8':
+        keys, vals = ref.q8_prefix(*ref.q8_store(keys)), ref.q8_prefix(*ref.q8_store(vals))
+    want = ref.attend_f64(q, keys, vals, ref.causal_mask(count, end, qstart, 0), heads, kv)
+    assert np.abs(out - want).max() <= 1e-5 * np.abs(want).max(), (count, end)
+print("ok")
+"""
+
+
+def test_vector_staging_of_f32_rows():
+    """CLQ_ATTN_BULK=0 stages f32 key and value rows with vector loads instead
+    of bulk copies.  A fresh process, since the knob is read once per process."""
+    import os
+    import subprocess
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    proc = subprocess.run([sys.executable, "-c", _TWO_LAUNCH_CHECK.format(root=root)], capture_output=True, text=True,
+                          timeout=600, env={**os.environ, "CLQ_ATTN_BULK": "0"})
+    assert proc.returncode == 0 and proc.stdout.strip().endswith("ok"), proc.stderr[-3000:]
