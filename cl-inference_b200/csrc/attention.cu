@@ -174,74 +174,60 @@ __host__ __device__ constexpr int key_ld(int hd) { return hd + 16; }
 // Query rows in shared memory: hd rounded up to 4 floats (16-byte rows).
 __host__ __device__ constexpr int query_ld(int hd) { return (hd + 3) & ~3; }
 
-// The split's rows of one KV head, keys or values, into shared memory as f32
-// rows LD floats apart: every thread issues its 16-byte loads (4 f32 or 16
-// codes) before any is used, so the split costs about one memory round trip.
+// The split's key and value rows of one KV head into shared memory as f32
+// (key rows LDK floats apart, value rows hd apart): every thread issues its
+// 16-byte loads (4 f32 or 16 codes) of both before any is used, so the split
+// costs about one memory round trip.
 template <bool Q8, int T>
-__device__ __forceinline__ void stage_rows(const AttnParams& P, const void* buf, const float* scl, int64_t p0, int np,
-                                           int kv, float* dst, int ld) {
+__device__ __forceinline__ void stage_kv(const AttnParams& P, int64_t p0, int np, int kv, float* ks, int ldk, float* vs) {
     const int hd = P.hd;
     if (hd % (Q8 ? 16 : 4)) {  // rows off the 16-byte grid: element by element
-        for (int e = threadIdx.x; e < np * hd; e += T) {
-            const int j = e / hd, d = e - j * hd;
+        const int n = np * hd;
+        for (int e = threadIdx.x; e < 2 * n; e += T) {
+            const bool val = e >= n;
+            const int f = val ? e - n : e, j = f / hd, d = f - j * hd;
             const int64_t slot = (p0 + j) * P.kvh + kv;
+            float* dst = val ? vs + j * hd + d : ks + j * ldk + d;
             if constexpr (Q8) {
-                dst[j * ld + d] =
-                    q8_decode(reinterpret_cast<const int8_t*>(buf)[slot * hd + d], scl[slot * P.groups + d / kQ8Group]);
+                const int8_t* codes = reinterpret_cast<const int8_t*>(val ? P.values : P.keys);
+                *dst = q8_decode(codes[slot * hd + d], (val ? P.vscale : P.kscale)[slot * P.groups + d / kQ8Group]);
             } else {
-                dst[j * ld + d] = reinterpret_cast<const float*>(buf)[slot * hd + d];
+                *dst = reinterpret_cast<const float*>(val ? P.values : P.keys)[slot * hd + d];
             }
         }
         return;
     }
     // vector rows: eight 16-byte loads per thread in flight before any store
     constexpr int B = 8;
-    if constexpr (Q8) {
-        const int per_row = hd / 16, n = np * per_row;
-        for (int e0 = threadIdx.x; e0 < n; e0 += B * T) {
-            uint4 w[B];
-            float sc[B];
+    const int per_row = hd / (Q8 ? 16 : 4), n = np * per_row;
+    for (int e0 = threadIdx.x; e0 < 2 * n; e0 += B * T) {
+        uint4 w[B];
+        float sc[B];
 #pragma unroll
-            for (int b = 0; b < B; b++) {
-                const int e = e0 + b * T;
-                if (e < n) {
-                    const int j = e / per_row, c = e - j * per_row;
-                    const int64_t slot = (p0 + j) * P.kvh + kv;
-                    w[b] = *reinterpret_cast<const uint4*>(reinterpret_cast<const int8_t*>(buf) + slot * hd + c * 16);
-                    sc[b] = scl[slot * P.groups + (c * 16) / kQ8Group];
-                }
-            }
-#pragma unroll
-            for (int b = 0; b < B; b++) {
-                const int e = e0 + b * T;
-                if (e < n) {
-                    const int j = e / per_row, c = e - j * per_row;
-                    const uint32_t ws[4] = {w[b].x, w[b].y, w[b].z, w[b].w};
-                    float* o = dst + j * ld + c * 16;
-#pragma unroll
-                    for (int i = 0; i < 16; i++) o[i] = q8_decode((int8_t)(ws[i >> 2] >> (8 * (i & 3))), sc[b]);
-                }
+        for (int b = 0; b < B; b++) {
+            const int e = e0 + b * T;
+            if (e < 2 * n) {
+                const bool val = e >= n;
+                const int f = val ? e - n : e, j = f / per_row, c = f - j * per_row;
+                const int64_t slot = (p0 + j) * P.kvh + kv;
+                const int8_t* row = reinterpret_cast<const int8_t*>(val ? P.values : P.keys) + slot * hd * (Q8 ? 1 : 4);
+                w[b] = *reinterpret_cast<const uint4*>(row + c * 16);
+                if constexpr (Q8) sc[b] = (val ? P.vscale : P.kscale)[slot * P.groups + (c * 16) / kQ8Group];
             }
         }
-    } else {
-        const int per_row = hd / 4, n = np * per_row;
-        for (int e0 = threadIdx.x; e0 < n; e0 += B * T) {
-            float4 v[B];
 #pragma unroll
-            for (int b = 0; b < B; b++) {
-                const int e = e0 + b * T;
-                if (e < n) {
-                    const int j = e / per_row, c = e - j * per_row;
-                    const int64_t slot = (p0 + j) * P.kvh + kv;
-                    v[b] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(buf) + slot * hd + c * 4);
-                }
-            }
+        for (int b = 0; b < B; b++) {
+            const int e = e0 + b * T;
+            if (e < 2 * n) {
+                const bool val = e >= n;
+                const int f = val ? e - n : e, j = f / per_row, c = f - j * per_row;
+                if constexpr (Q8) {
+                    const uint32_t ws[4] = {w[b].x, w[b].y, w[b].z, w[b].w};
+                    float* o = (val ? vs + j * hd : ks + j * ldk) + c * 16;
 #pragma unroll
-            for (int b = 0; b < B; b++) {
-                const int e = e0 + b * T;
-                if (e < n) {
-                    const int j = e / per_row, c = e - j * per_row;
-                    *reinterpret_cast<float4*>(dst + j * ld + c * 4) = v[b];
+                    for (int i = 0; i < 16; i++) o[i] = q8_decode((int8_t)(ws[i >> 2] >> (8 * (i & 3))), sc[b]);
+                } else {
+                    *reinterpret_cast<uint4*>((val ? vs + j * hd : ks + j * ldk) + c * 4) = w[b];
                 }
             }
         }
@@ -320,8 +306,7 @@ __global__ void __launch_bounds__(SR * 4, SR == 32 ? 4 : 2) attend_split_kernel(
     if (bulk) {
         if (np > 0 && !pipe::mbar_wait(bar, 0, P.err)) pipe::mbar_drain(bar, 0);
     } else {
-        stage_rows<Q8, T>(P, P.keys, P.kscale, p0, np, kv, ks, ld);
-        stage_rows<Q8, T>(P, P.values, P.vscale, p0, np, kv, vs, hd);
+        stage_kv<Q8, T>(P, p0, np, kv, ks, ld, vs);
     }
     __syncthreads();
     pipe::allow_dependents();
