@@ -730,13 +730,15 @@ def e2e_dropin(args, clq, stores, host_copies, m, job_bytes, prefill=False):
             xs[key] = rng.standard_normal((m, s.k), dtype=np.float32)
         out = np.empty((m, s.n), np.float32)
         outs.append(out)
-        calls.append((fns[dtype], out, xs[key], data, s.n, s.k))
+        # the buffers' addresses, as a foreign caller holds them (outs, xs and
+        # host_copies keep the arrays alive)
+        calls.append((fns[dtype], out.ctypes.data, xs[key].ctypes.data, data.ctypes.data, s.n, s.k))
         h2d += 4 * m * s.k
         d2h += 4 * m * s.n
 
     def one():
         for fn, out, x, data, n, k in calls:
-            rc = fn(out.ctypes.data, x.ctypes.data, data.ctypes.data, m, n, k)
+            rc = fn(out, x, data, m, n, k)
             if rc:
                 raise clq.ClqError(rc, clq._lib.last_error())
 

@@ -6,8 +6,11 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
+#include <map>
 #include <memory>
 #include <mutex>
+#include <tuple>
 #include <new>
 #include <string>
 #include <vector>
@@ -212,11 +215,42 @@ struct PinnedBuffer {
     }
 };
 
+// One host call's device work (the copy of x, the linear) as an instantiated
+// CUDA graph, replayed by later calls with the same store, shape and staging
+// buffers: one launch instead of two, with the kernels' parameters checked
+// once.  The entry keeps its store alive; a thread drops its graphs (and its
+// remembered lookups) when the weight cache changes (clq_forget,
+// clq_clear_cache).
+using GraphKey = std::tuple<const clq_store*, int64_t, int64_t, int64_t, int64_t, unsigned, void*, void*, void*>;
+struct CallGraph {
+    cudaGraphExec_t exec = nullptr;
+    std::shared_ptr<clq_store> store;
+};
+std::atomic<uint64_t> g_cache_generation{0};
+
 struct ThreadContext {
     int device = -1;
     cudaStream_t stream = nullptr;
     DeviceBuffer x, out, ids;
     PinnedBuffer hx, hout;  // host staging of x and out for small products
+    std::map<GraphKey, CallGraph> graphs;
+    // this thread's earlier lookups: (host address, n, k, dtype) -> (store, first row)
+    std::map<std::tuple<const uint8_t*, int64_t, int64_t, int>, std::pair<std::shared_ptr<clq_store>, int64_t>> hits;
+    uint64_t graph_generation = 0;
+    void drop_graphs() {
+        for (auto& kv : graphs)
+            if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+        graphs.clear();
+        hits.clear();
+    }
+    // Drops the graphs and lookups that predate a change of the weight cache.
+    void sync_generation() {
+        const uint64_t gen = g_cache_generation.load();
+        if (gen != graph_generation) {
+            drop_graphs();
+            graph_generation = gen;
+        }
+    }
 };
 
 struct ThreadContexts {
@@ -225,6 +259,7 @@ struct ThreadContexts {
         for (ThreadContext* c : per_device) {
             if (!c) continue;
             cudaSetDevice(c->device);
+            c->drop_graphs();
             if (c->stream) cudaStreamDestroy(c->stream);
             if (c->x.ptr) cudaFree(c->x.ptr);
             if (c->out.ptr) cudaFree(c->out.ptr);
@@ -602,9 +637,17 @@ int clq_matmul(int dtype, float* out, const float* x, const uint8_t* bytes, int6
     if ((rc = thread_context(device, &ctx))) return rc;
     std::shared_ptr<clq_store> store;
     int64_t row_begin = 0;
-    if ((rc = cached_store(dtype, n, k, bytes, device, !(flags & CLQ_NO_CACHE), ctx->stream, &store,
-                           &row_begin)))
-        return rc;
+    const bool use_cache = !(flags & CLQ_NO_CACHE);
+    ctx->sync_generation();
+    const auto hit_key = std::make_tuple(bytes, n, k, dtype);
+    const auto hit = use_cache ? ctx->hits.find(hit_key) : ctx->hits.end();
+    if (hit != ctx->hits.end()) {
+        store = hit->second.first;
+        row_begin = hit->second.second;
+    } else {
+        if ((rc = cached_store(dtype, n, k, bytes, device, use_cache, ctx->stream, &store, &row_begin))) return rc;
+        if (use_cache) ctx->hits[hit_key] = {store, row_begin};
+    }
     const size_t xbytes = (size_t)(m * k) * sizeof(float), obytes = (size_t)(m * n) * sizeof(float);
     cudaError_t e;
     if ((e = ctx->x.ensure(xbytes)) != cudaSuccess) return cuda_fail(e, "cudaMalloc(x)");
@@ -618,13 +661,44 @@ int clq_matmul(int dtype, float* out, const float* x, const uint8_t* bytes, int6
         if ((e = ctx->hout.ensure(obytes)) != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(out)");
         std::memcpy(ctx->hx.ptr, x, xbytes);
     }
-    if ((e = cudaMemcpyAsync(ctx->x.ptr, staged ? ctx->hx.ptr : x, xbytes, cudaMemcpyHostToDevice, ctx->stream)) !=
-        cudaSuccess)
-        return cuda_fail(e, "copy x to device");
     float* dout = staged ? (float*)ctx->hout.dptr : (float*)ctx->out.ptr;
-    if ((e = clq::launch_linear(view_of(store.get(), row_begin), n, ctx->x.ptr, CLQ_X_F32, m, dout, n,
-                                flags & (CLQ_MATH_FAST | CLQ_MATH_EXACT), ctx->stream)) != cudaSuccess)
-        return cuda_fail(e, "linear kernel launch");
+    const unsigned lflags = flags & (CLQ_MATH_FAST | CLQ_MATH_EXACT);
+    // staged: a copy kernel reads x from the mapped staging buffer, and the
+    // linear's kernel, launched behind it, prefetches its weights meanwhile
+    const bool copy_kernel = staged && xbytes % 16 == 0;
+    auto enqueue = [&]() -> cudaError_t {
+        cudaError_t r = copy_kernel ? clq::launch_copy_in(ctx->x.ptr, ctx->hx.dptr, xbytes, ctx->stream)
+                                    : cudaMemcpyAsync(ctx->x.ptr, staged ? ctx->hx.ptr : x, xbytes,
+                                                      cudaMemcpyHostToDevice, ctx->stream);
+        if (r != cudaSuccess) return r;
+        return clq::launch_linear(view_of(store.get(), row_begin), n, ctx->x.ptr, CLQ_X_F32, m, dout, n, lflags,
+                                  ctx->stream);
+    };
+    // decode-sized calls on cached weights replay a graph of the same work
+    cudaGraphExec_t exec = nullptr;
+    if (copy_kernel && m <= 8 && use_cache) {
+        const GraphKey key{store.get(), row_begin, n, k, m, lflags, ctx->x.ptr, ctx->hx.dptr, ctx->hout.dptr};
+        auto it = ctx->graphs.find(key);
+        if (it != ctx->graphs.end()) {
+            exec = it->second.exec;
+        } else if (cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal) == cudaSuccess) {
+            const cudaError_t le = enqueue();
+            cudaGraph_t graph = nullptr;
+            const cudaError_t ce = cudaStreamEndCapture(ctx->stream, &graph);
+            if (le == cudaSuccess && ce == cudaSuccess && graph &&
+                cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess) {
+                ctx->graphs[key] = CallGraph{exec, store};
+            } else {
+                exec = nullptr;  // not capturable: this call runs eagerly
+            }
+            if (graph) cudaGraphDestroy(graph);
+            cudaGetLastError();
+        } else {
+            cudaGetLastError();
+        }
+    }
+    e = exec ? cudaGraphLaunch(exec, ctx->stream) : enqueue();
+    if (e != cudaSuccess) return cuda_fail(e, "linear kernel launch");
     if (!staged && (e = cudaMemcpyAsync(out, ctx->out.ptr, obytes, cudaMemcpyDeviceToHost, ctx->stream)) !=
                        cudaSuccess)
         return cuda_fail(e, "copy out to host");
@@ -656,6 +730,7 @@ int clq_forget(const uint8_t* bytes, size_t nbytes) {
             if (overlap) {
                 dropped.push_back(e.store);
                 g_cache.erase(g_cache.begin() + i);
+                g_cache_generation.fetch_add(1);
             } else {
                 i++;
             }
@@ -669,6 +744,7 @@ int clq_clear_cache(void) {
     {
         std::lock_guard<std::mutex> lock(g_cache_mu);
         dropped.swap(g_cache);
+        g_cache_generation.fetch_add(1);
     }
     return CLQ_OK;
 }

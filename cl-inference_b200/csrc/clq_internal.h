@@ -43,6 +43,11 @@ cudaError_t launch_dequantize(const WeightView& w, int64_t rows, float* out, boo
 cudaError_t launch_gather(const WeightView& w, const int32_t* ids, int64_t count, float* out,
                           cudaStream_t stream);
 
+// BYTES (a multiple of 16) from page-locked host memory mapped into the
+// device's address space (SRC_MAPPED, its device pointer) to device DST, both
+// 16-byte aligned, by a kernel that lets the next one start early.
+cudaError_t launch_copy_in(void* dst, const void* src_mapped, size_t bytes, cudaStream_t stream);
+
 // out[i*ldo + j] = sum_c x[i, c] * W[j, c], i < m, j < rows.
 // Returns cudaErrorNotSupported when no kernel covers the request.
 cudaError_t launch_linear(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,

@@ -1,5 +1,6 @@
-// kernels_basic.cu -- scale validation, bit-exact dequantize/gather, and the
-// generic linear kernel (any row alignment, any number of activation rows).
+// kernels_basic.cu -- scale validation, bit-exact dequantize/gather, the
+// generic linear kernel (any row alignment, any number of activation rows) and
+// the host-call path's copy of its inputs from mapped page-locked memory.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -165,7 +166,39 @@ cudaError_t generic_by_dtype(const WeightView& w, int64_t rows, const XT* x, int
     }
 }
 
+// N16 16-byte words from SRC (page-locked host memory mapped into the device's
+// address space) to DST, every load in flight before any store.  The next
+// kernel in the stream may start at once under programmatic dependent launch:
+// it prefetches its weights and waits (griddepcontrol.wait) for this copy
+// before it reads DST.
+__global__ void __launch_bounds__(kThreads) copy_in_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src,
+                                                           int64_t n16) {
+    asm volatile("griddepcontrol.launch_dependents;");
+    constexpr int B = 4;
+    for (int64_t i0 = blockIdx.x * (int64_t)kThreads * B + threadIdx.x; i0 < n16;
+         i0 += (int64_t)gridDim.x * kThreads * B) {
+        uint4 v[B];
+#pragma unroll
+        for (int b = 0; b < B; b++)
+            if (i0 + b * kThreads < n16) v[b] = src[i0 + b * kThreads];
+#pragma unroll
+        for (int b = 0; b < B; b++)
+            if (i0 + b * kThreads < n16) dst[i0 + b * kThreads] = v[b];
+    }
+}
+
 }  // namespace
+
+cudaError_t launch_copy_in(void* dst, const void* src_mapped, size_t bytes, cudaStream_t s) {
+    if (bytes == 0) return cudaSuccess;
+    if (bytes % 16 || (uintptr_t)dst % 16 || (uintptr_t)src_mapped % 16) return cudaErrorInvalidValue;
+    const int64_t n16 = (int64_t)(bytes / 16);
+    int64_t blocks = (n16 + kThreads * 4 - 1) / (kThreads * 4);
+    if (blocks > 64) blocks = 64;
+    copy_in_kernel<<<(unsigned)blocks, kThreads, 0, s>>>(static_cast<uint4*>(dst), static_cast<const uint4*>(src_mapped),
+                                                        n16);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_validate_scales(const uint8_t* dev, int dtype, int64_t nblocks,
                                    unsigned long long* first_bad, cudaStream_t stream) {
