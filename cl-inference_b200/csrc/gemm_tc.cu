@@ -246,12 +246,18 @@ constexpr uint32_t kHNeg1024 = 0xE400E400u;
 constexpr uint32_t kHNeg64 = 0xD400D400u;
 constexpr uint32_t kLoNib = 0x640F640Fu;
 constexpr uint32_t kHiNib = 0x64F064F0u;
+constexpr uint32_t kH1032 = 0x64086408u;   // 1024 + 8
+constexpr uint32_t kH1152 = 0x64806480u;   // 1024 + 128
+constexpr uint32_t kHNeg72 = 0xD480D480u;
 
 template <int D> struct Raw;
 template <> struct Raw<kQ4_K> { uint4 hd, cw; };                          // header, 16 code bytes
 template <> struct Raw<kQ6_K> { uint32_t w[12]; uint4 sv; uint32_t d; };  // lane quads 2hv, 2hv+1: 6 words each
-template <> struct Raw<kQ4_0> { int dummy; };
-template <> struct Raw<kQ8_0> { int dummy; };
+// Q4_0 / Q8_0: the K block's two 32-element blocks, lane-quad words 0..3 of
+// each (Q4_0: all 16 code bytes; Q8_0: the half of the 32 this thread
+// converts), and their two fp16 scales
+template <> struct Raw<kQ4_0> { uint32_t w[2][4]; uint32_t d2; };
+template <> struct Raw<kQ8_0> { uint32_t w[2][4]; uint32_t d2; };
 
 template <int D>
 __device__ __forceinline__ void load_raw(const Planes& p, int64_t grow, int64_t kb, int hv, Raw<D>& r) {
@@ -282,6 +288,19 @@ __device__ __forceinline__ void load_raw(const Planes& p, int64_t grow, int64_t 
         }
         r.sv = *reinterpret_cast<const uint4*>(p.s + blk * 16);
         r.d = *reinterpret_cast<const unsigned short*>(p.d + 2 * blk);
+    } else {
+        // lane-major chunks of 8 blocks (layout.cuh, chunk_code_offset): lane
+        // quad t's words of blocks b, b+1 of chunk c; blocks 2kb, 2kb+1 share a chunk
+        constexpr int CB = D == kQ4_0 ? 16 : 32, words = CB / 16;
+        const int64_t j0 = 2 * kb, c = j0 / 8, b = j0 % 8;
+        const int64_t nbc = p.nb - 8 * c < 8 ? p.nb - 8 * c : 8;
+        const uint8_t* base = p.q + grow * p.nb * CB + c * 8 * CB + (D == kQ8_0 ? 4 * hv : 0);
+#pragma unroll
+        for (int jb = 0; jb < 2; jb++)
+#pragma unroll
+            for (int t = 0; t < 4; t++)
+                r.w[jb][t] = *reinterpret_cast<const uint32_t*>(base + (t * nbc + b + jb) * 4 * words);
+        r.d2 = *reinterpret_cast<const uint32_t*>(p.d + 2 * (grow * p.nb + j0));
     }
 }
 
@@ -366,18 +385,31 @@ __device__ __forceinline__ void convert_raw(const Planes& p, int64_t grow, int64
             }
         }
     } else {
-        // Q4_0 / Q8_0: element by element (two 32-element blocks)
-        uint32_t g0[8], g1[8];
+        // Q4_0 / Q8_0: chunk i holds elements 16hv + 8(i & 1) .. + 7 of block
+        // i >> 1 -- words 2(i & 1) and 2(i & 1) + 1, four elements each.  The
+        // code becomes an exact small integer in fp16 (Q4_0: nibble - 8, from
+        // the low nibbles for hv = 0 and the high ones for hv = 1; Q8_0: the
+        // signed byte), and one multiply by d rounds it once, as rounding the
+        // exact fp32 product of quant/packed.lisp:89-90 / q8-0.lisp:115-117 does
+        const uint32_t DD[2] = {prmt(rw.d2, rw.d2, 0x1010), prmt(rw.d2, rw.d2, 0x3232)};
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int64_t e0 = kb * kKB + 16 * hv + 2 * j, e1 = e0 + 32;
-            g0[j] = pack_half2(element_planar<D>(p, grow, e0), element_planar<D>(p, grow, e0 + 1));
-            g1[j] = pack_half2(element_planar<D>(p, grow, e1), element_planar<D>(p, grow, e1 + 1));
+        for (int i = 0; i < 4; i++) {
+            uint32_t v[4];
+#pragma unroll
+            for (int h = 0; h < 4; h++) {
+                const uint32_t w = rw.w[i >> 1][2 * (i & 1) + (h >> 1)];
+                const uint32_t sel = (h & 1) ? 0x4342u : 0x4140u;
+                uint32_t q;
+                if constexpr (D == kQ4_0) {
+                    const uint32_t pq = prmt(w, kMagic, sel);
+                    q = hv ? hfma2(pq & kHiNib, kHSixteenth, kHNeg72) : hsub2(pq & kLoNib, kH1032);
+                } else {
+                    q = hsub2(prmt(w ^ 0x80808080u, kMagic, sel), kH1152);
+                }
+                v[h] = hmul2(q, DD[i >> 1]);
+            }
+            ch[i] = make_uint4(v[0], v[1], v[2], v[3]);
         }
-        ch[0] = make_uint4(g0[0], g0[1], g0[2], g0[3]);
-        ch[1] = make_uint4(g0[4], g0[5], g0[6], g0[7]);
-        ch[2] = make_uint4(g1[0], g1[1], g1[2], g1[3]);
-        ch[3] = make_uint4(g1[4], g1[5], g1[6], g1[7]);
     }
 #pragma unroll
     for (int i = 0; i < 4; i++) *reinterpret_cast<uint4*>(a + swz(row, (uint32_t)ci[i])) = ch[i];
@@ -467,14 +499,21 @@ __device__ __forceinline__ void convert_raw_exact(const Planes& p, int64_t grow,
             }
         }
     } else {
-        // Q4_0 / Q8_0: element by element (two 32-element blocks)
+        // Q4_0 / Q8_0: chunk i as convert_raw's; w = d * code in fp32
+        // (quant/packed.lisp:89-90, quant/q8-0.lisp:115-117)
+        const float dd[2] = {__half2float(__ushort_as_half((unsigned short)(rw.d2 & 0xFFFF))),
+                             __half2float(__ushort_as_half((unsigned short)(rw.d2 >> 16)))};
 #pragma unroll
-        for (int j = 0; j < 8; j++) {
-            const int64_t e0 = kb * kKB + 16 * hv + 2 * j, e1 = e0 + 32;
-            put_split(element_planar<D>(p, grow, e0), element_planar<D>(p, grow, e0 + 1), hi[j >> 2][j & 3],
-                      lo[j >> 2][j & 3]);
-            put_split(element_planar<D>(p, grow, e1), element_planar<D>(p, grow, e1 + 1), hi[2 + (j >> 2)][j & 3],
-                      lo[2 + (j >> 2)][j & 3]);
+        for (int i = 0; i < 4; i++) {
+            float e[8];
+#pragma unroll
+            for (int x = 0; x < 8; x++) {
+                const uint32_t byte = (rw.w[i >> 1][2 * (i & 1) + (x >> 2)] >> (8 * (x & 3))) & 0xFF;
+                const int code = D == kQ4_0 ? (int)(hv ? byte >> 4 : byte & 15) - 8 : (int)(int8_t)byte;
+                e[x] = __fmul_rn(dd[i >> 1], (float)code);
+            }
+#pragma unroll
+            for (int h = 0; h < 4; h++) put_split(e[2 * h], e[2 * h + 1], hi[i][h], lo[i][h]);
         }
     }
 #pragma unroll

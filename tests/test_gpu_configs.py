@@ -7,8 +7,9 @@ Every shape a benchmark workload runs goes through the kernel it takes there:
     8192 x 8192, k/v 1024 x 8192, gate/up 28672 x 8192 and the Q6_K down
     projection 8192 x 28672, whose activations do not fit one CTA, so K is
     split across a thread-block cluster;
-  * the 128256 x 4096 Q6_K output head at eight and sixty-four rows (fp32
-    activations keep the GEMV at 64 rows; bf16 ones take the GEMM).
+  * the 128256 x 4096 Q6_K output head at eight and sixty-four rows (at 64
+    rows fp32 activations take the exact GEMM, bf16 ones the fp16-operand
+    GEMM).
 The fp64 check runs on slices of weight rows (start, middle, end) so the
 oracle finishes in seconds; the device computes the whole output.  Decode
 products meet the reference's bound 1e-5 + 1e-5 * sum|x*w|
