@@ -587,6 +587,22 @@ cudaError_t launch_gemv_bulk_group(const WeightView* const* w, const int64_t* ro
 cudaError_t launch_gemv_bulk_impl(const WeightView* const* w, const int64_t* rows, int count, const void* x,
                                   int xtype, int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
                                   cudaStream_t stream) {
+    if (bulk_enabled() && !tp && m > 8 && m <= 16 && count >= 1 && count <= kGroup) {
+        // 9 to 16 rows of Q4_K / Q6_K: the per-warp streams in two passes
+        // (rows 0-7, then the rest), each reading the weights once at the
+        // eight-row rate -- half the time of one 16-row pass of the other
+        // GEMVs.  The second pass has fewer rows, so its plan fits when the
+        // first one's does.
+        const cudaError_t e1 = launch_gemv_warp(w, rows, count, x, xtype, 8, out, ldo, nullptr, stream);
+        if (e1 != cudaErrorNotSupported) {
+            if (e1 != cudaSuccess) return e1;
+            const size_t esize = xtype == CLQ_X_F32 ? 4 : 2;
+            float* out2[kGroup];
+            for (int i = 0; i < count; i++) out2[i] = out[i] + 8 * ldo[i];
+            const void* x2 = static_cast<const uint8_t*>(x) + (size_t)8 * (size_t)w[0]->k * esize;
+            return launch_gemv_warp(w, rows, count, x2, xtype, m - 8, out2, ldo, nullptr, stream);
+        }
+    }
     if (!bulk_enabled() || m < 1 || m > 8 || count < 1 || count > kGroup) return cudaErrorNotSupported;
     // up to eight activation rows of Q4_K / Q6_K: the per-warp streams when their plan fits
     const cudaError_t ew = launch_gemv_warp(w, rows, count, x, xtype, m, out, ldo, tp, stream);
