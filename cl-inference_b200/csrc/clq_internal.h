@@ -56,8 +56,10 @@ cudaError_t launch_linear(const WeightView& w, int64_t rows, const void* x, int 
 // Tensor-core fused dequant + GEMV (K a multiple of 256).
 bool gemv_mma_supported(const WeightView& w, int64_t m);
 bool gemv_pdl_enabled();
-// The bulk-copy decode GEMV (m <= 8); cudaErrorNotSupported for shapes it does
-// not take, before anything is launched.
+// The streaming decode GEMVs: Q4_K / Q6_K on the per-warp streams (m <= 8 in
+// one pass, or two passes for 9 <= m <= 16 and for 5 <= m <= 8 when one pass
+// does not fit), else the bulk-copy kernel (m <= 8).  cudaErrorNotSupported
+// for shapes none of them takes, before anything is launched.
 cudaError_t launch_gemv_bulk_group(const WeightView* const* w, const int64_t* rows, int count, const void* x,
                                    int xtype, int64_t m, float* const* out, const int64_t* ldo,
                                    cudaStream_t stream);

@@ -587,26 +587,39 @@ cudaError_t launch_gemv_bulk_group(const WeightView* const* w, const int64_t* ro
 cudaError_t launch_gemv_bulk_impl(const WeightView* const* w, const int64_t* rows, int count, const void* x,
                                   int xtype, int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
                                   cudaStream_t stream) {
-    if (bulk_enabled() && !tp && m > 8 && m <= 16 && count >= 1 && count <= kGroup) {
-        // 9 to 16 rows of Q4_K / Q6_K: the per-warp streams in two passes
-        // (rows 0-7, then the rest), each reading the weights once at the
-        // eight-row rate -- half the time of one 16-row pass of the other
-        // GEMVs.  The second pass has fewer rows, so its plan fits when the
-        // first one's does.
-        const cudaError_t e1 = launch_gemv_warp(w, rows, count, x, xtype, 8, out, ldo, nullptr, stream);
-        if (e1 != cudaErrorNotSupported) {
-            if (e1 != cudaSuccess) return e1;
-            const size_t esize = xtype == CLQ_X_F32 ? 4 : 2;
-            float* out2[kGroup];
-            for (int i = 0; i < count; i++) out2[i] = out[i] + 8 * ldo[i];
-            const void* x2 = static_cast<const uint8_t*>(x) + (size_t)8 * (size_t)w[0]->k * esize;
-            return launch_gemv_warp(w, rows, count, x2, xtype, m - 8, out2, ldo, nullptr, stream);
+    // Q4_K / Q6_K rows the per-warp streams do not take in one pass (9 to 16
+    // rows; fewer when the plan of all of them does not fit, as on the
+    // largest vocabulary heads): passes of STEP rows, each reading the
+    // weights once at that row count's rate -- at 16 rows two passes of
+    // eight take half the time of one 16-row pass of the other GEMVs.  A
+    // later pass has no more rows than the first, so its plan fits when the
+    // first one's does; nothing is launched when the first does not fit.
+    auto passes = [&](int64_t step) -> cudaError_t {
+        const size_t esize = xtype == CLQ_X_F32 ? 4 : 2;
+        for (int64_t r0 = 0; r0 < m; r0 += step) {
+            float* o[kGroup];
+            for (int i = 0; i < count; i++) o[i] = out[i] + r0 * ldo[i];
+            const void* xr = static_cast<const uint8_t*>(x) + (size_t)r0 * (size_t)w[0]->k * esize;
+            const cudaError_t e = launch_gemv_warp(w, rows, count, xr, xtype, m - r0 < step ? m - r0 : step, o, ldo,
+                                                   nullptr, stream);
+            if (e != cudaSuccess) return e;
+        }
+        return cudaSuccess;
+    };
+    if (!bulk_enabled() || m < 1 || m > 16 || count < 1 || count > kGroup) return cudaErrorNotSupported;
+    if (m <= 8) {
+        // up to eight activation rows of Q4_K / Q6_K: the per-warp streams when their plan fits
+        const cudaError_t ew = launch_gemv_warp(w, rows, count, x, xtype, m, out, ldo, tp, stream);
+        if (ew != cudaErrorNotSupported) return ew;
+    }
+    if (!tp) {
+        for (int64_t step : {8, 4, 2}) {
+            if (step >= m) continue;
+            const cudaError_t e = passes(step);
+            if (e != cudaErrorNotSupported) return e;
         }
     }
-    if (!bulk_enabled() || m < 1 || m > 8 || count < 1 || count > kGroup) return cudaErrorNotSupported;
-    // up to eight activation rows of Q4_K / Q6_K: the per-warp streams when their plan fits
-    const cudaError_t ew = launch_gemv_warp(w, rows, count, x, xtype, m, out, ldo, tp, stream);
-    if (ew != cudaErrorNotSupported) return ew;
+    if (m > 8) return cudaErrorNotSupported;
     int* err = device_status_word();
     if (!err) return cudaErrorNotSupported;
     BulkParams P = {};
