@@ -234,6 +234,7 @@ struct ThreadContext {
     DeviceBuffer x, out, ids;
     PinnedBuffer hx, hout;  // host staging of x and out for small products
     std::map<GraphKey, CallGraph> graphs;
+    void* graph_buffers[3] = {nullptr, nullptr, nullptr};  // x, hx, hout when the graphs were made
     // this thread's earlier lookups: (host address, n, k, dtype) -> (store, first row)
     std::map<std::tuple<const uint8_t*, int64_t, int64_t, int>, std::pair<std::shared_ptr<clq_store>, int64_t>> hits;
     uint64_t graph_generation = 0;
@@ -677,6 +678,14 @@ int clq_matmul(int dtype, float* out, const float* x, const uint8_t* bytes, int6
     // decode-sized calls on cached weights replay a graph of the same work
     cudaGraphExec_t exec = nullptr;
     if (copy_kernel && m <= 8 && use_cache) {
+        // staging that moved (a larger call reallocated it) orphans every graph
+        void* const bufs[3] = {ctx->x.ptr, ctx->hx.dptr, ctx->hout.dptr};
+        if (bufs[0] != ctx->graph_buffers[0] || bufs[1] != ctx->graph_buffers[1] || bufs[2] != ctx->graph_buffers[2]) {
+            for (auto& kv : ctx->graphs)
+                if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+            ctx->graphs.clear();
+            for (int i = 0; i < 3; i++) ctx->graph_buffers[i] = bufs[i];
+        }
         const GraphKey key{store.get(), row_begin, n, k, m, lflags, ctx->x.ptr, ctx->hx.dptr, ctx->hout.dptr};
         auto it = ctx->graphs.find(key);
         if (it != ctx->graphs.end()) {
