@@ -584,10 +584,13 @@ cudaError_t launch_gemv_bulk_group(const WeightView* const* w, const int64_t* ro
     return launch_gemv_bulk_impl(w, rows, count, x, xtype, m, out, ldo, nullptr, stream);
 }
 
+// Most activation rows the per-warp passes take (GEMM territory beyond).
+constexpr int64_t kMaxPassRows = 32;
+
 cudaError_t launch_gemv_bulk_impl(const WeightView* const* w, const int64_t* rows, int count, const void* x,
                                   int xtype, int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
                                   cudaStream_t stream) {
-    // Q4_K / Q6_K rows the per-warp streams do not take in one pass (9 to 16
+    // Q4_K / Q6_K rows the per-warp streams do not take in one pass (9 to 32
     // rows; fewer when the plan of all of them does not fit, as on the
     // largest vocabulary heads): passes of STEP rows, each reading the
     // weights once at that row count's rate -- at 16 rows two passes of
@@ -606,7 +609,7 @@ cudaError_t launch_gemv_bulk_impl(const WeightView* const* w, const int64_t* row
         }
         return cudaSuccess;
     };
-    if (!bulk_enabled() || m < 1 || m > 16 || count < 1 || count > kGroup) return cudaErrorNotSupported;
+    if (!bulk_enabled() || m < 1 || m > kMaxPassRows || count < 1 || count > kGroup) return cudaErrorNotSupported;
     if (m <= 8) {
         // up to eight activation rows of Q4_K / Q6_K: the per-warp streams when their plan fits
         const cudaError_t ew = launch_gemv_warp(w, rows, count, x, xtype, m, out, ldo, tp, stream);

@@ -7,23 +7,31 @@
 
 #include "../../include/clq.h"
 #include "clq_internal.h"
+#include "formats.cuh"
 
 namespace clq {
 namespace {
 
-// Activation rows from which the tensor-core GEMM replaces the GEMV: past 16
-// rows the GEMVs' cost grows with every row while the GEMM's (its weight
-// conversion) does not (Llama-3.2-1B shapes, Q4_0 + Q4_K, fp32 activations:
-// 4.46 ms on the GEMV against 2.78 on the exact GEMM at 32 rows; at 16 rows
-// the GEMV is still ahead on Q4_0 / Q8_0, 2.44 against 2.73 ms).
-int64_t gemm_min_m() {
-    static int64_t v = -1;
-    if (v < 0) {
-        const char* e = getenv("CLQ_GEMM_MIN_M");  // tuning knob
-        v = e ? atoll(e) : 17;
-        if (v < 1) v = 1;
+// Activation rows from which the tensor-core GEMM replaces the GEMV
+// (CLQ_GEMM_MIN_M, a tuning knob, sets one threshold for every case).  The
+// GEMVs' cost grows with every row, the GEMM's (its weight conversion) does
+// not.  Measured with fp32 activations and the exact GEMM: Q4_0 / Q8_0 from
+// 17 rows (Llama-3.2-1B shapes at 32 rows: 4.46 ms on the register-fed GEMV
+// against 2.78); Q4_K / Q6_K from 25, since the per-warp GEMV in passes of
+// eight rows holds out longer (Llama-3-8B step at 24 rows: 9.5 against 12.7
+// ms; even at 32).  16-bit activations keep the fp32-class GEMVs below 64
+// rows: the fp16-operand GEMM misses the 1e-3 norm-relative gate there on
+// N(0, 0.02) weights quantized to Q4_K (1.2e-3 at 24 rows).
+int64_t gemm_min_m(const WeightView& w, bool exact) {
+    static int64_t v = -2;
+    if (v == -2) {
+        const char* e = getenv("CLQ_GEMM_MIN_M");
+        v = e ? atoll(e) : -1;
+        if (e && v < 1) v = 1;
     }
-    return v;
+    if (v > 0) return v;
+    if (!exact) return 64;
+    return w.dtype == kQ4_K || w.dtype == kQ6_K ? 25 : 17;
 }
 
 }  // namespace
@@ -52,13 +60,11 @@ cudaError_t keep_pool_memory() {
 // Every request of at least CLQ_GEMM_MIN_M rows: fp32 activations without
 // CLQ_MATH_FAST take the exact form (fp32-class products), 16-bit ones (or
 // CLQ_MATH_FAST) the fp16-operand form unless CLQ_MATH_EXACT asks otherwise.
-bool uses_gemm_tc(const WeightView& w, int xtype, int64_t m, unsigned flags) {
-    (void)xtype;
-    (void)flags;
-    return m >= gemm_min_m() && gemm_tc_supported(w, m);
-}
 bool gemm_exact(int xtype, unsigned flags) {
     return (flags & CLQ_MATH_EXACT) || (xtype == CLQ_X_F32 && !(flags & CLQ_MATH_FAST));
+}
+bool uses_gemm_tc(const WeightView& w, int xtype, int64_t m, unsigned flags) {
+    return m >= gemm_min_m(w, gemm_exact(xtype, flags)) && gemm_tc_supported(w, m);
 }
 
 cudaError_t launch_linear(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,

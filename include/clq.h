@@ -57,7 +57,8 @@ enum clq_status {
 #define CLQ_STORE_DEFAULT 0u
 
 /* Product flags. */
-#define CLQ_MATH_DEFAULT 0u   /* fp32-class results for fp32 activations (from 17 rows the
+#define CLQ_MATH_DEFAULT 0u   /* fp32-class results for fp32 activations (from 17 rows of
+                                 Q4_0 / Q8_0 and 25 of Q4_K / Q6_K the
                                  tcgen05 GEMM in its exact form: weights and activations as
                                  fp16 hi + lo parts, three MMAs per K step)             */
 #define CLQ_MATH_FAST 1u      /* prefill GEMM may round dequantized weights to fp16  */
