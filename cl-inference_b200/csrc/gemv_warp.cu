@@ -71,9 +71,11 @@ constexpr int kWEpochOff = kWW * kWMaxDepth * 8, kWNormOff = kWEpochOff + 16, kW
 constexpr int kWHeader = kWRedOff + kWW * 2 * 4;
 constexpr int kWMaxDevices = 64;
 constexpr size_t kWSmemLimit = 227 * 1024;
-// Units each warp copies before waiting for the previous kernel; the rest of
-// its ring is filled after its activation loads are issued, so that those
-// loads do not queue behind a full ring's worth of weight traffic.
+// Units each warp copies before waiting for the previous kernel (at most the
+// ring's depth); the rest of its ring is filled after its activation loads
+// are issued, so that those loads do not queue behind a full ring's worth of
+// weight traffic.  Three measured slower (1.60 against 1.51 ms on the
+// Llama-3-8B decode step).
 constexpr int kWPreWait = 2;
 
 // Bytes of one row of one unit in the q plane (the whole unit's data for Q4_K;
@@ -236,7 +238,10 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
             ++itile;
         }
     };
-    while (issued < u1 && issued < u0 + kWPreWait) issue();
+    // never more copies in flight than the ring has slots: each slot's barrier
+    // counts one copy per phase
+    const int prewait = kWPreWait < depth ? kWPreWait : depth;
+    while (issued < u1 && issued < u0 + prewait) issue();
 
     grid_dependency_wait();  // the activations may come from the previous kernel
     // read through L2: an SM's L1 may hold a line of epochs from an earlier call
