@@ -62,6 +62,8 @@ struct KvStore {
 
 __global__ void kv_store_q8_kernel(const KvStore S, int64_t count, int kvh, int hd, int64_t ps, int64_t hs,
                                    int64_t start, int* err) {
+    pipe::allow_dependents();
+    pipe::grid_dependency_wait();  // the rows may come from the previous kernel
     const int groups = (hd + kQ8Group - 1) / kQ8Group;
     const float* __restrict__ src = S.src[blockIdx.y];
     int8_t* __restrict__ codes = reinterpret_cast<int8_t*>(S.buf[blockIdx.y]);
@@ -93,6 +95,8 @@ __global__ void kv_store_q8_kernel(const KvStore S, int64_t count, int kvh, int 
 
 __global__ void kv_store_f32_kernel(const KvStore S, int64_t count, int kvh, int hd, int64_t ps, int64_t hs,
                                     int64_t start) {
+    pipe::allow_dependents();
+    pipe::grid_dependency_wait();  // the rows may come from the previous kernel
     const float* __restrict__ src = S.src[blockIdx.y];
     float* __restrict__ dst = reinterpret_cast<float*>(S.buf[blockIdx.y]);
     const int64_t total = count * kvh * hd;
@@ -121,9 +125,12 @@ __global__ void kv_read_q8_kernel(float* __restrict__ out, const int8_t* __restr
 // theta^(-2i / rope_dims) / factor_i and angle (start + position) * frequency
 // in double, cos and sin rounded to f32 (the reference's tables), then the
 // rotation in f32 with each product and sum rounded on its own.  Pairs are
-// (2i, 2i + 1) (adjacent) or (i, i + rope_dims / 2) (neox).
+// (2i, 2i + 1) (adjacent) or (i, i + rope_dims / 2) (neox).  Under
+// programmatic dependent launch the first angle's cos and sin are formed
+// before the wait for the kernel that wrote the rows.
 __global__ void rope_kernel(float* __restrict__ x, int64_t count, int heads, int64_t ps, int64_t hs, int rope_dims,
                             int64_t start, double theta, const float* __restrict__ factors, int neox) {
+    pipe::allow_dependents();
     const int half = rope_dims / 2;
     const int64_t total = count * heads * half;
     for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total; e += (int64_t)gridDim.x * blockDim.x) {
@@ -134,6 +141,7 @@ __global__ void rope_kernel(float* __restrict__ x, int64_t count, int heads, int
         if (factors) freq /= (double)factors[i];
         const double angle = (double)(start + pos) * freq;
         const float c = (float)cos(angle), s = (float)sin(angle);
+        pipe::grid_dependency_wait();  // returns at once after the first time
         float* row = x + pos * ps + head * hs;
         const int j0 = neox ? i : 2 * i, j1 = neox ? i + half : 2 * i + 1;
         const float x0 = row[j0], x1 = row[j1];
@@ -736,16 +744,17 @@ int clq_kv_cache_update(clq_kv_cache* c, int layer, const float* k, const float*
     S.buf[0] = kv_buffer(c, layer, 0);
     S.buf[1] = kv_buffer(c, layer, 1);
     S.code_bytes = c->code_bytes;
+    cudaError_t e;
     if (c->type == CLQ_KV_F32) {
         const int64_t n = count * c->kvh * c->hd;
-        clq::kv_store_f32_kernel<<<dim3(clq::grid_for(n, 256), 2), 256, 0, s>>>(S, count, c->kvh, c->hd, pos_stride,
-                                                                                 head_stride, start);
+        e = clq::launch_pdl(clq::kv_store_f32_kernel, dim3(clq::grid_for(n, 256), 2), 256, 0, s, S, (int64_t)count,
+                            (int)c->kvh, (int)c->hd, (int64_t)pos_stride, (int64_t)head_stride, (int64_t)start);
     } else {
         const int64_t warps = count * c->kvh * c->groups;
-        clq::kv_store_q8_kernel<<<dim3(clq::grid_for(warps * 32, 256), 2), 256, 0, s>>>(S, count, c->kvh, c->hd, pos_stride,
-                                                                                         head_stride, start, c->err);
+        e = clq::launch_pdl(clq::kv_store_q8_kernel, dim3(clq::grid_for(warps * 32, 256), 2), 256, 0, s, S,
+                            (int64_t)count, (int)c->kvh, (int)c->hd, (int64_t)pos_stride, (int64_t)head_stride,
+                            (int64_t)start, (int*)c->err);
     }
-    const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return clq::set_error(CLQ_ERR_CUDA, "KV cache store: %s", cudaGetErrorString(e));
     return CLQ_OK;
 }
@@ -807,9 +816,10 @@ int clq_rope_device(float* x, int64_t count, int heads, int head_dim, int64_t po
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return kv_fail(CLQ_ERR_NO_DEVICE, "no CUDA device");
     const int64_t n = count * heads * (rope_dims / 2);
-    clq::rope_kernel<<<clq::grid_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
-        x, count, heads, pos_stride, head_stride, rope_dims, start, theta, factors, pairing == CLQ_ROPE_NEOX);
-    const cudaError_t e = cudaGetLastError();
+    const cudaError_t e = clq::launch_pdl(clq::rope_kernel, dim3(clq::grid_for(n, 256)), 256, 0, (cudaStream_t)stream, x,
+                                          (int64_t)count, (int)heads, (int64_t)pos_stride, (int64_t)head_stride,
+                                          (int)rope_dims, (int64_t)start, (double)theta, (const float*)factors,
+                                          (int)(pairing == CLQ_ROPE_NEOX));
     if (e != cudaSuccess) return clq::set_error(CLQ_ERR_CUDA, "RoPE launch: %s", cudaGetErrorString(e));
     return CLQ_OK;
 }
