@@ -479,7 +479,29 @@ int clq_linear_group_device(const clq_store* const* w, const int64_t* row_begin,
                  !clq::uses_gemm_tc(view_of(w[0], 0), xtype, m, flags);
     for (int i = 0; i < count && fused; i++)
         fused = row_begin[i] >= 0 && rows[i] > 0 && row_begin[i] + rows[i] <= w[i]->n && ldo[i] >= rows[i] && out[i];
-    if (!fused) {  // validation and any shape the fused kernel does not cover, one call each
+    if (!fused) {
+        // the tensor-core GEMM forms the shared activation image once
+        bool gemm = m > 0 && w[0]->k > 0 && w[0]->k % 256 == 0 && x && !(flags & ~(CLQ_MATH_FAST | CLQ_MATH_EXACT)) &&
+                    (xtype == CLQ_X_F32 || xtype == CLQ_X_BF16 || xtype == CLQ_X_F16) &&
+                    clq::uses_gemm_tc(view_of(w[0], 0), xtype, m, flags);
+        int device = -1;
+        if (gemm && current_device(&device)) gemm = false;  // the calls below report it
+        for (int i = 0; i < count && gemm; i++)
+            gemm = row_begin[i] >= 0 && rows[i] > 0 && row_begin[i] + rows[i] <= w[i]->n && ldo[i] >= rows[i] &&
+                   out[i] && w[i]->device == device;
+        if (gemm) {
+            clq::WeightView views[4];
+            const clq::WeightView* vp[4];
+            for (int i = 0; i < count; i++) {
+                views[i] = view_of(w[i], row_begin[i]);
+                vp[i] = &views[i];
+            }
+            const cudaError_t e =
+                clq::launch_linear_group_gemm(vp, rows, count, x, xtype, m, out, ldo, flags, (cudaStream_t)stream);
+            if (e == cudaSuccess) return CLQ_OK;
+            if (e != cudaErrorNotSupported) return cuda_fail(e, "grouped GEMM launch");
+        }
+        // validation and any other shape, one call each
         for (int i = 0; i < count; i++) {
             int rc = clq_linear_device(w[i], row_begin[i], rows[i], x, xtype, m, out[i], ldo[i], flags, stream);
             if (rc) return rc;

@@ -145,9 +145,18 @@ size_t gemm_tc_scratch_bytes(const GemmPlan& g);
 GemmPlan plan_gemm_tc_capped(int dtype, int64_t rows, int64_t k, int64_t m, size_t cap);
 bool gemm_tc_supported(const WeightView& w, int64_t m);
 // SCRATCH: gemm_tc_scratch_bytes(g) device bytes, 256-byte aligned, private to
-// this call until it completes on STREAM.
+// this call until it completes on STREAM.  PREPPED: SCRATCH already holds
+// the activation image of X for a plan with the same tn, image sizes and
+// exactness (an earlier call of a group), so it is not formed again.
 cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m, float* out,
-                           int64_t ldo, uint8_t* scratch, const GemmPlan& g, cudaStream_t stream);
+                           int64_t ldo, uint8_t* scratch, const GemmPlan& g, cudaStream_t stream,
+                           bool prepped = false);
+// Weights sharing one activation X (q/k/v, gate/up) through the tensor-core
+// GEMM with the activation image formed once; cudaErrorNotSupported (nothing
+// launched) when the members' plans do not share one image.
+cudaError_t launch_linear_group_gemm(const WeightView* const* w, const int64_t* rows, int count, const void* x,
+                                     int xtype, int64_t m, float* const* out, const int64_t* ldo, unsigned flags,
+                                     cudaStream_t stream);
 
 // Whether launch_linear takes the tensor-core GEMM for this request.
 bool uses_gemm_tc(const WeightView& w, int xtype, int64_t m, unsigned flags);

@@ -1107,7 +1107,7 @@ size_t gemm_tc_scratch_bytes(const GemmPlan& g) {
 bool gemm_tc_supported(const WeightView& w, int64_t m) { return w.k > 0 && w.k % 256 == 0 && m > 0; }
 
 cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m, float* out,
-                           int64_t ldo, uint8_t* scratch, const GemmPlan& g, cudaStream_t stream) {
+                           int64_t ldo, uint8_t* scratch, const GemmPlan& g, cudaStream_t stream, bool prepped) {
     auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
     // an expired wait is reported through the status word clq_device_status reads
     int* err = device_status_word();
@@ -1118,7 +1118,8 @@ cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int
     float* part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(us) + al(g.us_bytes));
     cudaError_t e = cudaSuccess;
     const unsigned prep_grid = (unsigned)(g.token_tiles * g.tn);
-    switch (xtype) {
+    switch (prepped ? -1 : xtype) {
+    case -1: break;
     case CLQ_X_F32:
         prep_x_kernel<float><<<prep_grid, 256, 0, stream>>>((const float*)x, m, w.k, g.tn, xs, us, xs_lo);
         break;

@@ -67,6 +67,34 @@ bool uses_gemm_tc(const WeightView& w, int xtype, int64_t m, unsigned flags) {
     return m >= gemm_min_m(w, gemm_exact(xtype, flags)) && gemm_tc_supported(w, m);
 }
 
+cudaError_t launch_linear_group_gemm(const WeightView* const* w, const int64_t* rows, int count, const void* x,
+                                     int xtype, int64_t m, float* const* out, const int64_t* ldo, unsigned flags,
+                                     cudaStream_t stream) {
+    if (count < 1 || count > 4 || !uses_gemm_tc(*w[0], xtype, m, flags)) return cudaErrorNotSupported;
+    const bool exact = gemm_exact(xtype, flags);
+    GemmPlan g[4];
+    size_t scratch_bytes = 0;
+    for (int i = 0; i < count; i++) {
+        if (w[i]->dtype != w[0]->dtype || w[i]->k != w[0]->k || !uses_gemm_tc(*w[i], xtype, m, flags))
+            return cudaErrorNotSupported;
+        g[i] = plan_gemm_tc(w[i]->dtype, rows[i], w[i]->k, m, exact, exact && xtype == CLQ_X_F32);
+        // one activation image for all: the same tokens per tile and image layout
+        if (g[i].tn != g[0].tn || g[i].xs_bytes != g[0].xs_bytes || g[i].us_bytes != g[0].us_bytes ||
+            g[i].xlo != g[0].xlo)
+            return cudaErrorNotSupported;
+        const size_t b = gemm_tc_scratch_bytes(g[i]);
+        if (b > scratch_bytes) scratch_bytes = b;
+    }
+    cudaError_t e = keep_pool_memory();
+    if (e != cudaSuccess) return e;
+    void* scratch = nullptr;
+    if ((e = cudaMallocAsync(&scratch, scratch_bytes, stream)) != cudaSuccess) return e;
+    for (int i = 0; i < count && e == cudaSuccess; i++)
+        e = launch_gemm_tc(*w[i], rows[i], x, xtype, m, out[i], ldo[i], (uint8_t*)scratch, g[i], stream, i > 0);
+    const cudaError_t f = cudaFreeAsync(scratch, stream);
+    return e != cudaSuccess ? e : f;
+}
+
 cudaError_t launch_linear(const WeightView& w, int64_t rows, const void* x, int xtype, int64_t m,
                           float* out, int64_t ldo, unsigned flags, cudaStream_t stream) {
     if (uses_gemm_tc(w, xtype, m, flags)) {

@@ -165,3 +165,26 @@ def test_exact_gemm_meets_the_reference_bound(cuda, clq, synth, oracle, dtype, n
     refb, magb = oracle.matmul_f64(dtype, xb.float().cpu().numpy(), data, n)
     assert np.all(np.abs(outb - refb) <= 1e-5 * magb + 1e-37)
     store.close()
+
+
+@pytest.mark.parametrize("dtype,m,xtype", [("q4_k", 128, "bfloat16"), ("q6_k", 64, "float32"), ("q4_0", 40, "float32")])
+def test_grouped_gemm_shares_one_activation_image(cuda, clq, synth, oracle, dtype, m, xtype):
+    """A group (q/k/v shapes) through the GEMM forms the activation image once
+    and gives each member the bits of its own call."""
+    torch = cuda
+    k = 2048
+    shapes = [512, 128, 300]
+    datas = [synth.packed_blocks(dtype, n, k, seed=70 + i) for i, n in enumerate(shapes)]
+    stores = [clq.Store(dtype, n, k, d) for n, d in zip(shapes, datas)]
+    x = torch.from_numpy(synth.activations(m, k, seed=m)).cuda().to(getattr(torch, xtype))
+    outs = clq.linear_group(stores, x)
+    xf = x.float().cpu().numpy()
+    for st, d, n, o in zip(stores, datas, shapes, outs):
+        single = st.linear(x).cpu().numpy()
+        got = o.cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), single.view(np.uint32))
+        ref, mag = oracle.matmul_f64(dtype, xf, d, n)
+        bound = 1e-5 if xtype == "float32" else 1e-3
+        assert np.all(np.abs(got.astype(np.float64) - ref) <= bound * mag + 1e-6)
+    for st in stores:
+        st.close()
