@@ -19,6 +19,7 @@
 // issuing, drains what it issued and frees its tensor memory.
 #include <algorithm>
 #include <cstdlib>
+#include <type_traits>
 
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -957,14 +958,36 @@ __global__ void __launch_bounds__(kTThreads, 1) gemm_q4k_tma_kernel(const __grid
 }
 
 // out[t * ldo + r] = sum over splits of part[split][t][r], fixed order.
+// V = 4: four consecutive r per thread (rows, ldo and out 16-byte aligned);
+// every split's load is issued before the sum, in batches of eight.
+template <int V>
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int64_t m, int64_t rows,
                                      float* __restrict__ out, int64_t ldo) {
-    const int64_t total = m * rows;
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        float s = 0.f;
-        for (int j = 0; j < splits; j++) s += part[j * total + i];
-        const int64_t t = i / rows, r = i % rows;
-        out[t * ldo + r] = s;
+    using Vec = typename std::conditional<V == 4, float4, float>::type;
+    const int64_t total = m * rows, rv = rows / V, nv = m * rv;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < nv; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / rv, r = (i - t * rv) * V;
+        const float* src = part + t * rows + r;
+        float acc[V];
+#pragma unroll
+        for (int c = 0; c < V; c++) acc[c] = 0.f;
+        for (int j0 = 0; j0 < splits; j0 += 8) {
+            Vec v[8];
+#pragma unroll
+            for (int b = 0; b < 8; b++)
+                if (j0 + b < splits) v[b] = *reinterpret_cast<const Vec*>(src + (int64_t)(j0 + b) * total);
+#pragma unroll
+            for (int b = 0; b < 8; b++) {
+                if (j0 + b < splits) {
+                    const float* f = reinterpret_cast<const float*>(&v[b]);
+#pragma unroll
+                    for (int c = 0; c < V; c++) acc[c] += f[c];
+                }
+            }
+        }
+        float* dst = out + t * ldo + r;
+        if constexpr (V == 4) *reinterpret_cast<float4*>(dst) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        else dst[0] = acc[0];
     }
 }
 
@@ -1189,9 +1212,11 @@ cudaError_t launch_gemm_tc(const WeightView& w, int64_t rows, const void* x, int
         }
     }
     if (e != cudaSuccess || g.splits == 1) return e;
-    const int64_t total = m * rows;
-    const int rb = (int)((total + 255) / 256 < 148 * 8 ? (total + 255) / 256 : 148 * 8);
-    splitk_reduce_kernel<<<rb, 256, 0, stream>>>(part, g.splits, m, rows, out, ldo);
+    const bool vec = rows % 4 == 0 && ldo % 4 == 0 && (uintptr_t)out % 16 == 0;
+    const int64_t items = m * rows / (vec ? 4 : 1);
+    const int rb = (int)((items + 255) / 256 < 148 * 8 ? (items + 255) / 256 : 148 * 8);
+    if (vec) splitk_reduce_kernel<4><<<rb, 256, 0, stream>>>(part, g.splits, m, rows, out, ldo);
+    else splitk_reduce_kernel<1><<<rb, 256, 0, stream>>>(part, g.splits, m, rows, out, ldo);
     return cudaGetLastError();
 }
 
