@@ -305,6 +305,15 @@ __device__ __forceinline__ void load_raw(const Planes& p, int64_t grow, int64_t 
     }
 }
 
+// Q4_K block KB after the first of its superblock: the header HD of the
+// block before (the same superblock) and this block's codes.
+__device__ __forceinline__ void load_codes_q4k(const Planes& p, int64_t grow, int64_t kb, int hv, const uint4& hd,
+                                               Raw<kQ4_K>& r) {
+    const uint8_t* b = p.q + (grow * p.nb + (kb >> 2)) * 144;
+    r.hd = hd;
+    r.cw = *reinterpret_cast<const uint4*>(b + 16 + 32 * (int)(kb & 3) + 16 * hv);
+}
+
 // Half hv of row `row`: four of its eight 16-byte chunks -- {2hv, 2hv+1,
 // 4+2hv, 5+2hv} for Q4_K/Q4_0/Q8_0 (elements 16hv..16hv+15 of each 32),
 // {hv, 2+hv, 4+hv, 6+hv} for Q6_K (lane quads 2hv, 2hv+1).
@@ -604,7 +613,17 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
         if (nk > 1) load_raw<D>(P.p, grow, kb0 + 1, hv, r1);
         for (int it = 0; it < nk; it++) {
             const int s = it % NS;
-            if (it + 2 < nk) load_raw<D>(P.p, grow, kb0 + it + 2, hv, r2);  // two stages in flight
+            if (it + 2 < nk) {  // two stages in flight
+                const int64_t kb = kb0 + it + 2;
+                if (D == kQ6_K && (kb & 1)) {
+                    r2 = r1;  // Q6_K: an odd block reads the even block's words, sub-scales and scale
+                } else if constexpr (D == kQ4_K) {
+                    if (kb & 3) load_codes_q4k(P.p, grow, kb, hv, r1.hd, r2);  // the superblock's header again
+                    else load_raw<D>(P.p, grow, kb, hv, r2);
+                } else {
+                    load_raw<D>(P.p, grow, kb, hv, r2);
+                }
+            }
             if (it >= NS && !mbar_wait(&empty[s], ((it / NS) - 1) & 1, err)) break;
             if constexpr (EXACT)
                 convert_raw_exact<D>(P.p, grow, kb0 + it, hv, r0, row, A + (size_t)s * kA, A + (size_t)s * kA + kTM * 128);
