@@ -260,6 +260,28 @@ template <> struct Raw<kQ6_K> { uint32_t w[12]; uint4 sv; uint32_t d; };  // lan
 template <> struct Raw<kQ4_0> { uint32_t w[2][4]; uint32_t d2; };
 template <> struct Raw<kQ8_0> { uint32_t w[2][4]; uint32_t d2; };
 
+// Q6_K block KB's code words for lane quads 2hv, 2hv + 1 (superblock BLK).
+__device__ __forceinline__ void load_words_q6k(const Planes& p, int64_t blk, int64_t kb, int hv, Raw<kQ6_K>& r) {
+    // lane-major plane (layout.cuh): lane quad t's words for (hh, half) sit at
+    // t*48 + (2hh + half)*12; the 24 bytes of one hh start 16-byte aligned
+    // when hh = 0 and 8 bytes past alignment when hh = 1 (warp-uniform).
+    const int hh = (int)((kb & 3) >> 1);
+#pragma unroll
+    for (int tq = 0; tq < 2; tq++) {
+        const uint8_t* q = p.q + blk * 192 + (2 * hv + tq) * 48 + 24 * hh;
+        uint32_t* w = &r.w[6 * tq];
+        if (hh == 0) {
+            const uint4 a = *reinterpret_cast<const uint4*>(q);
+            const uint2 b = *reinterpret_cast<const uint2*>(q + 16);
+            w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y;
+        } else {
+            const uint2 a = *reinterpret_cast<const uint2*>(q);
+            const uint4 b = *reinterpret_cast<const uint4*>(q + 8);
+            w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y; w[4] = b.z; w[5] = b.w;
+        }
+    }
+}
+
 template <int D>
 __device__ __forceinline__ void load_raw(const Planes& p, int64_t grow, int64_t kb, int hv, Raw<D>& r) {
     if constexpr (D == kQ4_K) {
@@ -269,24 +291,7 @@ __device__ __forceinline__ void load_raw(const Planes& p, int64_t grow, int64_t 
         r.cw = *reinterpret_cast<const uint4*>(b + 16 + 32 * qt + 16 * hv);
     } else if constexpr (D == kQ6_K) {
         const int64_t blk = grow * p.nb + (kb >> 2);
-        // lane-major plane (layout.cuh): lane quad t's words for (hh, half) sit at
-        // t*48 + (2hh + half)*12; the 24 bytes of one hh start 16-byte aligned
-        // when hh = 0 and 8 bytes past alignment when hh = 1 (warp-uniform).
-        const int hh = (int)((kb & 3) >> 1);
-#pragma unroll
-        for (int tq = 0; tq < 2; tq++) {
-            const uint8_t* q = p.q + blk * 192 + (2 * hv + tq) * 48 + 24 * hh;
-            uint32_t* w = &r.w[6 * tq];
-            if (hh == 0) {
-                const uint4 a = *reinterpret_cast<const uint4*>(q);
-                const uint2 b = *reinterpret_cast<const uint2*>(q + 16);
-                w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w; w[4] = b.x; w[5] = b.y;
-            } else {
-                const uint2 a = *reinterpret_cast<const uint2*>(q);
-                const uint4 b = *reinterpret_cast<const uint4*>(q + 8);
-                w[0] = a.x; w[1] = a.y; w[2] = b.x; w[3] = b.y; w[4] = b.z; w[5] = b.w;
-            }
-        }
+        load_words_q6k(p, blk, kb, hv, r);
         r.sv = *reinterpret_cast<const uint4*>(p.s + blk * 16);
         r.d = *reinterpret_cast<const unsigned short*>(p.d + 2 * blk);
     } else {
@@ -617,6 +622,14 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
                 const int64_t kb = kb0 + it + 2;
                 if (D == kQ6_K && (kb & 1)) {
                     r2 = r1;  // Q6_K: an odd block reads the even block's words, sub-scales and scale
+                } else if constexpr (D == kQ6_K) {
+                    if (kb & 3) {  // the third block: new words, the superblock's sub-scales and scale again
+                        load_words_q6k(P.p, grow * P.p.nb + (kb >> 2), kb, hv, r2);
+                        r2.sv = r1.sv;
+                        r2.d = r1.d;
+                    } else {
+                        load_raw<D>(P.p, grow, kb, hv, r2);
+                    }
                 } else if constexpr (D == kQ4_K) {
                     if (kb & 3) load_codes_q4k(P.p, grow, kb, hv, r1.hd, r2);  // the superblock's header again
                     else load_raw<D>(P.p, grow, kb, hv, r2);
