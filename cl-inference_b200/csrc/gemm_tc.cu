@@ -300,12 +300,28 @@ __device__ __forceinline__ void load_raw(const Planes& p, int64_t grow, int64_t 
         constexpr int CB = D == kQ4_0 ? 16 : 32, words = CB / 16;
         const int64_t j0 = 2 * kb, c = j0 / 8, b = j0 % 8;
         const int64_t nbc = p.nb - 8 * c < 8 ? p.nb - 8 * c : 8;
-        const uint8_t* base = p.q + grow * p.nb * CB + c * 8 * CB + (D == kQ8_0 ? 4 * hv : 0);
+        const uint8_t* base = p.q + grow * p.nb * CB + c * 8 * CB;
+        if (!(nbc & 1)) {  // blocks b, b + 1 adjacent and aligned: one load per lane quad
 #pragma unroll
-        for (int jb = 0; jb < 2; jb++)
+            for (int t = 0; t < 4; t++) {
+                if constexpr (D == kQ4_0) {
+                    const uint2 v = *reinterpret_cast<const uint2*>(base + (t * nbc + b) * 4);
+                    r.w[0][t] = v.x;
+                    r.w[1][t] = v.y;
+                } else {
+                    const uint4 v = *reinterpret_cast<const uint4*>(base + (t * nbc + b) * 8);
+                    r.w[0][t] = hv ? v.y : v.x;
+                    r.w[1][t] = hv ? v.w : v.z;
+                }
+            }
+        } else {
 #pragma unroll
-            for (int t = 0; t < 4; t++)
-                r.w[jb][t] = *reinterpret_cast<const uint32_t*>(base + (t * nbc + b + jb) * 4 * words);
+            for (int jb = 0; jb < 2; jb++)
+#pragma unroll
+                for (int t = 0; t < 4; t++)
+                    r.w[jb][t] = *reinterpret_cast<const uint32_t*>(base + (D == kQ8_0 ? 4 * hv : 0) +
+                                                                    (t * nbc + b + jb) * 4 * words);
+        }
         r.d2 = *reinterpret_cast<const uint32_t*>(p.d + 2 * (grow * p.nb + j0));
     }
 }
