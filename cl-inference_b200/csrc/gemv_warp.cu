@@ -51,6 +51,7 @@
 #include <cuda_fp16.h>
 
 #include "../../include/clq.h"
+#include "fusion.cuh"
 #include "clq_internal.h"
 #include "gemv_common.cuh"
 #include "gemv_i8.cuh"
@@ -129,9 +130,8 @@ __device__ __forceinline__ float ld_cluster_f32(const float* local, uint32_t ran
 // W = min(16, U) warps in use, all non-empty.
 __device__ __forceinline__ int warp_of(int u, int U, int W) { return (W * (u + 1) + U - 1) / U - 1; }
 
-// The product's input element from activation X and gate G: silu(g) * x with a
-// gate, else x.
-__device__ __forceinline__ float swiglu_in(float x, float g) { return g / (1.f + expf(-g)) * x; }
+// The product's input element from activation X and gate G (fusion.cuh).
+__device__ __forceinline__ float swiglu_in(float x, float g) { return swiglu(g, x); }
 
 // The fused prologue as a staging transform: the gate and norm-weight words
 // are loaded beside the activations (one round trip for all three), then

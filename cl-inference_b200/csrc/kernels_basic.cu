@@ -7,6 +7,7 @@
 #include "../../include/clq.h"
 #include "clq_internal.h"
 #include "formats.cuh"
+#include "fusion.cuh"
 #include "layout.cuh"
 
 namespace clq {
@@ -279,7 +280,7 @@ __global__ void fuse_input_kernel(const XT* x, const XT* gate, const float* norm
         float v = act(xr + e);
         if (gr) {
             const float g = act(gr + e);
-            v = g / (1.f + expf(-g)) * v;
+            v = swiglu(g, v);
         }
         return v;
     };
