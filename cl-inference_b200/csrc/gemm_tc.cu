@@ -326,12 +326,9 @@ __device__ __forceinline__ void load_raw(const Planes& p, int64_t grow, int64_t 
     }
 }
 
-// Q4_K block KB after the first of its superblock: the header HD of the
-// block before (the same superblock) and this block's codes.
-__device__ __forceinline__ void load_codes_q4k(const Planes& p, int64_t grow, int64_t kb, int hv, const uint4& hd,
-                                               Raw<kQ4_K>& r) {
+// Q4_K block KB's codes only (its header is its superblock's first block's).
+__device__ __forceinline__ void load_codes_q4k(const Planes& p, int64_t grow, int64_t kb, int hv, Raw<kQ4_K>& r) {
     const uint8_t* b = p.q + (grow * p.nb + (kb >> 2)) * 144;
-    r.hd = hd;
     r.cw = *reinterpret_cast<const uint4*>(b + 16 + 32 * (int)(kb & 3) + 16 * hv);
 }
 
@@ -629,28 +626,48 @@ __global__ void __launch_bounds__(kThreads, 1) gemm_tc_kernel(GemmParams P) {
         const int hv = threadIdx.x >> 7;
         const int64_t grow_u = row0 + row;
         const int64_t grow = grow_u < P.rows ? grow_u : P.rows - 1;
+        // Each packed word is loaded once: a Q4_K block after the first of its
+        // superblock loads only its codes (the header is kept from the first);
+        // an odd Q6_K block loads nothing (it reads the even block's words,
+        // sub-scales and scale) and the third block of a superblock only its
+        // words.  The kept parts are filled in when a block is converted, from
+        // blocks already in registers, so no copy waits on a load in flight.
         Raw<D> r0, r1, r2;  // stages it, it+1, it+2
+        Raw<D> even;        // Q6_K: the last even block converted
+        uint4 hd_sb = {};   // Q4_K: the current superblock's header
+        (void)even;
+        (void)hd_sb;
         if (nk > 0) load_raw<D>(P.p, grow, kb0, hv, r0);
         if (nk > 1) load_raw<D>(P.p, grow, kb0 + 1, hv, r1);
         for (int it = 0; it < nk; it++) {
             const int s = it % NS;
             if (it + 2 < nk) {  // two stages in flight
                 const int64_t kb = kb0 + it + 2;
-                if (D == kQ6_K && (kb & 1)) {
-                    r2 = r1;  // Q6_K: an odd block reads the even block's words, sub-scales and scale
-                } else if constexpr (D == kQ6_K) {
-                    if (kb & 3) {  // the third block: new words, the superblock's sub-scales and scale again
-                        load_words_q6k(P.p, grow * P.p.nb + (kb >> 2), kb, hv, r2);
-                        r2.sv = r1.sv;
-                        r2.d = r1.d;
-                    } else {
-                        load_raw<D>(P.p, grow, kb, hv, r2);
+                if constexpr (D == kQ6_K) {
+                    if (!(kb & 1)) {
+                        if (kb & 3) load_words_q6k(P.p, grow * P.p.nb + (kb >> 2), kb, hv, r2);
+                        else load_raw<D>(P.p, grow, kb, hv, r2);
                     }
                 } else if constexpr (D == kQ4_K) {
-                    if (kb & 3) load_codes_q4k(P.p, grow, kb, hv, r1.hd, r2);  // the superblock's header again
+                    if (kb & 3) load_codes_q4k(P.p, grow, kb, hv, r2);
                     else load_raw<D>(P.p, grow, kb, hv, r2);
                 } else {
                     load_raw<D>(P.p, grow, kb, hv, r2);
+                }
+            }
+            const int64_t b = kb0 + it;
+            if constexpr (D == kQ4_K) {  // the first two blocks were loaded whole
+                if (it < 2 || !(b & 3)) hd_sb = r0.hd;
+                else r0.hd = hd_sb;
+            } else if constexpr (D == kQ6_K) {
+                if (it >= 2 && (b & 1)) {
+                    r0 = even;
+                } else {
+                    if (it >= 2 && (b & 3)) {
+                        r0.sv = even.sv;
+                        r0.d = even.d;
+                    }
+                    even = r0;
                 }
             }
             if (it >= NS && !mbar_wait(&empty[s], ((it / NS) - 1) & 1, err)) break;
