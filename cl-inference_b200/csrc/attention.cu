@@ -231,9 +231,19 @@ __device__ __forceinline__ void stage_kv(const AttnParams& P, int64_t p0, int np
                 const int f = val ? e - n : e, j = f / per_row, c = f - j * per_row;
                 if constexpr (Q8) {
                     const uint32_t ws[4] = {w[b].x, w[b].y, w[b].z, w[b].w};
-                    float* o = (val ? vs + j * hd : ks + j * ldk) + c * 16;
+                    float4* o = reinterpret_cast<float4*>((val ? vs + j * hd : ks + j * ldk) + c * 16);
+                    // q8_decode's single-precision case for all 16 codes at once
+                    const bool fast = (double)sc[b] <= (double)FLT_MAX / 127.0;
 #pragma unroll
-                    for (int i = 0; i < 16; i++) o[i] = q8_decode((int8_t)(ws[i >> 2] >> (8 * (i & 3))), sc[b]);
+                    for (int q = 0; q < 4; q++) {
+                        float f[4];
+#pragma unroll
+                        for (int i = 0; i < 4; i++) {
+                            const int8_t code = (int8_t)(ws[q] >> (8 * i));
+                            f[i] = fast ? __fmul_rn((float)code, sc[b]) : q8_decode(code, sc[b]);
+                        }
+                        o[q] = make_float4(f[0], f[1], f[2], f[3]);
+                    }
                 } else {
                     *reinterpret_cast<uint4*>((val ? vs + j * hd : ks + j * ldk) + c * 4) = w[b];
                 }
