@@ -611,11 +611,12 @@ cudaError_t launch_gemv_bulk_impl(const WeightView* const* w, const int64_t* row
     };
     if (!bulk_enabled() || m < 1 || m > kMaxPassRows || count < 1 || count > kGroup) return cudaErrorNotSupported;
     if (m <= 8) {
-        // up to eight activation rows of Q4_K / Q6_K: the per-warp streams when their plan fits
+        // up to eight activation rows: the per-warp streams when their plan fits
         const cudaError_t ew = launch_gemv_warp(w, rows, count, x, xtype, m, out, ldo, tp, stream);
         if (ew != cudaErrorNotSupported) return ew;
     }
-    if (!tp) {
+    // passes for the K formats; Q4_0 / Q8_0 beyond eight rows keep the register-fed kernel
+    if (!tp && (w[0]->dtype == kQ4_K || w[0]->dtype == kQ6_K)) {
         for (int64_t step : {8, 4, 2}) {
             if (step >= m) continue;
             const cudaError_t e = passes(step);

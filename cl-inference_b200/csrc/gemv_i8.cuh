@@ -1,5 +1,6 @@
-// gemv_i8.cuh -- decode GEMV compute on the integer tensor-core MMA for Q4_K and
-// Q6_K at one or two activation rows, and at up to four pairs of rows.
+// gemv_i8.cuh -- decode GEMV compute on the integer tensor-core MMA for Q4_K,
+// Q6_K, Q4_0 and Q8_0 at one or two activation rows, and at up to four pairs
+// of rows.
 //
 // Codes become unsigned bytes with one AND per four weights (Q4_K high nibbles
 // stay in place as 16 q; Q6_K adds a shift and an OR for its high bits) -- no
@@ -18,7 +19,10 @@
 // (-32 d sum_j sc_j X_j) are one fp16 MMA per chunk on hi + lo halves of the
 // sub-block sums, as in gemv_common.cuh.  The result carries fp32-class error:
 // the fixed-point image keeps 30 bits relative to the chunk's largest
-// activation, and the digit and term sums are formed in fp32.
+// activation, and the digit and term sums are formed in fp32.  Q4_0 and Q8_0
+// take one m16n8k32 MMA per 32-element block (Q8_0 codes as signed bytes, s8 x
+// s8) and apply each block's fp16 scale in fp32; Q4_0's offset term
+// (-8 sum_b d_b X_b) is one fp16 MMA per chunk like Q4_K's min term.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -37,6 +41,15 @@ __device__ __forceinline__ void imma_k32(int (&c)[4], uint32_t a0, uint32_t a1, 
         : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
         : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
 }
+// The same with signed A bytes (Q8_0 codes).
+__device__ __forceinline__ void imma_k32_ss(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
 __device__ __forceinline__ void imma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
     asm volatile(
         "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%7,%7,%7,%7};"
@@ -50,6 +63,10 @@ __device__ __forceinline__ void imma_k16(int (&c)[4], uint32_t a0, uint32_t a1, 
 template <int D> struct I8Block;
 template <> struct I8Block<kQ4_K> { static constexpr int sf = 32, bytes = 1024 + 32 + 16; };
 template <> struct I8Block<kQ6_K> { static constexpr int sf = 64, bytes = 1024 + 64 + 16; };
+// Q4_0 / Q8_0: 32-element blocks like Q4_K's sub-blocks, digits in the
+// blocks' own element order (below)
+template <> struct I8Block<kQ4_0> { static constexpr int sf = 32, bytes = 1024 + 32 + 16; };
+template <> struct I8Block<kQ8_0> { static constexpr int sf = 32, bytes = 1024 + 32 + 16; };
 
 // The four balanced base-256 digits of X (|X| < 2^30) as the bytes of one word,
 // least significant first: adding 128 to each of the three low digit positions
@@ -78,6 +95,9 @@ __device__ __forceinline__ void transpose4(uint32_t v0, uint32_t v1, uint32_t v2
 //               Q6_K uint4 at ((hh*4 + dg)*4 + tt) = word grp (0..3) for group
 //               hh*4 + grp, elements 16 half + 4tt.. of (h, half) = hh
 //               (k-slots 4tt..4tt+3);
+//               Q4_0 / Q8_0 uint4 at ((j*4 + dg)*4 + tt) = blocks 2j and 2j+1,
+//               elements 4tt..4tt+3 and 16+4tt..16+4tt+3 of each (k-slot =
+//               element, the order of the lane-major code planes);
 //   [1024, +sf) hi / lo fp16 halves of the sums S of X over the sub-blocks
 //               (Q4_K: uint32 pair (S_2t, S_2t+1) at (t*2 + part)) or groups
 //               (Q6_K: uint2 at (t*2 + part), pairs (2t, 2t+1) and (8+2t, 9+2t)),
@@ -114,12 +134,24 @@ __device__ __forceinline__ void stage_block_i8(const float (&v)[8], unsigned cha
     uint32_t d03[4], d47[4];  // [digit position 0 = least significant]
     transpose4(V[0], V[1], V[2], V[3], d03);
     transpose4(V[4], V[5], V[6], V[7], d47);
-    if constexpr (D == kQ4_K) {
-        const int s = lane >> 2, tt = lane & 3;  // sub-block s, elements 8tt..
-        uint2* xq = reinterpret_cast<uint2*>(base);
+    if constexpr (D == kQ4_K || D == kQ4_0 || D == kQ8_0) {
+        const int s = lane >> 2, tt = lane & 3;  // sub-block (block) s, elements 8tt..
+        if constexpr (D == kQ4_K) {
+            uint2* xq = reinterpret_cast<uint2*>(base);
 #pragma unroll
-        for (int dg = 0; dg < 4; dg++)
-            xq[(((s >> 1) * 4 + dg) * 4 + tt) * 2 + (s & 1)] = make_uint2(d03[3 - dg], d47[3 - dg]);
+            for (int dg = 0; dg < 4; dg++)
+                xq[(((s >> 1) * 4 + dg) * 4 + tt) * 2 + (s & 1)] = make_uint2(d03[3 - dg], d47[3 - dg]);
+        } else {
+            // elements 8tt..8tt+3 are k-slots of fragment lane 2 (tt & 1), half
+            // tt >> 1 (b0 below 16, b1 from 16); 8tt+4.. those of the next lane
+            uint32_t* xq = reinterpret_cast<uint32_t*>(base);
+            const int f0 = 2 * (tt & 1), part = tt >> 1;
+#pragma unroll
+            for (int dg = 0; dg < 4; dg++) {
+                xq[((((s >> 1) * 4 + dg) * 4 + f0) * 4) + (s & 1) * 2 + part] = d03[3 - dg];
+                xq[((((s >> 1) * 4 + dg) * 4 + f0 + 1) * 4) + (s & 1) * 2 + part] = d47[3 - dg];
+            }
+        }
         fsum += __shfl_xor_sync(0xffffffffu, fsum, 1);
         fsum += __shfl_xor_sync(0xffffffffu, fsum, 2);  // lanes 4s..4s+3: S_s
         const float S = fsum * 4.76837158203125e-07f;  // 2^-21
@@ -434,7 +466,7 @@ __device__ __forceinline__ I8LaneN<D, NP> i8_lane_n(int ntok) {
 #pragma unroll
     for (int q = 0; q < I8LaneN<D, NP>::NQ; q++) {
         const int tm = min(4 * q + (L.g >> 1), ntok - 1);
-        L.xm[q] = tm * TB + 1024 + (L.t * 2 + part) * (D == kQ4_K ? 4 : 8);
+        L.xm[q] = tm * TB + 1024 + (L.t * 2 + part) * (D == kQ6_K ? 8 : 4);
         L.um[q] = min(4 * q + L.t, ntok - 1) * TB + 1024 + I8Block<D>::sf;
     }
     return L;
@@ -579,6 +611,117 @@ __device__ __forceinline__ void q6k_i8_chunk_n(const I8LaneN<kQ6_K, NP>& L, cons
         const float uo = *reinterpret_cast<const float*>(xs + L.um[q]) * 67108864.f;
 #pragma unroll
         for (int h = 0; h < 2; h++) accn[q][h] = fmaf(d[h] * uo, co[2 * h] + co[2 * h + 1], accn[q][h]);
+    }
+}
+
+// The fp16 scales of row g + 8h's eight blocks, DW[h] (16 bytes), as floats.
+__device__ __forceinline__ void block_scales(const uint4 (&DW)[2], float (&dd)[2][8]) {
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const uint32_t w[4] = {DW[h].x, DW[h].y, DW[h].z, DW[h].w};
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            dd[h][2 * i] = lo_half(w[i]);
+            dd[h][2 * i + 1] = hi_half(w[i]);
+        }
+    }
+}
+
+// One block's MMA result C (rows g, g + 8; this lane's digit columns) into
+// the chunk's block-scaled sums ACCF: the two digit columns weigh 256 : 1
+// (their common factor, L.wb, is applied with the chunk's unscale), so one
+// integer multiply-add joins them (|C| < 2^19, the sum < 2^28).
+__device__ __forceinline__ void block_sum(const int (&c)[4], float d0, float d1, float (&accf)[2]) {
+    accf[0] = fmaf(d0, (float)(c[0] * 256 + c[1]), accf[0]);
+    accf[1] = fmaf(d1, (float)(c[2] * 256 + c[3]), accf[1]);
+}
+
+// Q8_0 over NP pairs, one chunk (eight blocks): QV[h][i] = this lane's 16
+// code bytes of blocks 2i, 2i + 1 in row g + 8h (per block: elements
+// 4t..4t+3, then 16+4t..16+4t+3); DW[h] = the row's eight fp16 scales.
+// Codes are signed bytes: one s8 x s8 MMA per block and pair, no offset term.
+template <int NP>
+__device__ __forceinline__ void q8_0_i8_chunk_n(const I8LaneN<kQ8_0, NP>& L, const uint4 (&QV)[2][4],
+                                                const uint4 (&DW)[2], const unsigned char* xs,
+                                                float (&accm)[NP][2]) {
+    float dd[2][8];
+    block_scales(DW, dd);
+    float accf[NP][2];
+#pragma unroll
+    for (int p = 0; p < NP; p++) accf[p][0] = accf[p][1] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+#pragma unroll
+        for (int p = 0; p < NP; p++) {
+            const uint4 b = reinterpret_cast<const uint4*>(xs + L.xb[p])[16 * j];
+            int c[4];
+            imma_k32_ss(c, QV[0][j].x, QV[1][j].x, QV[0][j].y, QV[1][j].y, b.x, b.y);
+            block_sum(c, dd[0][2 * j], dd[1][2 * j], accf[p]);
+            imma_k32_ss(c, QV[0][j].z, QV[1][j].z, QV[0][j].w, QV[1][j].w, b.z, b.w);
+            block_sum(c, dd[0][2 * j + 1], dd[1][2 * j + 1], accf[p]);
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+        const float ut = *reinterpret_cast<const float*>(xs + L.ua[p]) * L.wb;
+#pragma unroll
+        for (int h = 0; h < 2; h++) accm[p][h] = fmaf(ut, accf[p][h], accm[p][h]);
+    }
+}
+
+// Q4_0 over NP pairs, one chunk: QW[h][b] = this lane's code word of block b
+// in row g + 8h (low nibbles elements 4t..4t+3, high nibbles 16+4t..);
+// DW[h] = the row's eight fp16 scales.  Codes enter the u8 x s8 MMA as they
+// are (0..15); the offset term 8 sum_b d_b S_b (to be subtracted) is one fp16
+// MMA per chunk and group of four rows: A = the scales of blocks 2t, 2t + 1
+// (fp16, exact), B = hi + lo halves of the block sums of X.
+template <int NP>
+__device__ __forceinline__ void q4_0_i8_chunk_n(const I8LaneN<kQ4_0, NP>& L, const uint32_t (&QW)[2][8],
+                                                const uint4 (&DW)[2], const unsigned char* xs,
+                                                float (&accm)[NP][2], float (&accn)[(NP + 1) / 2][2]) {
+    constexpr int NQ = (NP + 1) / 2;
+    float dd[2][8];
+    block_scales(DW, dd);
+    float accf[NP][2];
+#pragma unroll
+    for (int p = 0; p < NP; p++) accf[p][0] = accf[p][1] = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int b = 2 * j + e;
+            const uint32_t lo0 = QW[0][b] & 0x0F0F0F0Fu, lo1 = QW[1][b] & 0x0F0F0F0Fu;
+            const uint32_t hi0 = (QW[0][b] >> 4) & 0x0F0F0F0Fu, hi1 = (QW[1][b] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int p = 0; p < NP; p++) {
+                const uint4 bx = reinterpret_cast<const uint4*>(xs + L.xb[p])[16 * j];
+                int c[4];
+                imma_k32(c, lo0, lo1, hi0, hi1, e ? bx.z : bx.x, e ? bx.w : bx.y);
+                block_sum(c, dd[0][b], dd[1][b], accf[p]);
+            }
+        }
+    }
+#pragma unroll
+    for (int p = 0; p < NP; p++) {
+        const float ut = *reinterpret_cast<const float*>(xs + L.ua[p]) * L.wb;
+#pragma unroll
+        for (int h = 0; h < 2; h++) accm[p][h] = fmaf(ut, accf[p][h], accm[p][h]);
+    }
+    // the scales of blocks 2t, 2t + 1: word t of each row's scales (selects,
+    // not an index, so DW stays in registers)
+    uint32_t am[2];
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+        const uint32_t a01 = (L.t & 1) ? DW[h].y : DW[h].x, a23 = (L.t & 1) ? DW[h].w : DW[h].z;
+        am[h] = (L.t & 2) ? a23 : a01;
+    }
+#pragma unroll
+    for (int q = 0; q < NQ; q++) {
+        float cm[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816(cm, am[0], am[1], 0u, 0u, *reinterpret_cast<const uint32_t*>(xs + L.xm[q]), 0u);
+        const float u8 = *reinterpret_cast<const float*>(xs + L.um[q]) * 16777216.f;  // times 8 * 2^21
+#pragma unroll
+        for (int h = 0; h < 2; h++) accn[q][h] = fmaf(u8, cm[2 * h] + cm[2 * h + 1], accn[q][h]);
     }
 }
 

@@ -1,5 +1,5 @@
-// gemv_warp.cu -- decode GEMV (one to eight activation rows) for Q4_K and Q6_K
-// with an independent weight stream per warp.
+// gemv_warp.cu -- decode GEMV (one to eight activation rows) for Q4_K, Q6_K,
+// Q4_0 and Q8_0 with an independent weight stream per warp.
 //
 // One persistent CTA of 16 warps per SM owns a contiguous range of 16-row
 // tiles.  Its (tile, chunk) units -- 16 rows x 256 columns, tile-major -- are
@@ -80,10 +80,19 @@ constexpr size_t kWSmemLimit = 227 * 1024;
 constexpr int kWPreWait = 2;
 
 // Bytes of one row of one unit in the q plane (the whole unit's data for Q4_K;
-// Q6_K's sub-scales and scale, 9% of its bytes, are read with plain loads).
+// Q6_K's sub-scales and scale, 9% of its bytes, and the fp16 block scales of
+// Q4_0 / Q8_0, 11% and 6%, are read with plain loads).  SWZ: the unit lands
+// in shared memory under the 128-byte swizzle (16-byte chunk c of 128-byte
+// line l at chunk c ^ (l & 7)), so that the lanes' 16-byte reads of rows
+// 256 or 128 bytes apart spread over all banks.
 template <int D> struct WGeo;
-template <> struct WGeo<kQ4_K> { static constexpr int q = 144; };
-template <> struct WGeo<kQ6_K> { static constexpr int q = 192; };
+template <> struct WGeo<kQ4_K> { static constexpr int q = 144; static constexpr bool swz = false; };
+template <> struct WGeo<kQ6_K> { static constexpr int q = 192; static constexpr bool swz = false; };
+template <> struct WGeo<kQ4_0> { static constexpr int q = 128; static constexpr bool swz = true; };
+template <> struct WGeo<kQ8_0> { static constexpr int q = 256; static constexpr bool swz = true; };
+
+// Offset of 16-byte chunk C of 128-byte line L in a swizzled slot.
+__device__ __forceinline__ int swz_off(int l, int c) { return l * 128 + ((c ^ (l & 7)) << 4); }
 
 struct WarpParams {
     CUtensorMap maps[kGroup];  // q plane of each member: [rows][K / 256 * Q] bytes, box 16 x Q
@@ -211,7 +220,11 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
     const int W = U < kWW ? U : kWW;
     const int u0 = warp < W ? warp * U / W : 0, u1 = warp < W ? (warp + 1) * U / W : 0;
     uint64_t* bar = bars + warp * kWMaxDepth;
-    unsigned char* ring = smem + P.ring_off + (size_t)warp * depth * kSlot;
+    unsigned char* rings = smem + P.ring_off;
+    // the swizzle pattern repeats every 1024 bytes of shared memory: swizzled
+    // slots start on that boundary (the plan leaves room to round up)
+    if constexpr (WGeo<D>::swz) rings += (1024u - (smem_u32(rings) & 1023u)) & 1023u;
+    unsigned char* ring = rings + (size_t)warp * depth * kSlot;
     int* err = P.err;
 
     if (lane == 0) {
@@ -228,8 +241,14 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
         if (lane == 0) {
             const int mi = member_of(P, (int64_t)itile);
             mbar_arrive_tx(&bar[islot], kSlot);
-            tensor_copy_2d_hint(ring + islot * kSlot, &P.maps[mi], (kc0 + ic) * Q,
-                                (itile - (int)P.mem[mi].tile_begin) * 16, &bar[islot], policy);
+            const int row0 = (itile - (int)P.mem[mi].tile_begin) * 16;
+            if constexpr (D == kQ8_0) {
+                // the 3-D map's box: two 128-byte halves of the chunk x 16 rows
+                tensor_copy_3d_hint(ring + islot * kSlot, &P.maps[mi], 0, 2 * (kc0 + ic), row0, &bar[islot],
+                                    policy);
+            } else {
+                tensor_copy_2d_hint(ring + islot * kSlot, &P.maps[mi], (kc0 + ic) * Q, row0, &bar[islot], policy);
+            }
         }
         ++issued;
         if (++islot == depth) islot = 0;
@@ -304,6 +323,7 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
     int done = u0;
 
     // Q6_K sub-scales and scale of rows g, g + 8 for a unit, one unit ahead
+    // (Q4_0 / Q8_0: the rows' eight block scales, 16 bytes each, in s_*)
     uint4 s_cur[2] = {}, s_nxt[2] = {};
     uint32_t d_cur[2] = {0u, 0u}, d_nxt[2] = {0u, 0u};
     auto side = [&](int tile, int c) {
@@ -312,20 +332,26 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
         if (r0 >= M.rows) r0 = M.rows - 1;
         if (r1 >= M.rows) r1 = M.rows - 1;
         const int64_t cg = kc0 + c, nc = P.nchunks;
-        s_nxt[0] = __ldg(reinterpret_cast<const uint4*>(M.p.s + (r0 * nc + cg) * 16));
-        s_nxt[1] = __ldg(reinterpret_cast<const uint4*>(M.p.s + (r1 * nc + cg) * 16));
-        d_nxt[0] = __ldg(reinterpret_cast<const unsigned short*>(M.p.d + (r0 * nc + cg) * 2));
-        d_nxt[1] = __ldg(reinterpret_cast<const unsigned short*>(M.p.d + (r1 * nc + cg) * 2));
+        if constexpr (D == kQ6_K) {
+            s_nxt[0] = __ldg(reinterpret_cast<const uint4*>(M.p.s + (r0 * nc + cg) * 16));
+            s_nxt[1] = __ldg(reinterpret_cast<const uint4*>(M.p.s + (r1 * nc + cg) * 16));
+            d_nxt[0] = __ldg(reinterpret_cast<const unsigned short*>(M.p.d + (r0 * nc + cg) * 2));
+            d_nxt[1] = __ldg(reinterpret_cast<const unsigned short*>(M.p.d + (r1 * nc + cg) * 2));
+        } else {
+            // block b of row r at (r * 8 nc + b) * 2 bytes: the chunk's eight are 16 aligned bytes
+            s_nxt[0] = __ldg(reinterpret_cast<const uint4*>(M.p.d + (r0 * nc + cg) * 16));
+            s_nxt[1] = __ldg(reinterpret_cast<const uint4*>(M.p.d + (r1 * nc + cg) * 16));
+        }
     };
 
     int tl = u0 / (nch > 0 ? nch : 1), c = u0 - tl * nch, slot = 0;
     const int tl_first = tl;  // the first tile of this warp's run
     uint32_t phase = 0;
-    if constexpr (D == kQ6_K) {
+    if constexpr (D != kQ4_K) {
         if (u0 < u1) side(t_begin + tl, c);
     }
     for (int u = u0; u < u1; u++) {
-        if constexpr (D == kQ6_K) {
+        if constexpr (D != kQ4_K) {
             s_cur[0] = s_nxt[0]; s_cur[1] = s_nxt[1];
             d_cur[0] = d_nxt[0]; d_cur[1] = d_nxt[1];
             if (u + 1 < u1) {
@@ -356,6 +382,33 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
             __syncwarp();
             if (issued < u1) issue();  // the slot's words are in registers: refill it
             q4k_i8_chunk_n<NP>(L8, HD, CW, xs, accm, accn);
+        } else if constexpr (D == kQ8_0) {
+            // row g + 8h, this lane's 64 bytes: half t / 2 of the chunk,
+            // chunks 4 (t & 1) .. + 3 of its 128-byte line 2 (g + 8h) + t / 2
+            uint4 QV[2][4];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int l = 2 * (g + 8 * h) + (t >> 1);
+#pragma unroll
+                for (int i = 0; i < 4; i++) QV[h][i] = *reinterpret_cast<const uint4*>(st + swz_off(l, 4 * (t & 1) + i));
+            }
+            __syncwarp();
+            if (issued < u1) issue();
+            q8_0_i8_chunk_n<NP>(L8, QV, s_cur, xs, accm);
+        } else if constexpr (D == kQ4_0) {
+            // row g + 8h, this lane's 32 bytes: chunks 2t, 2t + 1 of line g + 8h
+            uint32_t QW[2][8];
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+#pragma unroll
+                for (int i = 0; i < 2; i++) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(st + swz_off(g + 8 * h, 2 * t + i));
+                    QW[h][4 * i] = v.x; QW[h][4 * i + 1] = v.y; QW[h][4 * i + 2] = v.z; QW[h][4 * i + 3] = v.w;
+                }
+            }
+            __syncwarp();
+            if (issued < u1) issue();
+            q4_0_i8_chunk_n<NP>(L8, QW, s_cur, xs, accm, accn);
         } else {
             uint32_t QW[2][12];
 #pragma unroll
@@ -487,46 +540,51 @@ __global__ void __launch_bounds__(kWThreads, 1) gemv_warp_kernel(const __grid_co
     }
 }
 
-// Encoded maps, per thread, by (base, rows, row bytes, box): a map is a pure
-// function of these, so an entry never goes stale.  Decode calls one weight at
-// a time, so the per-call encode is the common case to avoid.
+// Encoded maps, per thread, by (base, rows, row bytes, box, dtype): a map is a
+// pure function of these, so an entry never goes stale.  Decode calls one
+// weight at a time, so the per-call encode is the common case to avoid.
 struct MapKey {
     const void* base;
     int64_t rows, row_bytes;
-    int box;
+    int box, dtype;
     bool operator==(const MapKey& o) const {
-        return base == o.base && rows == o.rows && row_bytes == o.row_bytes && box == o.box;
+        return base == o.base && rows == o.rows && row_bytes == o.row_bytes && box == o.box && dtype == o.dtype;
     }
 };
 struct MapKeyHash {
     size_t operator()(const MapKey& k) const {
         return std::hash<const void*>()(k.base) ^ (std::hash<int64_t>()(k.rows) * 31) ^
-               (std::hash<int64_t>()(k.row_bytes) * 131) ^ (size_t)k.box;
+               (std::hash<int64_t>()(k.row_bytes) * 131) ^ (size_t)k.box ^ ((size_t)k.dtype << 20);
     }
 };
-bool cached_encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t row_bytes, int box) {
+bool encode_unit_map(CUtensorMap* map, int dtype, const void* base, int64_t rows, int64_t row_bytes, int box);
+bool cached_encode_rows(CUtensorMap* map, int dtype, const void* base, int64_t rows, int64_t row_bytes, int box) {
     thread_local std::unordered_map<MapKey, CUtensorMap, MapKeyHash> cache;
-    const MapKey key{base, rows, row_bytes, box};
+    const MapKey key{base, rows, row_bytes, box, dtype};
     auto it = cache.find(key);
     if (it != cache.end()) {
         *map = it->second;
         return true;
     }
-    if (!encode_rows(map, base, rows, row_bytes, box, 16)) return false;
+    if (!encode_unit_map(map, dtype, base, rows, row_bytes, box)) return false;
     if (cache.size() >= 4096) cache.clear();
     cache.emplace(key, *map);
     return true;
 }
 
-bool warp_enabled() {
+// Tuning knob CLQ_GEMV_WARP: 0 sends decode to the shared-ring bulk kernel
+// (Q4_K / Q6_K) and the register-fed one; k keeps the per-warp kernel for the
+// K formats only (Q4_0 / Q8_0 on the register-fed kernel).  1: all four.
+int warp_mode() {
     static int on = -1;
     if (on < 0) {
-        const char* e = getenv("CLQ_GEMV_WARP");  // tuning knob: 0 sends decode to the shared-ring bulk kernel
+        const char* e = getenv("CLQ_GEMV_WARP");
         const char* i = getenv("CLQ_GEMV_I8");
-        on = ((e && e[0] == '0') || (i && i[0] == '0')) ? 0 : 1;
+        on = ((e && e[0] == '0') || (i && i[0] == '0')) ? 0 : (e && e[0] == 'k') ? 2 : 1;
     }
-    return on == 1;
+    return on;
 }
+bool warp_enabled() { return warp_mode() != 0; }
 
 size_t al128(size_t v) { return (v + 127) & ~(size_t)127; }
 
@@ -567,7 +625,7 @@ bool wplan(WarpParams& P, int64_t groups, int ks, size_t* smem) {
     P.tsum_off = (uint32_t)al128(P.piece_off + (size_t)2 * kWW * P.m * 16 * 4);
     P.ring_off = (uint32_t)al128(P.tsum_off + (ks > 1 ? (size_t)tiles_cta * P.m * 16 * 4 : 0));
     for (int depth = kWMaxDepth; depth >= (ks > 1 ? 2 : 3); depth--) {
-        const size_t total = P.ring_off + (size_t)kWW * depth * 16 * WGeo<D>::q;
+        const size_t total = P.ring_off + (WGeo<D>::swz ? 1024 : 0) + (size_t)kWW * depth * 16 * WGeo<D>::q;
         if (total <= kWSmemLimit) {
             P.depth = depth;
             *smem = total;
@@ -743,10 +801,15 @@ cudaError_t launch_warp(WarpParams P, cudaStream_t stream) {
 }
 
 // One instance per pair count of activation rows; the fused prologue at one
-// pair only.
+// pair only, for Q4_K and Q6_K (fused Q4_0 / Q8_0 calls take the unfused
+// product behind the fusion kernels).
 template <int D, typename XT>
 cudaError_t launch_warp_rows(const WarpParams& P, bool fuse, cudaStream_t s) {
-    if (fuse) return launch_warp<D, XT, true, 1>(P, s);
+    if constexpr (D == kQ4_K || D == kQ6_K) {
+        if (fuse) return launch_warp<D, XT, true, 1>(P, s);
+    } else {
+        if (fuse) return cudaErrorNotSupported;
+    }
     switch ((P.m + 1) / 2) {
     case 1: return launch_warp<D, XT, false, 1>(P, s);
     case 2: return launch_warp<D, XT, false, 2>(P, s);
@@ -761,6 +824,8 @@ cudaError_t launch_warp_dtype(const WarpParams& P, int dtype, bool fuse, cudaStr
     switch (dtype) {
     case kQ4_K: return launch_warp_rows<kQ4_K, XT>(P, fuse, s);
     case kQ6_K: return launch_warp_rows<kQ6_K, XT>(P, fuse, s);
+    case kQ4_0: return launch_warp_rows<kQ4_0, XT>(P, fuse, s);
+    case kQ8_0: return launch_warp_rows<kQ8_0, XT>(P, fuse, s);
     default: return cudaErrorNotSupported;
     }
 }
@@ -793,6 +858,35 @@ bool encode_rows(CUtensorMap* map, const void* base, int64_t rows, int64_t row_b
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+namespace {
+// The per-warp kernel's map over a weight's q plane (ROWS rows of ROW_BYTES),
+// one box per unit of 16 rows x BOX bytes: Q4_K / Q6_K plain; Q4_0 (128-byte
+// units) under the 128-byte swizzle; Q8_0 (256-byte units) as a 3-D map of
+// 128-byte halves, {128, 2, 16} per box, so that a unit row's two halves are
+// consecutive swizzled lines.
+bool encode_unit_map(CUtensorMap* map, int dtype, const void* base, int64_t rows, int64_t row_bytes, int box) {
+    if (dtype == kQ4_K || dtype == kQ6_K) return encode_rows(map, base, rows, row_bytes, box, 16);
+    PFN_cuTensorMapEncodeTiled_v12000 fn = encode_tiled();
+    if (!fn || (uintptr_t)base % 16 || row_bytes % 256) return false;
+    const cuuint64_t dims2[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    const cuuint64_t strides2[1] = {(cuuint64_t)row_bytes};
+    const cuuint32_t box2[2] = {128u, 16u};
+    const cuuint64_t dims3[3] = {128u, (cuuint64_t)(row_bytes / 128), (cuuint64_t)rows};
+    const cuuint64_t strides3[2] = {128u, (cuuint64_t)row_bytes};
+    const cuuint32_t box3[3] = {128u, 2u, 16u};
+    const cuuint32_t estr[3] = {1u, 1u, 1u};
+    if (dtype == kQ4_0 && box == 128)
+        return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims2, strides2, box2, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    if (dtype == kQ8_0 && box == 256)
+        return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims3, strides3, box3, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return false;
+}
+}  // namespace
+
 cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, int count, const void* x, int xtype,
                              int64_t m, float* const* out, const int64_t* ldo, const TpLink* tp,
                              cudaStream_t stream, const Fusion* fuse) {
@@ -800,7 +894,17 @@ cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, in
     const bool fused = fuse && fuse->any();
     if (fused && (m > 2 || tp || (fuse->res && count != 1))) return cudaErrorNotSupported;
     const int dtype = w[0]->dtype;
-    if ((dtype != kQ4_K && dtype != kQ6_K) || w[0]->k < 256) return cudaErrorNotSupported;
+    const bool kfmt = dtype == kQ4_K || dtype == kQ6_K;
+    // Q4_0 / Q8_0: plain products, at eight rows or rows of at least 4096
+    // (tensor-parallel ones take the other kernels).  Measured per launch, the
+    // register-fed kernel is faster on 512-8192 x 2048 weights at one to four
+    // rows (Q4_0 2048 x 2048, one row: 2.8 against 4.0 us); from K = 4096, or
+    // at eight rows, this kernel is (Q4_0 2048 x 8192, one row: 6.5 against
+    // 8.8 us; Q8_0 4096 x 14336, eight rows: 25.6 against 65.3 us).
+    const bool small_k = !kfmt && m < 8 && w[0]->k < 4096;
+    if (!(kfmt || ((dtype == kQ4_0 || dtype == kQ8_0) && !tp && !fused && warp_mode() == 1 && !small_k)) ||
+        w[0]->k < 256)
+        return cudaErrorNotSupported;
     int* err = device_status_word();
     if (!err) return cudaErrorNotSupported;
     WarpParams P = {};
@@ -823,9 +927,12 @@ cudaError_t launch_gemv_warp(const WeightView* const* w, const int64_t* rows, in
     P.m = (int)m;
     P.x = x;
     P.err = err;
-    const int qb = dtype == kQ4_K ? WGeo<kQ4_K>::q : WGeo<kQ6_K>::q;
+    const int qb = dtype == kQ4_K ? WGeo<kQ4_K>::q
+                 : dtype == kQ6_K ? WGeo<kQ6_K>::q
+                 : dtype == kQ4_0 ? WGeo<kQ4_0>::q
+                                  : WGeo<kQ8_0>::q;
     for (int i = 0; i < count; i++)
-        if (!cached_encode_rows(&P.maps[i], w[i]->q, rows[i], (int64_t)P.nchunks * qb, qb))
+        if (!cached_encode_rows(&P.maps[i], dtype, w[i]->q, rows[i], (int64_t)P.nchunks * qb, qb))
             return cudaErrorNotSupported;
     if (tp) {
         P.tp_on = 1;

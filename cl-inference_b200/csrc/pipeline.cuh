@@ -1,6 +1,6 @@
 // pipeline.cuh -- shared-memory pipelines fed by the bulk-copy (TMA) engine:
 // mbarrier set-up, arrival, bounded waits, 1-D cp.async.bulk copies and 2-D
-// tensor-map box copies from global to shared memory.  Every copy has one
+// and 3-D tensor-map box copies from global to shared memory.  Every copy has one
 // destination, this CTA's shared memory, and reads this GPU's own memory.
 //
 // Every wait is bounded.  When a wait gives up it sets the sticky error word
@@ -95,6 +95,15 @@ __device__ __forceinline__ void tensor_copy_2d_hint(void* dst, const void* map, 
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
         "%3}], [%4], %5;" ::"r"(smem_u32(dst)),
         "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+// The same for a 3-D map (coordinates innermost first).
+__device__ __forceinline__ void tensor_copy_3d_hint(void* dst, const void* map, int x, int y, int z, uint64_t* bar,
+                                                    uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+        "%3, %4}], [%5], %6;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar)), "l"(policy)
         : "memory");
 }
 // Programmatic dependent launch: wait until the grids this one depends on

@@ -1,4 +1,5 @@
-"""Decode products of one to eight activation rows on Q4_K and Q6_K (needs a B200).
+"""Decode products of one to eight activation rows on Q4_K, Q6_K, Q4_0 and Q8_0
+(needs a B200).
 
 These shapes run the per-warp streaming GEMV: every warp copies its own
 (16-row, 256-column) units with a tensor-map box and the tile partials meet
@@ -43,6 +44,27 @@ def test_decode_rows_against_oracle(cuda, clq, synth, oracle, dtype, m, n, k):
     again = store.linear(torch.from_numpy(x).cuda()).cpu().numpy()
     assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
     store.close()
+
+
+@pytest.mark.parametrize("dtype", ["q4_0", "q8_0"])
+@pytest.mark.parametrize("m", [1, 3, 8])
+@pytest.mark.parametrize("n,k", [(300, 2048), (1000, 4096), (77, 14336)])
+def test_q4_0_q8_0_decode_rows_against_oracle(cuda, clq, synth, oracle, dtype, m, n, k):
+    """Q4_0 / Q8_0 rows of at least 4096, or eight activation rows, stream
+    through the per-warp kernel (swizzled 16-row units, one s8 or u8 MMA per
+    32-element block); shorter rows at one to four tokens take the
+    register-fed kernel.  Both meet the reference's bound, bit-stable."""
+    torch = cuda
+    data = synth.packed_blocks(dtype, n, k, seed=3 * n + k + m)
+    for xtype in ("float32", "bfloat16"):
+        x = torch.from_numpy(synth.activations(m, k, seed=5 * m + k)).cuda().to(getattr(torch, xtype))
+        store = clq.Store(dtype, n, k, data)
+        got = store.linear(x).cpu().numpy()
+        ref, mag = oracle.matmul_f64(dtype, x.float().cpu().numpy(), data, n)
+        check(got, ref, mag)
+        again = store.linear(x).cpu().numpy()
+        assert np.array_equal(got.view(np.uint32), again.view(np.uint32))
+        store.close()
 
 
 @pytest.mark.parametrize("dtype", DTYPES)
